@@ -1,0 +1,178 @@
+/*
+ * sdvk_cuda.h -- C ABI of the sdvk-b200 CUDA back end (libsdvk_b200.so).
+ *
+ * It replaces sdvk's Vulkan GPU module (src/Modules/GPU/: vk_engine, fused_attn, volk) for the
+ * UNet transformer-block hot path: the Q8_0 dequant GEMMs and the fused attention.  Everything is
+ * extern "C", takes plain pointers and sizes, never throws, and returns an int status
+ * (SDVK_OK = 0).  Device pointers are CUDA device addresses obtained from sdvk_alloc() (or any
+ * cudaMalloc'd memory on the context's device); host pointers are ordinary memory (pinned memory
+ * from sdvk_host_alloc() makes the *_async copies truly asynchronous).
+ *
+ * Threading: one context per device per process; calls on a context are not thread-safe, matching
+ * the reference's single-queue Engine (src/Modules/GPU/vk_engine.hpp:90-247).  Work is queued on
+ * the context's stream in call order; stream order replaces the reference's hazard barriers
+ * (vk_engine.cpp:1046-1126).
+ *
+ * Every entry point's comment names the reference interface it replaces (paths relative to the
+ * sdvk project root).
+ */
+#ifndef SDVK_CUDA_H
+#define SDVK_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SDVK_API __attribute__((visibility("default")))
+#else
+#define SDVK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------- */
+#define SDVK_OK 0
+#define SDVK_E_OOM 1         /* device/host allocation failed (reference: OomError, vk_engine.hpp:30-32) */
+#define SDVK_E_SHAPE 2       /* unsupported shape, stride or alignment */
+#define SDVK_E_CUDA 3        /* a CUDA runtime/driver call failed (reference: VK_CHECK throw, vk_engine.cpp:33-41) */
+#define SDVK_E_TIMEOUT 4     /* a kernel's bounded wait or sdvk_step_wait's deadline ran out */
+#define SDVK_E_ARG 5         /* invalid argument (null pointer, bad dtype, bad push size) */
+#define SDVK_E_KERNEL 6      /* sdvk_dispatch: unknown kernel name (reference exits, vk_engine.cpp:1147-1150) */
+#define SDVK_E_STATE 7       /* step protocol misuse (e.g. step_end without step_begin) */
+#define SDVK_E_NOT_FINITE 8  /* sdvk_check_finite found a NaN/Inf */
+
+/* ---- element types ------------------------------------------------------------------------ */
+#define SDVK_F32 0
+#define SDVK_F16 1
+#define SDVK_BF16 2
+
+typedef struct sdvk_ctx sdvk_ctx;
+
+/* A non-owning view of device memory: base + offset, size bytes.
+ * Replaces BufRef{VkBuffer, offset, size} (src/Modules/GPU/vk_engine.hpp:21-25). */
+typedef struct sdvk_buf {
+    void* ptr;
+    uint64_t offset;
+    uint64_t size;
+} sdvk_buf;
+
+/* ---- context ------------------------------------------------------------------------------ */
+/* Engine::init + setDeviceIndex (vk_engine.hpp:97-100, vk_engine.cpp:317-436). */
+SDVK_API int sdvk_ctx_create(int device, sdvk_ctx** out);
+/* Engine::destroy (vk_engine.hpp:101). */
+SDVK_API int sdvk_ctx_destroy(sdvk_ctx* ctx);
+/* Run subsequent work on a caller-owned cudaStream_t (NULL restores the context's own stream). */
+SDVK_API int sdvk_ctx_set_stream(sdvk_ctx* ctx, void* cuda_stream);
+SDVK_API void* sdvk_ctx_stream(sdvk_ctx* ctx);
+/* Deadline for every bounded wait inside the kernels (default 2000 ms). */
+SDVK_API int sdvk_ctx_set_timeout_ms(sdvk_ctx* ctx, uint32_t ms);
+/* Human-readable device report (Engine::deviceReport, vk_engine.hpp:169). */
+SDVK_API int sdvk_device_report(sdvk_ctx* ctx, char* buf, size_t len);
+/* Text of the last error on this context (empty when none). */
+SDVK_API const char* sdvk_last_error(sdvk_ctx* ctx);
+SDVK_API const char* sdvk_status_string(int status);
+
+/* ---- memory ------------------------------------------------------------------------------- */
+/* Arena::alloc (vk_engine.hpp:38, vk_engine.cpp:251-261): 256-byte aligned device memory. */
+SDVK_API int sdvk_alloc(sdvk_ctx* ctx, uint64_t bytes, void** dptr);
+SDVK_API int sdvk_free(sdvk_ctx* ctx, void* dptr);
+/* Pinned host memory for the asynchronous copies (the reference's staging ring, vk_engine.hpp:150-153). */
+SDVK_API int sdvk_host_alloc(sdvk_ctx* ctx, uint64_t bytes, void** hptr);
+SDVK_API int sdvk_host_free(sdvk_ctx* ctx, void* hptr);
+/* Engine::uploadNow / downloadNow (vk_engine.hpp:135, 146): synchronous copies. */
+SDVK_API int sdvk_upload(sdvk_ctx* ctx, void* dst_dev, const void* src_host, uint64_t bytes);
+SDVK_API int sdvk_download(sdvk_ctx* ctx, void* dst_host, const void* src_dev, uint64_t bytes);
+/* Stream-ordered copies (the staged in-step uploads/readbacks, vk_engine.hpp:136-153). */
+SDVK_API int sdvk_upload_async(sdvk_ctx* ctx, void* dst_dev, const void* src_host, uint64_t bytes);
+SDVK_API int sdvk_download_async(sdvk_ctx* ctx, void* dst_host, const void* src_dev, uint64_t bytes);
+/* Engine::fill (vk_engine.hpp:114): fill with a 32-bit pattern, bytes % 4 == 0. */
+SDVK_API int sdvk_fill_u32(sdvk_ctx* ctx, void* dst_dev, uint32_t value, uint64_t bytes);
+
+/* ---- step protocol ------------------------------------------------------------------------ */
+/* Engine::beginStep / endStep / waitStep (vk_engine.hpp:109-117, vk_engine.cpp:930-950,
+ * 1245-1295).  begin opens a step (kernels may be queued before it too), end records the step's
+ * completion, wait blocks until it completes or timeout_ms passes (SDVK_E_TIMEOUT). */
+SDVK_API int sdvk_step_begin(sdvk_ctx* ctx);
+SDVK_API int sdvk_step_end(sdvk_ctx* ctx);
+SDVK_API int sdvk_step_wait(sdvk_ctx* ctx, uint32_t timeout_ms);
+/* Block until all queued work is done and report any device-side error (timeouts). */
+SDVK_API int sdvk_synchronize(sdvk_ctx* ctx);
+
+/* ---- the reference's dispatch interface --------------------------------------------------- */
+/* Engine::dispatch(kernel, bufs, push, gx, gy, gz) (vk_engine.hpp:111-112, vk_engine.cpp:1143-1180)
+ * for the hot-path kernels, with the reference's binding order and push-constant layouts
+ * (kernel table vk_engine.cpp:51-125).  All buffers hold fp32 data, as in the reference.
+ *   "gemm_nt_q8", "gemm_nt_q8_v", "gemm_nt_q8_v_bm128", "gemm_nt_q8_v_bk32",
+ *   "gemm_nt_q8_v_bm128_bk32"           bufs {A, Bq, C, S}        push Pg (48 B)
+ *   "gemm_nt_q8_v_b", "gemm_nt_q8_v_bm128_b"  bufs {A, Bq, C, S, bias}  push Pg
+ *   "gemm_nn_q8", "gemm_nn_q8_v"        bufs {Aq, B, C, S}        push Pg
+ *   "fused_attn", "fused_attn_tiled"    bufs {Q, K, V, O}         push FaPush (36 B)
+ * Pg = {M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, pad} (sdvkgen.cpp:901-903);
+ * FaPush = {Tq, Tk, C, heads, hd, causal, pad0, pad1, scale} (fused_attn.cpp:15-26).
+ * The grid (gx, gy, gz) the caller computed for the Vulkan tiling is accepted and ignored: each
+ * kernel covers the whole shape in the push constants with its own B200 tiling.
+ * Deviations: Q8 kernels require K % 32 == 0 (whole Q8_0 blocks); attention requires hd <= 64.
+ * Numerics: the GEMM runs the tensor cores in tf32 on fp32 activations, attention computes in
+ * f16 operands with fp32 accumulation. */
+SDVK_API int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint32_t nbufs, const void* push,
+                  uint32_t push_bytes, uint32_t gx, uint32_t gy, uint32_t gz);
+
+/* fusedAttention(Engine&, FusedAttnArgs) (src/Modules/GPU/fused_attn.hpp:13-28,
+ * fused_attn.cpp:40-61): fp32 Q/K/V/out, rows of C = heads*hd, scale 1/sqrt(hd).
+ * Returns SDVK_E_SHAPE where the reference's fusedAttnSupported (fused_attn.cpp:34-38) is false. */
+SDVK_API int sdvk_fused_attention(sdvk_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t Tq,
+                         uint32_t Tk, uint32_t C, uint32_t heads, int causal);
+/* fusedAttnSupported (fused_attn.cpp:34-38): 1 if hd = C/heads is in 1..64. */
+SDVK_API int sdvk_fused_attn_supported(uint32_t C, uint32_t heads);
+
+/* ---- typed hot-path entry points ---------------------------------------------------------- */
+/* Q8_0 NT GEMM (gemm_nt_q8_v.comp:5-128 via gemmNtQ8 / gemmNtQ8Bias, sdvkgen.cpp:917-936):
+ *   C[z][m][n] (=|+=) sum_k A[z][m][k] * q[n][k] * s[(n*K + k) >> 5] (+ bias[n])
+ * A: a_dtype (F16, BF16 or F32), row stride lda, batch stride sA (elements).
+ * q: int8 [N][K] (row stride K), s: fp32 per 32 elements, shared by all batches.
+ * C: c_dtype (F32 or F16), row stride ldc, batch stride sC.  accumulate != 0 adds into C
+ * (F32 only) and, unlike the reference's mode 1, also adds the bias when one is given.
+ * Requirements: K % 32 == 0; 16-byte aligned base pointers; lda, ldc (in bytes) multiples of 16. */
+SDVK_API int sdvk_gemm_q8_nt(sdvk_ctx* ctx, const void* A, int a_dtype, const int8_t* q, const float* s, const float* bias,
+                    void* C, int c_dtype, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldc,
+                    uint32_t batch, uint64_t sA, uint64_t sC, int accumulate);
+
+/* Q8_0 NN GEMM (gemm_nn_q8_v.comp:5-110 via gemmNnQ8, sdvkgen.cpp:944-948; used by conv1 for
+ * proj_in/proj_out, sdvkgen.cpp:1180-1189):
+ *   C[z][m][n] (=|+=) sum_k q[z][m][k] * s[(z*sA + m*lda + k) >> 5] * B[z][k][n] (+ bias[m])
+ * q: int8 [M][lda] weight (lda % 32 == 0, batch stride sA, 0 = shared), B: b_dtype [K][ldb]. */
+SDVK_API int sdvk_gemm_q8_nn(sdvk_ctx* ctx, const int8_t* q, const float* s, const void* B, int b_dtype, const float* bias,
+                    void* C, int c_dtype, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                    uint32_t ldc, uint32_t batch, uint64_t sA, uint64_t sB, uint64_t sC, int accumulate);
+
+/* Fused attention with explicit layout (generalises FusedAttnArgs, fused_attn.hpp:13-23, with a
+ * batch dimension, strides and a caller-chosen scale; attnCore's fused branch, sdvkgen.cpp:1226-1238).
+ * Element (b, h, t, d) of Q is at q[b*sq + h*hq + t*ldq + d] (same for K, V, O).  dtype applies to
+ * Q/K/V (F16, BF16 or F32); o_dtype to O (F32 or F16).  hd <= 64. */
+typedef struct sdvk_attn_desc {
+    const void* q;
+    const void* k;
+    const void* v;
+    void* o;
+    int dtype;
+    int o_dtype;
+    uint32_t batch, heads, Tq, Tk, hd;
+    uint64_t ldq, ldk, ldv, ldo;
+    uint64_t sq, sk, sv, so;
+    uint64_t hq, hk, hv, ho;
+    float scale;
+    int causal;
+} sdvk_attn_desc;
+SDVK_API int sdvk_attention(sdvk_ctx* ctx, const sdvk_attn_desc* desc);
+
+/* NaN/Inf check of n fp32 or f16 values (the reference aborts on a non-finite UNet output,
+ * sdvkgen.cpp:3819-3823): returns SDVK_E_NOT_FINITE if any value is not finite. */
+SDVK_API int sdvk_check_finite(sdvk_ctx* ctx, const void* x, int dtype, uint64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SDVK_CUDA_H */

@@ -1,0 +1,302 @@
+"""TEST INFRASTRUCTURE ONLY: numpy/ctypes front end of liboracle.so (see oracle.h).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may import this module, as the
+checker or the timed CPU baseline.  The product (sdvk_b200) never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+REF_DIR = os.path.join(HERE, "_ref")
+REF_GGUF = os.path.join(REF_DIR, "libref_gguf.so")
+
+_lib = None
+_P, _U32, _U64, _I, _F = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_float
+
+_SIG = {
+    "orc_mt19937_new": (_P, [_U32]),
+    "orc_mt19937_free": (None, [_P]),
+    "orc_mt19937_uniform_f32": (None, [_P, _F, _F, _P, _U64]),
+    "orc_mt19937_uniform_int": (None, [_P, ctypes.c_int32, ctypes.c_int32, _P, _U64]),
+    "orc_normal_f32": (None, [_U64, _U64, _F, _P, _U64]),
+    "orc_normal_f16": (None, [_U64, _U64, _F, _P, _U64]),
+    "orc_q8_weights": (None, [_U64, _U64, _U64, _U64, _P, _P, _P]),
+    "orc_f32_to_f16": (None, [_P, _P, _U64]),
+    "orc_f16_to_f32": (None, [_P, _P, _U64]),
+    "orc_q8_0_pack_blocks": (None, [_P, _P, _U64, _P]),
+    "orc_q8_0_split_blocks": (None, [_P, _U64, _P, _P]),
+    "orc_gguf_write_q8": (_I, [ctypes.c_char_p, ctypes.c_char_p, _U64, _U64, _P]),
+    "orc_gemm_nt_q8_shader": (None, [_P, _P, _P, _P, _P] + [_U32] * 9),
+    "orc_gemm_nt_q8_f64": (None, [_P, _P, _P, _P, _P] + [_U32] * 8),
+    "orc_gemm_nn_q8_shader": (None, [_P, _P, _P, _P] + [_U32] * 11),
+    "orc_gemm_nn_q8_f64": (None, [_P, _P, _P, _P] + [_U32] * 9),
+    "orc_attn_tiled_shader": (_I, [_P, _P, _P, _P] + [_U32] * 5 + [_F]),
+    "orc_attn_simple_shader": (_I, [_P, _P, _P, _P] + [_U32] * 5 + [_F]),
+    "orc_fused_attention": (_I, [_P, _P, _P, _P] + [_U32] * 5 + [_I]),
+    "orc_attn_f64": (None, [_P, _P, _P, _P] + [_U32] * 5 + [_U64] * 8 + [_U32, ctypes.c_double]),
+    "orc_layernorm_shader": (None, [_P, _P, _P, _P, _U32, _U32, _F, _U32]),
+    "orc_layernorm_f64": (None, [_P, _P, _P, _P, _U32, _U32, ctypes.c_double]),
+    "orc_gelu_erf_shader": (None, [_P, _P, _U64]),
+    "orc_num_threads": (_I, []),
+    "orc_set_num_threads": (None, [_I]),
+}
+
+
+def build() -> None:
+    """Build liboracle.so (and, when the reference sources are present, the _ref/ checkers)."""
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    if os.path.isdir("/root/reference"):
+        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB):
+            build()
+        L = ctypes.CDLL(LIB)
+        for k, (r, a) in _SIG.items():
+            f = getattr(L, k)
+            f.restype = r
+            f.argtypes = a
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+# ------------------------------------------------------------------------------ RNG
+class MT19937:
+    """std::mt19937 with libstdc++'s uniform distributions (the reference tests' RNG)."""
+
+    def __init__(self, seed: int):
+        self.h = lib().orc_mt19937_new(seed)
+
+    def uniform_f32(self, n: int, lo=-1.0, hi=1.0) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        lib().orc_mt19937_uniform_f32(self.h, lo, hi, _p(out), n)
+        return out
+
+    def uniform_int(self, n: int, lo: int, hi: int) -> np.ndarray:
+        out = np.empty(n, np.int32)
+        lib().orc_mt19937_uniform_int(self.h, lo, hi, _p(out), n)
+        return out
+
+    def __del__(self):
+        try:
+            lib().orc_mt19937_free(self.h)
+        except Exception:
+            pass
+
+
+def normal_f32(seed: int, stream: int, shape, std: float = 1.0) -> np.ndarray:
+    out = np.empty(int(np.prod(shape)), np.float32)
+    lib().orc_normal_f32(seed, stream, std, _p(out), out.size)
+    return out.reshape(shape)
+
+
+def normal_f16(seed: int, stream: int, shape, std: float = 1.0) -> np.ndarray:
+    out = np.empty(int(np.prod(shape)), np.uint16)
+    lib().orc_normal_f16(seed, stream, std, _p(out), out.size)
+    return out.view(np.float16).reshape(shape)
+
+
+def q8_weights(seed: int, stream: int, rows: int, cols: int):
+    """BASELINE config-0 Q8_0 weight: (int8 [rows, cols], fp16 scales, fp32 scales [rows*cols/32])."""
+    q = np.empty(rows * cols, np.int8)
+    d16 = np.empty(rows * cols // 32, np.uint16)
+    d32 = np.empty(rows * cols // 32, np.float32)
+    lib().orc_q8_weights(seed, stream, rows, cols, _p(q), _p(d16), _p(d32))
+    return q.reshape(rows, cols), d16.view(np.float16), d32
+
+
+def f32_to_f16(x: np.ndarray) -> np.ndarray:
+    x = _c(x, np.float32)
+    out = np.empty(x.size, np.uint16)
+    lib().orc_f32_to_f16(_p(x), _p(out), x.size)
+    return out.view(np.float16).reshape(x.shape)
+
+
+def f16_to_f32(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x).view(np.uint16)
+    out = np.empty(x.size, np.float32)
+    lib().orc_f16_to_f32(_p(x), _p(out), x.size)
+    return out.reshape(x.shape)
+
+
+# ------------------------------------------------------------------------------ GGUF Q8_0
+def q8_0_pack(q: np.ndarray, d16: np.ndarray) -> np.ndarray:
+    q = _c(q, np.int8).ravel()
+    d = np.ascontiguousarray(d16).view(np.uint16).ravel()
+    out = np.empty(d.size * 34, np.uint8)
+    lib().orc_q8_0_pack_blocks(_p(q), _p(d), d.size, _p(out))
+    return out
+
+
+def q8_0_split(blocks: np.ndarray):
+    blocks = _c(blocks, np.uint8)
+    nb = blocks.size // 34
+    q = np.empty(nb * 32, np.int8)
+    s = np.empty(nb, np.float32)
+    lib().orc_q8_0_split_blocks(_p(blocks), nb, _p(q), _p(s))
+    return q, s
+
+
+def gguf_write_q8(path: str, name: str, rows: int, cols: int, blocks: np.ndarray) -> None:
+    blocks = _c(blocks, np.uint8)
+    if lib().orc_gguf_write_q8(path.encode(), name.encode(), rows, cols, _p(blocks)) != 0:
+        raise OSError(f"cannot write {path}")
+
+
+# ------------------------------------------------------------------------------ GEMMs
+def gemm_nt_q8_shader(A, q, s, bias=None, C=None, mode=0, batch=1, sA=0, sC=0, lda=0, ldc=0, M=None, N=None, K=None):
+    A = _c(A, np.float32)
+    q = _c(q, np.int8)
+    s = _c(s, np.float32)
+    N = q.shape[0] if N is None else N
+    K = q.shape[1] if K is None else K
+    M = (A.shape[-2] if A.ndim >= 2 else 1) if M is None else M
+    if C is None:
+        C = np.zeros((batch, M, ldc or N) if batch > 1 else (M, ldc or N), np.float32)
+    b = _c(bias, np.float32) if bias is not None else None
+    lib().orc_gemm_nt_q8_shader(_p(A), _p(q), _p(s), _p(b) if b is not None else None, _p(C), M, N, K, mode, sA, sC,
+                                batch, lda, ldc)
+    return C
+
+
+def gemm_nt_q8_f64(A, q, s, bias=None, batch=1, sA=0, lda=0):
+    A = _c(A, np.float32)
+    q = _c(q, np.int8)
+    s = _c(s, np.float32)
+    N, K = q.shape
+    M = A.shape[-2]
+    C = np.zeros((batch, M, N) if batch > 1 else (M, N), np.float64)
+    b = _c(bias, np.float32) if bias is not None else None
+    lib().orc_gemm_nt_q8_f64(_p(A), _p(q), _p(s), _p(b) if b is not None else None, _p(C), M, N, K, sA or M * K,
+                             M * N, batch, lda, 0)
+    return C
+
+
+def gemm_nn_q8_shader(q, s, B, mode=0, batch=1, sA=0, sB=0, sC=0, lda=0, ldb=0, ldc=0, C=None):
+    q = _c(q, np.int8)
+    s = _c(s, np.float32)
+    B = _c(B, np.float32)
+    M, K = q.shape[-2], q.shape[-1]
+    N = B.shape[-1]
+    if C is None:
+        C = np.zeros((batch, M, N) if batch > 1 else (M, N), np.float32)
+    lib().orc_gemm_nn_q8_shader(_p(q), _p(s), _p(B), _p(C), M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc)
+    return C
+
+
+def gemm_nn_q8_f64(q, s, B, batch=1):
+    q = _c(q, np.int8)
+    s = _c(s, np.float32)
+    B = _c(B, np.float32)
+    M, K = q.shape
+    N = B.shape[-1]
+    C = np.zeros((batch, M, N) if batch > 1 else (M, N), np.float64)
+    lib().orc_gemm_nn_q8_f64(_p(q), _p(s), _p(B), _p(C), M, N, K, K * N, M * N, batch, 0, 0, 0)
+    return C
+
+
+# ------------------------------------------------------------------------------ attention
+def fused_attention(Q, K, V, Tq, Tk, C, heads, causal=False, force_simple=False):
+    Q, K, V = (_c(x, np.float32) for x in (Q, K, V))
+    O = np.zeros((Tq, C), np.float32)
+    rc = lib().orc_fused_attention(_p(Q), _p(K), _p(V), _p(O), Tq, Tk, C, heads, int(causal), int(force_simple))
+    if rc:
+        raise ValueError("shape not supported by the reference operator")
+    return O
+
+
+def attn_tiled_shader(Q, K, V, Tq, Tk, C, heads, causal, scale):
+    Q, K, V = (_c(x, np.float32) for x in (Q, K, V))
+    O = np.zeros((Tq, C), np.float32)
+    if lib().orc_attn_tiled_shader(_p(Q), _p(K), _p(V), _p(O), Tq, Tk, C, heads, int(causal), scale):
+        raise ValueError("tiled kernel needs hd == 64")
+    return O
+
+
+def attn_simple_shader(Q, K, V, Tq, Tk, C, heads, causal, scale):
+    Q, K, V = (_c(x, np.float32) for x in (Q, K, V))
+    O = np.zeros((Tq, C), np.float32)
+    if lib().orc_attn_simple_shader(_p(Q), _p(K), _p(V), _p(O), Tq, Tk, C, heads, int(causal), scale):
+        raise ValueError("simple kernel restated for 32 <= hd <= 64 only")
+    return O
+
+
+def attn_f64(Q, K, V, heads, causal=False, scale=None):
+    """fp64 truth on token-major [B, T, C] (or [T, C]) arrays."""
+    squeeze = Q.ndim == 2
+    Q3, K3, V3 = (x[None] if x.ndim == 2 else x for x in (Q, K, V))
+    Q3, K3, V3 = (_c(x, np.float32) for x in (Q3, K3, V3))
+    B, Tq, C = Q3.shape
+    Tk = K3.shape[1]
+    hd = C // heads
+    if scale is None:
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
+    O = np.zeros((B, Tq, C), np.float64)
+    lib().orc_attn_f64(_p(Q3), _p(K3), _p(V3), _p(O), B, Tq, Tk, heads, hd, C, C, C, C, Tq * C, Tk * C, Tk * C,
+                       Tq * C, int(causal), scale)
+    return O[0] if squeeze else O
+
+
+# ------------------------------------------------------------------------------ block glue
+def layernorm_shader(x, gamma, beta, eps=1e-5):
+    x = _c(x, np.float32)
+    rows, d = x.reshape(-1, x.shape[-1]).shape
+    y = np.empty_like(x)
+    lib().orc_layernorm_shader(_p(x), _p(_c(gamma, np.float32)), _p(_c(beta, np.float32)), _p(y), rows, d, eps, 1)
+    return y
+
+
+def layernorm_f64(x, gamma, beta, eps=1e-5):
+    x = _c(x, np.float64)
+    rows, d = x.reshape(-1, x.shape[-1]).shape
+    y = np.empty_like(x)
+    lib().orc_layernorm_f64(_p(x), _p(_c(gamma, np.float32)), _p(_c(beta, np.float32)), _p(y), rows, d, eps)
+    return y
+
+
+def gelu_erf_shader(x):
+    x = _c(x, np.float32)
+    y = np.empty_like(x)
+    lib().orc_gelu_erf_shader(_p(x), _p(y), x.size)
+    return y
+
+
+def num_threads() -> int:
+    return lib().orc_num_threads()
+
+
+# ------------------------------------------------------------------------------ metrics
+def err_stats(got, ref) -> dict:
+    """max-abs and RMS error, relative to max|ref| and RMS(ref)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = got - ref
+    max_ref = float(np.max(np.abs(ref))) if ref.size else 0.0
+    rms_ref = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
+    max_abs = float(np.max(np.abs(d))) if d.size else 0.0
+    rms = float(np.sqrt(np.mean(d * d))) if d.size else 0.0
+    return {
+        "max_abs": max_abs,
+        "rms": rms,
+        "rel_max": max_abs / max(max_ref, 1e-30),
+        "rel_max_rms": max_abs / max(rms_ref, 1e-30),
+        "rel_rms": rms / max(rms_ref, 1e-30),
+        "finite": bool(np.all(np.isfinite(got))),
+    }

@@ -1,0 +1,238 @@
+"""sdvk-b200: B200-native CUDA back end for sdvk's UNet transformer-block hot path.
+
+The product is libsdvk_b200.so (C ABI in include/sdvk_cuda.h).  This package is a thin ctypes
+binding over it, used by the tests, bench.py and Python callers:
+
+  * ``Context``      -- one per device: memory, copies, step protocol, and the hot-path calls
+                        (``gemm_q8_nt``, ``gemm_q8_nn``, ``attention``, ``dispatch``,
+                        ``fused_attention``) on raw device pointers.
+  * ``sdvk_b200.torch_ops`` -- the same calls on torch CUDA tensors (torch's stream).
+
+There is no CPU fallback: if the library is missing or fails to load, importing the binding
+raises.  Build it with ``python -m sdvk_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import struct
+from typing import Optional, Sequence
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libsdvk_b200.so")
+
+OK, E_OOM, E_SHAPE, E_CUDA, E_TIMEOUT, E_ARG, E_KERNEL, E_STATE, E_NOT_FINITE = range(9)
+F32, F16, BF16 = 0, 1, 2
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+class SdvkError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"sdvk status {status}: {message}")
+        self.status = status
+
+
+class Buf(ctypes.Structure):
+    """sdvk_buf: non-owning device view (the reference's BufRef{buffer, offset, size})."""
+
+    _fields_ = [("ptr", ctypes.c_void_p), ("offset", ctypes.c_uint64), ("size", ctypes.c_uint64)]
+
+
+class AttnDesc(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("o", ctypes.c_void_p),
+        ("dtype", ctypes.c_int), ("o_dtype", ctypes.c_int),
+        ("batch", ctypes.c_uint32), ("heads", ctypes.c_uint32), ("Tq", ctypes.c_uint32),
+        ("Tk", ctypes.c_uint32), ("hd", ctypes.c_uint32),
+        ("ldq", ctypes.c_uint64), ("ldk", ctypes.c_uint64), ("ldv", ctypes.c_uint64), ("ldo", ctypes.c_uint64),
+        ("sq", ctypes.c_uint64), ("sk", ctypes.c_uint64), ("sv", ctypes.c_uint64), ("so", ctypes.c_uint64),
+        ("hq", ctypes.c_uint64), ("hk", ctypes.c_uint64), ("hv", ctypes.c_uint64), ("ho", ctypes.c_uint64),
+        ("scale", ctypes.c_float), ("causal", ctypes.c_int),
+    ]
+
+
+# name -> (restype, argtypes) for every symbol include/sdvk_cuda.h declares
+_P, _U32, _U64, _I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
+SIGNATURES = {
+    "sdvk_ctx_create": (_I, [_I, ctypes.POINTER(_P)]),
+    "sdvk_ctx_destroy": (_I, [_P]),
+    "sdvk_ctx_set_stream": (_I, [_P, _P]),
+    "sdvk_ctx_stream": (_P, [_P]),
+    "sdvk_ctx_set_timeout_ms": (_I, [_P, _U32]),
+    "sdvk_device_report": (_I, [_P, ctypes.c_char_p, ctypes.c_size_t]),
+    "sdvk_last_error": (ctypes.c_char_p, [_P]),
+    "sdvk_status_string": (ctypes.c_char_p, [_I]),
+    "sdvk_alloc": (_I, [_P, _U64, ctypes.POINTER(_P)]),
+    "sdvk_free": (_I, [_P, _P]),
+    "sdvk_host_alloc": (_I, [_P, _U64, ctypes.POINTER(_P)]),
+    "sdvk_host_free": (_I, [_P, _P]),
+    "sdvk_upload": (_I, [_P, _P, _P, _U64]),
+    "sdvk_download": (_I, [_P, _P, _P, _U64]),
+    "sdvk_upload_async": (_I, [_P, _P, _P, _U64]),
+    "sdvk_download_async": (_I, [_P, _P, _P, _U64]),
+    "sdvk_fill_u32": (_I, [_P, _P, _U32, _U64]),
+    "sdvk_step_begin": (_I, [_P]),
+    "sdvk_step_end": (_I, [_P]),
+    "sdvk_step_wait": (_I, [_P, _U32]),
+    "sdvk_synchronize": (_I, [_P]),
+    "sdvk_dispatch": (_I, [_P, ctypes.c_char_p, ctypes.POINTER(Buf), _U32, _P, _U32, _U32, _U32, _U32]),
+    "sdvk_fused_attention": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _I]),
+    "sdvk_fused_attn_supported": (_I, [_U32, _U32]),
+    "sdvk_gemm_q8_nt": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _U32, _U32, _U32, _U32, _U32, _U32, _U64, _U64, _I]),
+    "sdvk_gemm_q8_nn": (_I, [_P, _P, _P, _P, _I, _P, _P, _I, _U32, _U32, _U32, _U32, _U32, _U32, _U32,
+                             _U64, _U64, _U64, _I]),
+    "sdvk_attention": (_I, [_P, ctypes.POINTER(AttnDesc)]),
+    "sdvk_check_finite": (_I, [_P, _P, _I, _U64]),
+}
+
+
+def lib() -> ctypes.CDLL:
+    """Load libsdvk_b200.so (raises if it is missing: there is no fallback path)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing; build it with `python -m sdvk_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def fused_attn_supported(C: int, heads: int) -> bool:
+    """fusedAttnSupported (src/Modules/GPU/fused_attn.cpp:34-38)."""
+    return bool(lib().sdvk_fused_attn_supported(C, heads))
+
+
+class Context:
+    """One sdvk context on one CUDA device (the reference's ``Engine``)."""
+
+    def __init__(self, device: int = 0):
+        self._h = ctypes.c_void_p()
+        st = lib().sdvk_ctx_create(device, ctypes.byref(self._h))
+        if st != OK:
+            raise SdvkError(st, f"sdvk_ctx_create(device={device}) failed: {lib().sdvk_status_string(st).decode()}")
+        self.device = device
+
+    # -- plumbing --------------------------------------------------------------------------
+    @property
+    def handle(self):
+        return self._h
+
+    def _check(self, st: int, what: str) -> None:
+        if st != OK:
+            msg = lib().sdvk_last_error(self._h)
+            raise SdvkError(st, f"{what}: {(msg or b'').decode()} ({lib().sdvk_status_string(st).decode()})")
+
+    def close(self) -> None:
+        if self._h:
+            lib().sdvk_ctx_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_ptr: Optional[int]) -> None:
+        self._check(lib().sdvk_ctx_set_stream(self._h, stream_ptr or None), "set_stream")
+
+    def set_timeout_ms(self, ms: int) -> None:
+        self._check(lib().sdvk_ctx_set_timeout_ms(self._h, ms), "set_timeout_ms")
+
+    def device_report(self) -> str:
+        buf = ctypes.create_string_buffer(1024)
+        self._check(lib().sdvk_device_report(self._h, buf, len(buf)), "device_report")
+        return buf.value.decode()
+
+    # -- memory ----------------------------------------------------------------------------
+    def alloc(self, nbytes: int) -> int:
+        p = ctypes.c_void_p()
+        self._check(lib().sdvk_alloc(self._h, nbytes, ctypes.byref(p)), "alloc")
+        return p.value
+
+    def free(self, ptr: int) -> None:
+        self._check(lib().sdvk_free(self._h, ptr), "free")
+
+    def host_alloc(self, nbytes: int) -> int:
+        p = ctypes.c_void_p()
+        self._check(lib().sdvk_host_alloc(self._h, nbytes, ctypes.byref(p)), "host_alloc")
+        return p.value
+
+    def host_free(self, ptr: int) -> None:
+        self._check(lib().sdvk_host_free(self._h, ptr), "host_free")
+
+    def upload(self, dst: int, src_host: int, nbytes: int) -> None:
+        self._check(lib().sdvk_upload(self._h, dst, src_host, nbytes), "upload")
+
+    def download(self, dst_host: int, src: int, nbytes: int) -> None:
+        self._check(lib().sdvk_download(self._h, dst_host, src, nbytes), "download")
+
+    def upload_async(self, dst: int, src_host: int, nbytes: int) -> None:
+        self._check(lib().sdvk_upload_async(self._h, dst, src_host, nbytes), "upload_async")
+
+    def download_async(self, dst_host: int, src: int, nbytes: int) -> None:
+        self._check(lib().sdvk_download_async(self._h, dst_host, src, nbytes), "download_async")
+
+    def synchronize(self) -> None:
+        self._check(lib().sdvk_synchronize(self._h), "synchronize")
+
+    # -- step protocol (beginStep / endStep / waitStep) --------------------------------------
+    def step_begin(self) -> None:
+        self._check(lib().sdvk_step_begin(self._h), "step_begin")
+
+    def step_end(self) -> None:
+        self._check(lib().sdvk_step_end(self._h), "step_end")
+
+    def step_wait(self, timeout_ms: int = 0) -> None:
+        self._check(lib().sdvk_step_wait(self._h, timeout_ms), "step_wait")
+
+    # -- hot path ----------------------------------------------------------------------------
+    def gemm_q8_nt(self, A: int, a_dtype: int, q: int, s: int, bias: Optional[int], C: int, c_dtype: int,
+                   M: int, N: int, K: int, lda: int = 0, ldc: int = 0, batch: int = 1, sA: int = 0, sC: int = 0,
+                   accumulate: bool = False) -> None:
+        self._check(lib().sdvk_gemm_q8_nt(self._h, A, a_dtype, q, s, bias or None, C, c_dtype, M, N, K, lda, ldc,
+                                          batch, sA, sC, int(accumulate)), "gemm_q8_nt")
+
+    def gemm_q8_nn(self, q: int, s: int, B: int, b_dtype: int, bias: Optional[int], C: int, c_dtype: int,
+                   M: int, N: int, K: int, lda: int = 0, ldb: int = 0, ldc: int = 0, batch: int = 1, sA: int = 0,
+                   sB: int = 0, sC: int = 0, accumulate: bool = False) -> None:
+        self._check(lib().sdvk_gemm_q8_nn(self._h, q, s, B, b_dtype, bias or None, C, c_dtype, M, N, K, lda, ldb,
+                                          ldc, batch, sA, sB, sC, int(accumulate)), "gemm_q8_nn")
+
+    def attention(self, desc: AttnDesc) -> None:
+        self._check(lib().sdvk_attention(self._h, ctypes.byref(desc)), "attention")
+
+    def fused_attention(self, q: int, k: int, v: int, out: int, Tq: int, Tk: int, C: int, heads: int,
+                        causal: bool = False) -> None:
+        """fusedAttention(Engine&, FusedAttnArgs) (src/Modules/GPU/fused_attn.cpp:40-61), fp32 buffers."""
+        self._check(lib().sdvk_fused_attention(self._h, q, k, v, out, Tq, Tk, C, heads, int(causal)),
+                    "fused_attention")
+
+    def dispatch(self, kernel: str, bufs: Sequence[Buf], push: bytes, gx: int, gy: int = 1, gz: int = 1) -> None:
+        """Engine::dispatch (src/Modules/GPU/vk_engine.hpp:111-112) for the hot-path kernel names."""
+        arr = (Buf * len(bufs))(*bufs)
+        pbuf = ctypes.create_string_buffer(push, len(push))
+        self._check(lib().sdvk_dispatch(self._h, kernel.encode(), arr, len(bufs), pbuf, len(push), gx, gy, gz),
+                    f"dispatch({kernel})")
+
+    def check_finite(self, ptr: int, dtype: int, n: int) -> bool:
+        st = lib().sdvk_check_finite(self._h, ptr, dtype, n)
+        if st == E_NOT_FINITE:
+            return False
+        self._check(st, "check_finite")
+        return True
+
+
+def pack_pg(M, N, K, mode=0, sA=0, sB=0, sC=0, batch=1, lda=0, ldb=0, ldc=0) -> bytes:
+    """Pg push constants of the Q8 GEMM kernels (sdvkgen.cpp:901-903)."""
+    return struct.pack("<12I", M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, 0)
+
+
+def pack_fa(Tq, Tk, C, heads, hd, causal, scale) -> bytes:
+    """FaPush of the fused attention kernels (fused_attn.cpp:15-26)."""
+    return struct.pack("<8If", Tq, Tk, C, heads, hd, int(causal), 0, 0, scale)

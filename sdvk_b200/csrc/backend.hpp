@@ -1,0 +1,58 @@
+// backend.hpp -- internal interface between the C ABI (sdvk_abi.cu) and the kernel launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "../../include/sdvk_cuda.h"
+
+namespace sdvk {
+
+// What every launcher needs from the context.
+struct LaunchEnv {
+    cudaStream_t stream;
+    uint32_t* err_dev;    // device error word the kernels OR their error codes into
+    uint64_t timeout_ns;  // deadline of every bounded wait inside a kernel
+    int device;
+    int num_sms;
+    std::string* msg;     // error text for sdvk_last_error
+};
+
+// One Q8_0 GEMM in kernel terms: x = activation operand, w = quantised weight operand.
+//   nn == false: C[z][x][w] = sum_k X[z][x][k] * W[w][k]      (X row stride ldx)
+//   nn == true:  C[z][w][x] = sum_k W[z][w][k] * X[z][k][x]   (X row stride ldx along k)
+struct GemmQ8Desc {
+    const void* x;
+    int x_dtype;
+    uint64_t ldx, sx;
+    const int8_t* wq;
+    const float* ws;
+    uint64_t ldw, sw;
+    const float* bias;  // per w row, or null
+    void* c;
+    int c_dtype;
+    uint64_t ldc, sc;
+    uint32_t xrows, wrows, K, batch;
+    bool nn;
+    bool accumulate;
+};
+
+int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env);
+int attention(const sdvk_attn_desc& d, const LaunchEnv& env);
+int check_finite(const void* x, int dtype, uint64_t n, uint32_t* flag_dev, const LaunchEnv& env);
+
+inline int dtype_size(int dt) { return dt == SDVK_F32 ? 4 : (dt == SDVK_F16 || dt == SDVK_BF16) ? 2 : 0; }
+
+inline int fail(const LaunchEnv& env, int code, const std::string& what) {
+    if (env.msg) *env.msg = what;
+    return code;
+}
+
+inline int cuda_check(const LaunchEnv& env, cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return SDVK_OK;
+    return fail(env, SDVK_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+}  // namespace sdvk

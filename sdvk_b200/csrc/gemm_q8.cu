@@ -1,0 +1,193 @@
+// gemm_q8.cu -- host side of the Q8_0 tensor-core GEMM: argument checks, TMA tensor maps, tile
+// selection and launch of gemm_q8_tc_kernel (gemm_q8.cuh).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "backend.hpp"
+#include "gemm_q8.cuh"
+
+namespace sdvk {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D tiled tensor map: dims {d0 (contiguous), d1, d2}, byte strides for d1 and d2.
+int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+             uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw, const LaunchEnv& env,
+             const char* what) {
+    auto fn = encode_fn();
+    if (!fn) return fail(env, SDVK_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if (d2 <= 1) {
+        d2 = 1;
+        s2 = s1 * d1;
+    }
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {b0, b1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(env, SDVK_E_SHAPE, std::string("tensor map rejected: ") + what);
+    return SDVK_OK;
+}
+
+CUtensorMapDataType tma_type(int dt) {
+    return dt == SDVK_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                          : dt == SDVK_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// K == 0: the product is empty, so C = bias (or 0), or C += bias when accumulating.
+__global__ void gemm_k0_fill(float* c, const float* bias, uint32_t rows, uint32_t cols, uint64_t ld, uint64_t sb,
+                             uint32_t batch, bool bias_per_row, bool accumulate) {
+    const uint64_t n = (uint64_t)rows * cols * batch;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t z = i / ((uint64_t)rows * cols), rc = i % ((uint64_t)rows * cols);
+        const uint32_t r = (uint32_t)(rc / cols), cc = (uint32_t)(rc % cols);
+        const float b = bias ? bias[bias_per_row ? r : cc] : 0.0f;
+        float* dst = c + z * sb + (uint64_t)r * ld + cc;
+        *dst = accumulate ? *dst + b : b;
+    }
+}
+
+bool set_smem_attr(const void* kern, int bytes, int device) {
+    static std::mutex mu;
+    static uint64_t done[64] = {};
+    static const void* keys[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < 64; ++i) {
+        if (keys[i] == kern) {
+            if (done[i] & (1ull << device)) return true;
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+                return false;
+            done[i] |= 1ull << device;
+            return true;
+        }
+        if (!keys[i]) {
+            keys[i] = kern;
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+                return false;
+            done[i] = 1ull << device;
+            return true;
+        }
+    }
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+}
+
+template <class TA, int BN, bool NN, class TC>
+int launch(const GemmQ8Desc& d, const LaunchEnv& env) {
+    using Cfg = GemmQ8Config<TA, BN>;
+    const int es = sizeof(TA), ces = sizeof(TC);
+    CUtensorMap tmA, tmW, tmC;
+    int rc;
+    if (!NN) {
+        rc = make_map(&tmA, tma_type(d.x_dtype), d.x, d.K, d.xrows, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
+                      Cfg::kBM, CU_TENSOR_MAP_SWIZZLE_128B, env, "activation");
+    } else {
+        rc = make_map(&tmA, tma_type(d.x_dtype), d.x, d.xrows, d.K, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
+                      Cfg::kBK, CU_TENSOR_MAP_SWIZZLE_128B, env, "activation");
+    }
+    if (rc) return rc;
+    rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, d.wq, d.K, d.wrows, d.sw ? d.batch : 1, d.ldw, d.sw,
+                  Cfg::kBK, BN, CU_TENSOR_MAP_SWIZZLE_NONE, env, "weight");
+    if (rc) return rc;
+    if (!NN) {
+        rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.wrows, d.xrows, d.batch, d.ldc * ces, d.sc * ces, 32, 32,
+                      ces == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, env, "output");
+    } else {
+        rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.xrows, d.wrows, d.batch, d.ldc * ces, d.sc * ces, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, env, "output");
+    }
+    if (rc) return rc;
+
+    GemmQ8Params p{};
+    p.wq = d.wq;
+    p.ws = d.ws;
+    p.bias = d.bias;
+    p.xrows = d.xrows;
+    p.wrows = d.wrows;
+    p.K = d.K;
+    p.batch = d.batch;
+    p.ldw = d.ldw;
+    p.sW = d.sw;
+    p.tiles_x = (d.xrows + Cfg::kBM - 1) / Cfg::kBM;
+    p.tiles_w = (d.wrows + BN - 1) / BN;
+    p.num_tiles = p.tiles_x * p.tiles_w * d.batch;
+    p.k_stages = (d.K + Cfg::kBK - 1) / Cfg::kBK;
+    p.accumulate = d.accumulate ? 1u : 0u;
+    p.err = env.err_dev;
+    p.timeout_ns = env.timeout_ns;
+
+    auto kern = gemm_q8_tc_kernel<TA, BN, NN, TC>;
+    if (!set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, env.device))
+        return fail(env, SDVK_E_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
+    const uint32_t grid = std::min<uint32_t>(p.num_tiles, (uint32_t)env.num_sms);
+    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, env.stream>>>(tmA, tmW, tmC, p);
+    return cuda_check(env, cudaGetLastError(), "gemm_q8_tc_kernel launch");
+}
+
+template <class TA, bool NN, class TC>
+int launch_bn(const GemmQ8Desc& d, const LaunchEnv& env) {
+    if (d.wrows <= 128) return launch<TA, 128, NN, TC>(d, env);
+    return launch<TA, 256, NN, TC>(d, env);
+}
+
+template <class TA, bool NN>
+int launch_c(const GemmQ8Desc& d, const LaunchEnv& env) {
+    if (d.c_dtype == SDVK_F32) return launch_bn<TA, NN, float>(d, env);
+    return launch_bn<TA, NN, __half>(d, env);
+}
+
+template <bool NN>
+int launch_a(const GemmQ8Desc& d, const LaunchEnv& env) {
+    switch (d.x_dtype) {
+        case SDVK_F16: return launch_c<__half, NN>(d, env);
+        case SDVK_BF16: return launch_c<__nv_bfloat16, NN>(d, env);
+        default: return launch_c<float, NN>(d, env);
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env) {
+    if (!d.x || !d.wq || !d.ws || !d.c) return fail(env, SDVK_E_ARG, "null pointer");
+    if (d.x_dtype != SDVK_F32 && d.x_dtype != SDVK_F16 && d.x_dtype != SDVK_BF16)
+        return fail(env, SDVK_E_ARG, "activation dtype must be F32, F16 or BF16");
+    if (d.c_dtype != SDVK_F32 && d.c_dtype != SDVK_F16) return fail(env, SDVK_E_ARG, "output dtype must be F32 or F16");
+    if (d.accumulate && d.c_dtype != SDVK_F32) return fail(env, SDVK_E_ARG, "accumulate requires an F32 output");
+    if (d.batch == 0 || d.xrows == 0 || d.wrows == 0) return SDVK_OK;
+    if (d.K % 32) return fail(env, SDVK_E_SHAPE, "K must be a multiple of 32 (whole Q8_0 blocks)");
+    if (d.ldw % 32 || d.sw % 32 || d.ldw < d.K) return fail(env, SDVK_E_SHAPE, "weight strides must be multiples of 32");
+    const int es = dtype_size(d.x_dtype), ces = dtype_size(d.c_dtype);
+    const uint64_t xmin = d.nn ? d.xrows : d.K, cmin = d.nn ? d.xrows : d.wrows;
+    if (d.ldx < xmin || d.ldc < cmin) return fail(env, SDVK_E_SHAPE, "row stride smaller than the row");
+    if (!aligned16(d.x) || !aligned16(d.c) || !aligned16(d.wq))
+        return fail(env, SDVK_E_SHAPE, "operands must be 16-byte aligned");
+    if ((d.ldx * es) % 16 || (d.ldc * ces) % 16 || (d.batch > 1 && ((d.sx * es) % 16 || (d.sc * ces) % 16)))
+        return fail(env, SDVK_E_SHAPE, "row/batch strides must be multiples of 16 bytes");
+    if (d.K == 0) {
+        if (d.accumulate && !d.bias) return SDVK_OK;
+        if (d.c_dtype != SDVK_F32) return fail(env, SDVK_E_SHAPE, "K == 0 needs an F32 output");
+        const uint32_t rows = d.nn ? d.wrows : d.xrows, cols = d.nn ? d.xrows : d.wrows;
+        gemm_k0_fill<<<256, 256, 0, env.stream>>>(static_cast<float*>(d.c), d.bias, rows, cols, d.ldc, d.sc, d.batch,
+                                                   d.nn, d.accumulate);
+        return cuda_check(env, cudaGetLastError(), "gemm_k0_fill launch");
+    }
+    return d.nn ? launch_a<true>(d, env) : launch_a<false>(d, env);
+}
+
+}  // namespace sdvk

@@ -1,0 +1,469 @@
+// gemm_q8.cuh -- Q8_0 dequant GEMM on the sm_100a tensor cores (tcgen05 + TMA + TMEM).
+//
+// One kernel template serves both reference GEMM shapes:
+//   NT (gemm_nt_q8_v.comp):  C[M,N]  = A[M,K] . (q[N,K]*s)^T (+bias[N])     activation is K-major
+//   NN (gemm_nn_q8_v.comp):  C[M,N]  = (q[M,K]*s) . B[K,N]                  activation is N-major
+// In both, the tensor-core "M" side is the activation (x rows: NT tokens M, NN tokens N) and the
+// tensor-core "N" side is the weight (w rows: NT out-features N, NN out-channels M).  The TMEM
+// accumulator is D[x][w]; the NN epilogue stores it transposed.
+//
+// Per CTA (persistent, one per SM, 16 warps):
+//   warp 0      TMA producer: activation tile (128 x 128B, 128B-swizzled) + raw int8 weight tile
+//   warp 1      TMEM allocator and the single MMA-issuing thread
+//   warps 4-11  dequantisers: int8 smem tile * per-32-block scale -> f16/bf16/f32 operand tile in
+//               the 128B-swizzled K-major layout the tensor core reads
+//   warps 12-15 epilogue: TMEM -> registers (+bias) -> swizzled smem -> TMA store / TMA reduce-add
+// Rings: 4 activation/raw-weight stages, 2 dequantised-weight stages, 2 TMEM accumulators, so
+// loads, dequantisation, MMA and the previous tile's epilogue all overlap.
+//
+// Every mbarrier wait is bounded (GemmQ8Params::timeout_ns): a wait that runs out records
+// kErrTimeout in *err, the CTA drains its in-flight copies and MMAs, frees TMEM and returns.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace sdvk {
+
+struct GemmQ8Params {
+    const int8_t* wq;       // weight payload, element (row, k) of batch z at wq[z*sW + row*ldw + k]
+    const float* ws;        // fp32 scale per 32 payload elements (flat index >> 5)
+    const float* bias;      // per weight row (NT: per output column, NN: per output row), or null
+    uint32_t xrows;         // activation rows (tensor-core M extent)
+    uint32_t wrows;         // weight rows (tensor-core N extent)
+    uint32_t K;
+    uint32_t batch;
+    uint64_t ldw;           // weight row stride in elements (multiple of 32)
+    uint64_t sW;            // weight batch stride in elements (0: one weight for all batches)
+    uint32_t tiles_x, tiles_w, num_tiles, k_stages;
+    uint32_t accumulate;    // 0: C = result, 1: C += result (TMA reduce-add)
+    uint32_t* err;          // device error word
+    uint64_t timeout_ns;
+};
+
+template <class TA>
+struct OperandTraits;
+template <>
+struct OperandTraits<__half> {
+    static constexpr uint32_t kFmt = 0;  // f16
+    static constexpr bool kTf32 = false;
+};
+template <>
+struct OperandTraits<__nv_bfloat16> {
+    static constexpr uint32_t kFmt = 1;  // bf16
+    static constexpr bool kTf32 = false;
+};
+template <>
+struct OperandTraits<float> {
+    static constexpr uint32_t kFmt = 2;  // tf32
+    static constexpr bool kTf32 = true;
+};
+
+template <class TA, int BN>
+struct GemmQ8Config {
+    static constexpr int kBM = 128;
+    static constexpr int kES = sizeof(TA);
+    static constexpr int kBK = 128 / kES;            // K elements per 128-byte swizzle row
+    static constexpr int kUmmaK = 32 / kES;          // K per tcgen05.mma (32 bytes)
+    static constexpr int kStages = 4;
+    static constexpr int kBStages = 2;
+    static constexpr int kAcc = 2;
+    static constexpr int kABytes = kBM * 128;        // activation stage
+    static constexpr int kWBytes = BN * kBK;         // raw int8 stage
+    static constexpr int kBBytes = BN * 128;         // dequantised stage
+    static constexpr int kEpiBytes = 4 * 2 * 32 * 32 * 4;  // 4 warps x 2 buffers x 32x32 fp32
+    static constexpr uint32_t kTmemCols = (kAcc * BN <= 32) ? 32 : (kAcc * BN <= 64) ? 64 : (kAcc * BN <= 128) ? 128 : (kAcc * BN <= 256) ? 256 : 512;
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + kStages * kABytes;
+    static constexpr int kOffW = kOffB + kBStages * kBBytes;
+    static constexpr int kOffEpi = kOffW + kStages * kWBytes;
+    static constexpr int kOffBar = kOffEpi + kEpiBytes;
+    static constexpr int kNumBars = 3 * kStages + 2 * kBStages + 2 * kAcc + 1;
+    static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // +1024: manual alignment
+    static constexpr int kThreads = 512;
+    static constexpr int kConvThreads = 256;
+    static constexpr int kChunksPerRow = kBK / 16;  // 16 int8 per dequant task
+    static constexpr int kTasksPerThread = BN * kChunksPerRow / kConvThreads;
+    static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+    static_assert(kAcc * BN <= 512, "TMEM");
+    static_assert(kSmemBytes <= 232448, "shared memory");
+    static_assert((BN * kChunksPerRow) % kConvThreads == 0, "dequant task split");
+};
+
+// Dequantise 16 int8 (one uint4) with one scale into 16 operand elements written as 16-byte
+// chunks `chunk0 .. chunk0+n-1` of a 128-byte swizzled row at `row_base` (row index r).
+template <class TA>
+__device__ __forceinline__ void dequant16(const uint4 raw, float scale, uint8_t* row_base, int r, int chunk0);
+
+template <>
+__device__ __forceinline__ void dequant16<__half>(const uint4 raw, float scale, uint8_t* row_base, int r, int chunk0) {
+    // int8 -> fp16 exactly: byte^0x80 is v+128; placing it under exponent 0x64 gives the half
+    // 1024+v+128; subtracting 1152 leaves v.  One hmul2 then rounds v*s to fp16 once.
+    const __half2 s2 = __float2half2_rn(scale);
+    const __half2 bias = __float2half2_rn(1152.0f);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t x = w[i] ^ 0x80808080u;
+        uint32_t lo = __byte_perm(x, 0x64646464u, 0x4140u);
+        uint32_t hi = __byte_perm(x, 0x64646464u, 0x4342u);
+        __half2 l2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&lo), bias), s2);
+        __half2 h2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&hi), bias), s2);
+        o[2 * i] = *reinterpret_cast<uint32_t*>(&l2);
+        o[2 * i + 1] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    const int sw = r & 7;
+    *reinterpret_cast<uint4*>(row_base + (((chunk0 + 0) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(row_base + (((chunk0 + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__device__ __forceinline__ void int8x4_to_f32(uint32_t w, float (&f)[4]) {
+    // byte^0x80 placed in the low mantissa byte of 2^23 gives 2^23 + v + 128 exactly.
+    const uint32_t x = w ^ 0x80808080u;
+    f[0] = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7440u)) - 8388736.0f;
+    f[1] = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7441u)) - 8388736.0f;
+    f[2] = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7442u)) - 8388736.0f;
+    f[3] = __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7443u)) - 8388736.0f;
+}
+
+template <>
+__device__ __forceinline__ void dequant16<__nv_bfloat16>(const uint4 raw, float scale, uint8_t* row_base, int r,
+                                                         int chunk0) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float f[4];
+        int8x4_to_f32(w[i], f);
+        __nv_bfloat162 a = __floats2bfloat162_rn(f[0] * scale, f[1] * scale);
+        __nv_bfloat162 b = __floats2bfloat162_rn(f[2] * scale, f[3] * scale);
+        o[2 * i] = *reinterpret_cast<uint32_t*>(&a);
+        o[2 * i + 1] = *reinterpret_cast<uint32_t*>(&b);
+    }
+    const int sw = r & 7;
+    *reinterpret_cast<uint4*>(row_base + (((chunk0 + 0) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(row_base + (((chunk0 + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__device__ __forceinline__ uint32_t round_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+template <>
+__device__ __forceinline__ void dequant16<float>(const uint4 raw, float scale, uint8_t* row_base, int r, int chunk0) {
+    // float(int8) * scale in fp32 (the reference's own dequantisation), then rounded to tf32.
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    const int sw = r & 7;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float f[4];
+        int8x4_to_f32(w[i], f);
+        *reinterpret_cast<uint4*>(row_base + (((chunk0 + i) ^ sw) << 4)) =
+            make_uint4(round_tf32(f[0] * scale), round_tf32(f[1] * scale), round_tf32(f[2] * scale),
+                       round_tf32(f[3] * scale));
+    }
+}
+
+template <class TC>
+__device__ __forceinline__ void store_epi_row(uint8_t* buf, int lane, const float (&v)[32]);
+
+template <>
+__device__ __forceinline__ void store_epi_row<float>(uint8_t* buf, int lane, const float (&v)[32]) {
+    // 32 fp32 = one 128-byte row, 128B-swizzled (matches the store tensor map).
+    uint8_t* row = buf + lane * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<float4*>(row + ((c ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+template <>
+__device__ __forceinline__ void store_epi_row<__half>(uint8_t* buf, int lane, const float (&v)[32]) {
+    // 32 fp16 = one 64-byte row, 64B-swizzled.
+    uint8_t* row = buf + lane * 64;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        __half2 h0 = __floats2half2_rn(v[8 * c + 0], v[8 * c + 1]);
+        __half2 h1 = __floats2half2_rn(v[8 * c + 2], v[8 * c + 3]);
+        __half2 h2 = __floats2half2_rn(v[8 * c + 4], v[8 * c + 5]);
+        __half2 h3 = __floats2half2_rn(v[8 * c + 6], v[8 * c + 7]);
+        *reinterpret_cast<uint4*>(row + ((c ^ ((lane >> 1) & 3)) << 4)) =
+            make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                       *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+    }
+}
+// Transposed tile for the NN store: element (w = j, x = lane) of a [32 w][32 x] row-major tile.
+template <class TC>
+__device__ __forceinline__ void store_epi_col(uint8_t* buf, int lane, const float (&v)[32]) {
+    TC* t = reinterpret_cast<TC*>(buf);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if constexpr (sizeof(TC) == 4) t[j * 32 + lane] = v[j];
+        else t[j * 32 + lane] = __float2half_rn(v[j]);
+    }
+}
+
+template <class TA, int BN, bool NN, class TC>
+__global__ void __launch_bounds__(512, 1)
+    gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                      const __grid_constant__ CUtensorMap tmC, const GemmQ8Params p) {
+    using Cfg = GemmQ8Config<TA, BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem + Cfg::kOffA;
+    uint8_t* sB = smem + Cfg::kOffB;
+    uint8_t* sW = smem + Cfg::kOffW;
+    uint8_t* sEpi = smem + Cfg::kOffEpi;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+    uint64_t* ld_full = bars;                                // [kStages] TMA tx (activation + raw weight)
+    uint64_t* a_empty = ld_full + Cfg::kStages;              // [kStages] MMA commit
+    uint64_t* w_empty = a_empty + Cfg::kStages;              // [kStages] 8 dequant warps
+    uint64_t* b_full = w_empty + Cfg::kStages;               // [kBStages] 8 dequant warps
+    uint64_t* b_empty = b_full + Cfg::kBStages;              // [kBStages] MMA commit
+    uint64_t* acc_full = b_empty + Cfg::kBStages;            // [kAcc] MMA commit
+    uint64_t* acc_empty = acc_full + Cfg::kAcc;              // [kAcc] 4 epilogue warps
+    uint64_t* mma_done = acc_empty + Cfg::kAcc;              // final drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < Cfg::kStages; ++i) {
+            mbar_init(&ld_full[i], 1);
+            mbar_init(&a_empty[i], 1);
+            mbar_init(&w_empty[i], 8);
+        }
+        for (int i = 0; i < Cfg::kBStages; ++i) {
+            mbar_init(&b_full[i], 8);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < Cfg::kAcc; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);
+        }
+        mbar_init(mma_done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmC);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 2 || warp == 3) return;  // spare warps take no part in the pipeline
+
+    bool ok = true;
+    auto fail = [&]() {
+        atomicOr(p.err, kErrTimeout);
+        ok = false;
+    };
+    auto decode = [&](uint32_t tile, uint32_t& z, uint32_t& xt, uint32_t& wt) {
+        wt = tile % p.tiles_w;
+        const uint32_t rest = tile / p.tiles_w;
+        xt = rest % p.tiles_x;
+        z = rest / p.tiles_x;
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (uint32_t tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+                uint32_t z, xt, wt;
+                decode(tile, z, xt, wt);
+                const int zw = p.sW ? (int)z : 0;
+                for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
+                    const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+                    if (!mbar_wait(&a_empty[slot], ph ^ 1, p.timeout_ns) ||
+                        !mbar_wait(&w_empty[slot], ph ^ 1, p.timeout_ns)) {
+                        fail();
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&ld_full[slot], Cfg::kABytes + Cfg::kWBytes);
+                    const int k0 = (int)(ks * Cfg::kBK);
+                    uint8_t* a_dst = sA + slot * Cfg::kABytes;
+                    if constexpr (!NN) {
+                        tma_load_3d(a_dst, &tmA, &ld_full[slot], k0, (int)(xt * Cfg::kBM), (int)z);
+                    } else {
+                        // N-major activation: kBM/kBK boxes of [kBK k-rows][kBK x-elements].
+#pragma unroll
+                        for (int j = 0; j < Cfg::kBM / Cfg::kBK; ++j)
+                            tma_load_3d(a_dst + j * Cfg::kBK * 128, &tmA, &ld_full[slot],
+                                        (int)(xt * Cfg::kBM) + j * Cfg::kBK, k0, (int)z);
+                    }
+                    tma_load_3d(sW + slot * Cfg::kWBytes, &tmW, &ld_full[slot], k0, (int)(wt * BN), zw);
+                }
+            }
+            // Drain: make sure no load this CTA issued is still landing in shared memory.
+            const uint32_t issued = it;
+            for (uint32_t i = (issued > Cfg::kStages ? issued - Cfg::kStages : 0); i < issued; ++i)
+                if (!mbar_wait(&ld_full[i % Cfg::kStages], (i / Cfg::kStages) & 1, p.timeout_ns)) fail();
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = make_idesc(OperandTraits<TA>::kFmt, OperandTraits<TA>::kFmt, NN ? 1 : 0, 0,
+                                                  Cfg::kBM, BN);
+            uint32_t it = 0, bit = 0, tcount = 0;
+            for (uint32_t tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+                const uint32_t acc = tcount % Cfg::kAcc, aph = (tcount / Cfg::kAcc) & 1;
+                if (!mbar_wait(&acc_empty[acc], aph ^ 1, p.timeout_ns)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it, ++bit) {
+                    const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+                    const uint32_t bslot = bit % Cfg::kBStages, bph = (bit / Cfg::kBStages) & 1;
+                    if (!mbar_wait(&ld_full[slot], ph, p.timeout_ns) ||
+                        !mbar_wait(&b_full[bslot], bph, p.timeout_ns)) {
+                        fail();
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + slot * Cfg::kABytes);
+                    const uint32_t b_addr = smem_u32(sB + bslot * Cfg::kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < Cfg::kBK / Cfg::kUmmaK; ++kk) {
+                        uint64_t adesc;
+                        if constexpr (!NN)
+                            adesc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+                        else  // MN-major: k advances by kUmmaK rows of 128 B; x chunks kBK*128 B apart
+                            adesc = smem_desc_sw128(a_addr + kk * Cfg::kUmmaK * 128, Cfg::kBK * 128, 1024);
+                        const uint64_t bdesc = smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+                        const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
+                        if constexpr (OperandTraits<TA>::kTf32) mma_tf32(d_tmem, adesc, bdesc, idesc, accum);
+                        else mma_f16(d_tmem, adesc, bdesc, idesc, accum);
+                    }
+                    mma_commit(&a_empty[slot]);
+                    mma_commit(&b_empty[bslot]);
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[acc]);
+            }
+            // Drain: every MMA issued by this thread completes before TMEM is released.
+            mma_commit(mma_done);
+            if (!mbar_wait(mma_done, 0, p.timeout_ns)) fail();
+        }
+    } else if (warp >= 4 && warp < 12) {
+        // ------------------------------------------------------------ dequantisers
+        const int ct = threadIdx.x - 128;
+        const int chunk = ct % Cfg::kChunksPerRow;
+        const int row0 = ct / Cfg::kChunksPerRow;
+        constexpr int kRowStep = Cfg::kConvThreads / Cfg::kChunksPerRow;
+        const uint64_t kblocks = p.K / 32;
+        const uint64_t ldw_blocks = p.ldw / 32;
+        uint32_t it = 0, bit = 0;
+        for (uint32_t tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+            uint32_t z, xt, wt;
+            decode(tile, z, xt, wt);
+            const float* ws = p.ws + (p.sW ? (uint64_t)z * (p.sW / 32) : 0);
+            for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it, ++bit) {
+                const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+                const uint32_t bslot = bit % Cfg::kBStages, bph = (bit / Cfg::kBStages) & 1;
+                // Scales first: their L2 latency overlaps the barrier waits.
+                const uint64_t kb = ((uint64_t)ks * Cfg::kBK + (uint64_t)chunk * 16) / 32;
+                float sc[Cfg::kTasksPerThread];
+#pragma unroll
+                for (int j = 0; j < Cfg::kTasksPerThread; ++j) {
+                    const uint32_t n = wt * BN + row0 + j * kRowStep;
+                    sc[j] = (n < p.wrows && kb < kblocks) ? __ldg(ws + (uint64_t)n * ldw_blocks + kb) : 0.0f;
+                }
+                if (!mbar_wait(&ld_full[slot], ph, p.timeout_ns) ||
+                    !mbar_wait(&b_empty[bslot], bph ^ 1, p.timeout_ns)) {
+                    fail();
+                    break;
+                }
+                const uint8_t* wsrc = sW + slot * Cfg::kWBytes;
+                uint8_t* bdst = sB + bslot * Cfg::kBBytes;
+#pragma unroll
+                for (int j = 0; j < Cfg::kTasksPerThread; ++j) {
+                    const int r = row0 + j * kRowStep;
+                    const uint4 raw = *reinterpret_cast<const uint4*>(wsrc + r * Cfg::kBK + chunk * 16);
+                    dequant16<TA>(raw, sc[j], bdst + r * 128, r, chunk * Cfg::kES);  // 16 elements = kES chunks
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&w_empty[slot]);
+                    mbar_arrive(&b_full[bslot]);
+                }
+            }
+        }
+    } else if (warp >= 12) {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;  // TMEM lane quarter this warp may read
+        uint8_t* ebuf = sEpi + q * (2 * 4096);
+        uint32_t tcount = 0, nstore = 0;
+        for (uint32_t tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++tcount) {
+            uint32_t z, xt, wt;
+            decode(tile, z, xt, wt);
+            const uint32_t acc = tcount % Cfg::kAcc, aph = (tcount / Cfg::kAcc) & 1;
+            if (!mbar_wait(&acc_full[acc], aph, p.timeout_ns)) {
+                fail();
+                break;
+            }
+            tc_fence_after();
+            const int x0 = (int)(xt * Cfg::kBM) + q * 32;
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 32; ++cc, ++nstore) {
+                const int w0 = (int)(wt * BN) + cc * 32;
+                uint32_t raw[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + cc * 32, raw);
+                tmem_wait_ld();
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+                if (p.bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const uint32_t n = (uint32_t)w0 + j;
+                        v[j] += (n < p.wrows) ? __ldg(p.bias + n) : 0.0f;
+                    }
+                }
+                uint8_t* buf = ebuf + (nstore & 1) * 4096;
+                if (lane == 0) bulk_wait_read<1>();  // the store that last used `buf` has read it
+                __syncwarp();
+                if constexpr (!NN) store_epi_row<TC>(buf, lane, v);
+                else store_epi_col<TC>(buf, lane, v);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (!NN) {
+                        if (p.accumulate) tma_reduce_add_3d(&tmC, buf, w0, x0, (int)z);
+                        else tma_store_3d(&tmC, buf, w0, x0, (int)z);
+                    } else {
+                        if (p.accumulate) tma_reduce_add_3d(&tmC, buf, x0, w0, (int)z);
+                        else tma_store_3d(&tmC, buf, x0, w0, (int)z);
+                    }
+                    bulk_commit();
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+
+    // ---------------------------------------------------------------- teardown
+    asm volatile("bar.sync 1, 448;" ::: "memory");  // warps 0, 1, 4-15
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+}  // namespace sdvk

@@ -1,0 +1,471 @@
+// sdvk_abi.cu -- the extern "C" boundary declared in include/sdvk_cuda.h: context, memory, step
+// protocol, the reference-compatible name dispatch and the typed hot-path entry points.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <thread>
+
+#include "backend.hpp"
+
+struct sdvk_ctx {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    uint32_t* err_dev = nullptr;   // kernels OR device error codes in here
+    uint32_t* flag_dev = nullptr;  // sdvk_check_finite
+    uint64_t timeout_ns = 2000000000ull;
+    cudaEvent_t step_done = nullptr;
+    bool in_step = false;
+    bool step_recorded = false;
+    std::string last_error;
+    std::string device_name;
+};
+
+namespace {
+
+// Mirrors of the reference push-constant blocks (sdvkgen.cpp:901-903, fused_attn.cpp:15-26).
+struct Pg {
+    uint32_t M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, pad;
+};
+struct FaPush {
+    uint32_t Tq, Tk, C, heads, hd, causal, pad0, pad1;
+    float scale;
+};
+static_assert(sizeof(Pg) == 48, "Pg layout");
+static_assert(sizeof(FaPush) == 36, "FaPush layout");
+
+int set_err(sdvk_ctx* ctx, int code, const std::string& msg) {
+    if (ctx) ctx->last_error = msg;
+    return code;
+}
+
+int cuda_err(sdvk_ctx* ctx, cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return SDVK_OK;
+    return set_err(ctx, SDVK_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Make the context's device current for this thread (callers may switch devices in between).
+int use_device(sdvk_ctx* ctx) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != ctx->device)
+        return cuda_err(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+    return SDVK_OK;
+}
+
+sdvk::LaunchEnv env_of(sdvk_ctx* ctx) {
+    return sdvk::LaunchEnv{ctx->stream, ctx->err_dev, ctx->timeout_ns, ctx->device, ctx->num_sms, &ctx->last_error};
+}
+
+// After a synchronisation point: surface (and clear) any device-side error code.
+int collect_device_error(sdvk_ctx* ctx) {
+    uint32_t err = 0;
+    cudaError_t e = cudaMemcpy(&err, ctx->err_dev, sizeof(err), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_err(ctx, e, "reading device error word");
+    if (err) {
+        cudaMemset(ctx->err_dev, 0, sizeof(uint32_t));
+        return set_err(ctx, SDVK_E_TIMEOUT, "a kernel's bounded wait timed out (device error word " +
+                                                std::to_string(err) + ")");
+    }
+    return SDVK_OK;
+}
+
+bool buf_holds(const sdvk_buf& b, uint64_t bytes) { return b.ptr && (b.size == 0 || bytes <= b.size); }
+const void* buf_ptr(const sdvk_buf& b) { return static_cast<const char*>(b.ptr) + b.offset; }
+void* buf_mptr(const sdvk_buf& b) { return static_cast<char*>(b.ptr) + b.offset; }
+
+}  // namespace
+
+extern "C" {
+
+const char* sdvk_status_string(int s) {
+    switch (s) {
+        case SDVK_OK: return "ok";
+        case SDVK_E_OOM: return "out of memory";
+        case SDVK_E_SHAPE: return "unsupported shape or layout";
+        case SDVK_E_CUDA: return "CUDA error";
+        case SDVK_E_TIMEOUT: return "timeout";
+        case SDVK_E_ARG: return "invalid argument";
+        case SDVK_E_KERNEL: return "unknown kernel";
+        case SDVK_E_STATE: return "step protocol misuse";
+        case SDVK_E_NOT_FINITE: return "non-finite values";
+        default: return "unknown status";
+    }
+}
+
+int sdvk_ctx_create(int device, sdvk_ctx** out) {
+    if (!out) return SDVK_E_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return SDVK_E_ARG;
+    auto* ctx = new (std::nothrow) sdvk_ctx();
+    if (!ctx) return SDVK_E_OOM;
+    ctx->device = device;
+    int rc = cuda_err(ctx, cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop{};
+    if (!rc) rc = cuda_err(ctx, cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (!rc && prop.major != 10) rc = set_err(ctx, SDVK_E_CUDA, "sdvk-b200 kernels need an sm_100 (B200) device");
+    if (!rc) rc = cuda_err(ctx, cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking), "stream");
+    if (!rc) rc = cuda_err(ctx, cudaMalloc(&ctx->err_dev, 256), "cudaMalloc(error word)");
+    if (!rc) rc = cuda_err(ctx, cudaMemset(ctx->err_dev, 0, 256), "cudaMemset");
+    if (!rc) rc = cuda_err(ctx, cudaEventCreateWithFlags(&ctx->step_done, cudaEventDisableTiming), "event");
+    if (rc) {
+        sdvk_ctx_destroy(ctx);
+        return rc;
+    }
+    ctx->flag_dev = ctx->err_dev + 32;
+    ctx->stream = ctx->own_stream;
+    ctx->num_sms = prop.multiProcessorCount;
+    ctx->device_name = prop.name;
+    *out = ctx;
+    return SDVK_OK;
+}
+
+int sdvk_ctx_destroy(sdvk_ctx* ctx) {
+    if (!ctx) return SDVK_E_ARG;
+    cudaSetDevice(ctx->device);
+    if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
+    if (ctx->step_done) cudaEventDestroy(ctx->step_done);
+    if (ctx->err_dev) cudaFree(ctx->err_dev);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return SDVK_OK;
+}
+
+int sdvk_ctx_set_stream(sdvk_ctx* ctx, void* s) {
+    if (!ctx) return SDVK_E_ARG;
+    ctx->stream = s ? static_cast<cudaStream_t>(s) : ctx->own_stream;
+    return SDVK_OK;
+}
+
+void* sdvk_ctx_stream(sdvk_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int sdvk_ctx_set_timeout_ms(sdvk_ctx* ctx, uint32_t ms) {
+    if (!ctx || ms == 0) return SDVK_E_ARG;
+    ctx->timeout_ns = (uint64_t)ms * 1000000ull;
+    return SDVK_OK;
+}
+
+int sdvk_device_report(sdvk_ctx* ctx, char* buf, size_t len) {
+    if (!ctx || !buf || !len) return SDVK_E_ARG;
+    size_t free_b = 0, total_b = 0;
+    use_device(ctx);
+    cudaMemGetInfo(&free_b, &total_b);
+    std::snprintf(buf, len, "device|%d\nname|%s\nsms|%d\nmem_total_mb|%llu\nmem_free_mb|%llu\n", ctx->device,
+                  ctx->device_name.c_str(), ctx->num_sms, (unsigned long long)(total_b >> 20),
+                  (unsigned long long)(free_b >> 20));
+    return SDVK_OK;
+}
+
+const char* sdvk_last_error(sdvk_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "no context"; }
+
+// ------------------------------------------------------------------ memory
+int sdvk_alloc(sdvk_ctx* ctx, uint64_t bytes, void** dptr) {
+    if (!ctx || !dptr) return SDVK_E_ARG;
+    *dptr = nullptr;
+    if (int rc = use_device(ctx)) return rc;
+    if (cudaMalloc(dptr, bytes ? bytes : 256) != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(ctx, SDVK_E_OOM, "device allocation of " + std::to_string(bytes) + " bytes failed");
+    }
+    return SDVK_OK;
+}
+
+int sdvk_free(sdvk_ctx* ctx, void* dptr) {
+    if (!ctx) return SDVK_E_ARG;
+    if (!dptr) return SDVK_OK;
+    if (int rc = use_device(ctx)) return rc;
+    return cuda_err(ctx, cudaFree(dptr), "cudaFree");
+}
+
+int sdvk_host_alloc(sdvk_ctx* ctx, uint64_t bytes, void** hptr) {
+    if (!ctx || !hptr) return SDVK_E_ARG;
+    *hptr = nullptr;
+    if (cudaMallocHost(hptr, bytes ? bytes : 256) != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(ctx, SDVK_E_OOM, "pinned host allocation failed");
+    }
+    return SDVK_OK;
+}
+
+int sdvk_host_free(sdvk_ctx* ctx, void* hptr) {
+    if (!ctx) return SDVK_E_ARG;
+    return hptr ? cuda_err(ctx, cudaFreeHost(hptr), "cudaFreeHost") : SDVK_OK;
+}
+
+int sdvk_upload(sdvk_ctx* ctx, void* dst, const void* src, uint64_t bytes) {
+    if (!ctx || (!dst && bytes) || (!src && bytes)) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    if (int rc = cuda_err(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream), "upload"))
+        return rc;
+    return cuda_err(ctx, cudaStreamSynchronize(ctx->stream), "upload sync");
+}
+
+int sdvk_download(sdvk_ctx* ctx, void* dst, const void* src, uint64_t bytes) {
+    if (!ctx || (!dst && bytes) || (!src && bytes)) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    if (int rc = cuda_err(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "download"))
+        return rc;
+    if (int rc = cuda_err(ctx, cudaStreamSynchronize(ctx->stream), "download sync")) return rc;
+    return collect_device_error(ctx);
+}
+
+int sdvk_upload_async(sdvk_ctx* ctx, void* dst, const void* src, uint64_t bytes) {
+    if (!ctx || (!dst && bytes) || (!src && bytes)) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return cuda_err(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream), "upload_async");
+}
+
+int sdvk_download_async(sdvk_ctx* ctx, void* dst, const void* src, uint64_t bytes) {
+    if (!ctx || (!dst && bytes) || (!src && bytes)) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return cuda_err(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "download_async");
+}
+
+int sdvk_fill_u32(sdvk_ctx* ctx, void* dst, uint32_t value, uint64_t bytes) {
+    if (!ctx || !dst || bytes % 4) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    if (value == 0) return cuda_err(ctx, cudaMemsetAsync(dst, 0, bytes, ctx->stream), "fill");
+    if ((value & 0xFFu) * 0x01010101u == value)
+        return cuda_err(ctx, cudaMemsetAsync(dst, (int)(value & 0xFF), bytes, ctx->stream), "fill");
+    return set_err(ctx, SDVK_E_ARG, "sdvk_fill_u32 supports byte-repeating patterns only");
+}
+
+// ------------------------------------------------------------------ step protocol
+int sdvk_step_begin(sdvk_ctx* ctx) {
+    if (!ctx) return SDVK_E_ARG;
+    if (ctx->in_step) return set_err(ctx, SDVK_E_STATE, "step_begin inside an open step");
+    ctx->in_step = true;
+    ctx->step_recorded = false;
+    return use_device(ctx);
+}
+
+int sdvk_step_end(sdvk_ctx* ctx) {
+    if (!ctx) return SDVK_E_ARG;
+    if (!ctx->in_step) return set_err(ctx, SDVK_E_STATE, "step_end without step_begin");
+    ctx->in_step = false;
+    if (int rc = use_device(ctx)) return rc;
+    if (int rc = cuda_err(ctx, cudaEventRecord(ctx->step_done, ctx->stream), "step event")) return rc;
+    ctx->step_recorded = true;
+    return SDVK_OK;
+}
+
+int sdvk_step_wait(sdvk_ctx* ctx, uint32_t timeout_ms) {
+    if (!ctx) return SDVK_E_ARG;
+    if (!ctx->step_recorded) return set_err(ctx, SDVK_E_STATE, "step_wait without a finished step");
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        cudaError_t e = cudaEventQuery(ctx->step_done);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return cuda_err(ctx, e, "step wait");
+        if (timeout_ms && std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
+            return set_err(ctx, SDVK_E_TIMEOUT, "step did not finish within the deadline");
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    ctx->step_recorded = false;
+    return collect_device_error(ctx);
+}
+
+int sdvk_synchronize(sdvk_ctx* ctx) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    if (int rc = cuda_err(ctx, cudaStreamSynchronize(ctx->stream), "synchronize")) return rc;
+    return collect_device_error(ctx);
+}
+
+// ------------------------------------------------------------------ typed entry points
+int sdvk_gemm_q8_nt(sdvk_ctx* ctx, const void* A, int a_dtype, const int8_t* q, const float* s, const float* bias,
+                    void* C, int c_dtype, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldc,
+                    uint32_t batch, uint64_t sA, uint64_t sC, int accumulate) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    sdvk::GemmQ8Desc d{};
+    d.x = A;
+    d.x_dtype = a_dtype;
+    d.ldx = lda ? lda : K;
+    d.sx = sA;
+    d.wq = q;
+    d.ws = s;
+    d.ldw = K;
+    d.sw = 0;
+    d.bias = bias;
+    d.c = C;
+    d.c_dtype = c_dtype;
+    d.ldc = ldc ? ldc : N;
+    d.sc = sC;
+    d.xrows = M;
+    d.wrows = N;
+    d.K = K;
+    d.batch = batch ? batch : 1;
+    d.nn = false;
+    d.accumulate = accumulate != 0;
+    return sdvk::gemm_q8(d, env_of(ctx));
+}
+
+int sdvk_gemm_q8_nn(sdvk_ctx* ctx, const int8_t* q, const float* s, const void* B, int b_dtype, const float* bias,
+                    void* C, int c_dtype, uint32_t M, uint32_t N, uint32_t K, uint32_t lda, uint32_t ldb,
+                    uint32_t ldc, uint32_t batch, uint64_t sA, uint64_t sB, uint64_t sC, int accumulate) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    sdvk::GemmQ8Desc d{};
+    d.x = B;
+    d.x_dtype = b_dtype;
+    d.ldx = ldb ? ldb : N;
+    d.sx = sB;
+    d.wq = q;
+    d.ws = s;
+    d.ldw = lda ? lda : K;
+    d.sw = sA;
+    d.bias = bias;
+    d.c = C;
+    d.c_dtype = c_dtype;
+    d.ldc = ldc ? ldc : N;
+    d.sc = sC;
+    d.xrows = N;
+    d.wrows = M;
+    d.K = K;
+    d.batch = batch ? batch : 1;
+    d.nn = true;
+    d.accumulate = accumulate != 0;
+    return sdvk::gemm_q8(d, env_of(ctx));
+}
+
+int sdvk_attention(sdvk_ctx* ctx, const sdvk_attn_desc* desc) {
+    if (!ctx || !desc) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::attention(*desc, env_of(ctx));
+}
+
+int sdvk_fused_attn_supported(uint32_t C, uint32_t heads) {
+    if (!C || !heads || C % heads) return 0;
+    const uint32_t hd = C / heads;
+    return hd > 0 && hd <= 64;
+}
+
+int sdvk_fused_attention(sdvk_ctx* ctx, const void* q, const void* k, const void* v, void* out, uint32_t Tq,
+                         uint32_t Tk, uint32_t C, uint32_t heads, int causal) {
+    if (!ctx) return SDVK_E_ARG;
+    if (!sdvk_fused_attn_supported(C, heads))
+        return set_err(ctx, SDVK_E_SHAPE, "fusedAttention: unsupported C=" + std::to_string(C) +
+                                              " heads=" + std::to_string(heads));
+    const uint32_t hd = C / heads;
+    sdvk_attn_desc d{};
+    d.q = q;
+    d.k = k;
+    d.v = v;
+    d.o = out;
+    d.dtype = SDVK_F32;
+    d.o_dtype = SDVK_F32;
+    d.batch = 1;
+    d.heads = heads;
+    d.Tq = Tq;
+    d.Tk = Tk;
+    d.hd = hd;
+    d.ldq = d.ldk = d.ldv = d.ldo = C;
+    d.hq = d.hk = d.hv = d.ho = hd;
+    d.scale = 1.0f / std::sqrt((float)hd);
+    d.causal = causal;
+    return sdvk_attention(ctx, &d);
+}
+
+int sdvk_check_finite(sdvk_ctx* ctx, const void* x, int dtype, uint64_t n) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    auto env = env_of(ctx);
+    if (int rc = cuda_err(ctx, cudaMemsetAsync(ctx->flag_dev, 0, 4, ctx->stream), "memset")) return rc;
+    if (int rc = sdvk::check_finite(x, dtype, n, ctx->flag_dev, env)) return rc;
+    uint32_t flag = 0;
+    if (int rc = cuda_err(ctx, cudaMemcpyAsync(&flag, ctx->flag_dev, 4, cudaMemcpyDeviceToHost, ctx->stream), "copy"))
+        return rc;
+    if (int rc = cuda_err(ctx, cudaStreamSynchronize(ctx->stream), "sync")) return rc;
+    return flag ? set_err(ctx, SDVK_E_NOT_FINITE, "non-finite value found") : SDVK_OK;
+}
+
+// ------------------------------------------------------------------ name dispatch
+int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint32_t nbufs, const void* push,
+                  uint32_t push_bytes, uint32_t gx, uint32_t gy, uint32_t gz) {
+    (void)gx;
+    (void)gy;
+    if (!ctx || !kernel || !bufs || !push) return SDVK_E_ARG;
+    const std::string name(kernel);
+    const uint32_t batch = gz ? gz : 1;  // the shaders batch over the z workgroup index
+    auto is = [&](std::initializer_list<const char*> names) {
+        for (const char* n : names)
+            if (name == n) return true;
+        return false;
+    };
+    if (is({"gemm_nt_q8", "gemm_nt_q8_v", "gemm_nt_q8_v_bm128", "gemm_nt_q8_v_bk32", "gemm_nt_q8_v_bm128_bk32",
+            "gemm_nt_q8_v_b", "gemm_nt_q8_v_bm128_b"})) {
+        const bool with_bias = name.size() > 2 && name.compare(name.size() - 2, 2, "_b") == 0;
+        if (push_bytes < sizeof(Pg) || nbufs < (with_bias ? 5u : 4u))
+            return set_err(ctx, SDVK_E_ARG, name + ": needs " + (with_bias ? "5" : "4") + " buffers and a 48-byte Pg");
+        Pg pc;
+        std::memcpy(&pc, push, sizeof(pc));
+        const uint64_t lda = pc.lda ? pc.lda : pc.K, ldc = pc.ldc ? pc.ldc : pc.N;
+        // Buffer extents the shape reads/writes (fp32 A/C/S/bias, int8 payload).
+        const uint64_t a_end = ((uint64_t)(batch - 1) * pc.sA + (uint64_t)(pc.M ? pc.M - 1 : 0) * lda + pc.K) * 4;
+        const uint64_t c_end = ((uint64_t)(batch - 1) * pc.sC + (uint64_t)(pc.M ? pc.M - 1 : 0) * ldc + pc.N) * 4;
+        const uint64_t q_end = (uint64_t)pc.N * pc.K, s_end = (uint64_t)pc.N * pc.K / 32 * 4;
+        if (!buf_holds(bufs[0], a_end) || !buf_holds(bufs[1], q_end) || !buf_holds(bufs[2], c_end) ||
+            !buf_holds(bufs[3], s_end) || (with_bias && !buf_holds(bufs[4], (uint64_t)pc.N * 4)))
+            return set_err(ctx, SDVK_E_ARG, name + ": a buffer is smaller than the shape needs");
+        const float* bias = (with_bias && pc.mode == 0) ? static_cast<const float*>(buf_ptr(bufs[4])) : nullptr;
+        return sdvk_gemm_q8_nt(ctx, buf_ptr(bufs[0]), SDVK_F32, static_cast<const int8_t*>(buf_ptr(bufs[1])),
+                               static_cast<const float*>(buf_ptr(bufs[3])), bias, buf_mptr(bufs[2]), SDVK_F32, pc.M,
+                               pc.N, pc.K, (uint32_t)lda, (uint32_t)ldc, batch, pc.sA, pc.sC, pc.mode != 0);
+    }
+    if (is({"gemm_nn_q8", "gemm_nn_q8_v"})) {
+        if (push_bytes < sizeof(Pg) || nbufs < 4u)
+            return set_err(ctx, SDVK_E_ARG, name + ": needs 4 buffers and a 48-byte Pg");
+        Pg pc;
+        std::memcpy(&pc, push, sizeof(pc));
+        const uint64_t lda = pc.lda ? pc.lda : pc.K, ldb = pc.ldb ? pc.ldb : pc.N, ldc = pc.ldc ? pc.ldc : pc.N;
+        const uint64_t q_end = (uint64_t)(batch - 1) * pc.sA + (uint64_t)(pc.M ? pc.M - 1 : 0) * lda + pc.K;
+        const uint64_t b_end = ((uint64_t)(batch - 1) * pc.sB + (uint64_t)(pc.K ? pc.K - 1 : 0) * ldb + pc.N) * 4;
+        const uint64_t c_end = ((uint64_t)(batch - 1) * pc.sC + (uint64_t)(pc.M ? pc.M - 1 : 0) * ldc + pc.N) * 4;
+        if (!buf_holds(bufs[0], q_end) || !buf_holds(bufs[1], b_end) || !buf_holds(bufs[2], c_end) ||
+            !buf_holds(bufs[3], (q_end + 31) / 32 * 4))
+            return set_err(ctx, SDVK_E_ARG, name + ": a buffer is smaller than the shape needs");
+        return sdvk_gemm_q8_nn(ctx, static_cast<const int8_t*>(buf_ptr(bufs[0])),
+                               static_cast<const float*>(buf_ptr(bufs[3])), buf_ptr(bufs[1]), SDVK_F32, nullptr,
+                               buf_mptr(bufs[2]), SDVK_F32, pc.M, pc.N, pc.K, (uint32_t)lda, (uint32_t)ldb,
+                               (uint32_t)ldc, batch, pc.sA, pc.sB, pc.sC, pc.mode != 0);
+    }
+    if (is({"fused_attn", "fused_attn_tiled"})) {
+        if (push_bytes < sizeof(FaPush) || nbufs < 4u)
+            return set_err(ctx, SDVK_E_ARG, name + ": needs 4 buffers and a 36-byte FaPush");
+        FaPush pc;
+        std::memcpy(&pc, push, sizeof(pc));
+        if (!pc.heads || !pc.hd || pc.hd > 64 || (uint64_t)pc.heads * pc.hd > pc.C)
+            return set_err(ctx, SDVK_E_SHAPE, name + ": head layout not supported");
+        const uint64_t q_end = (uint64_t)pc.Tq * pc.C * 4, kv_end = (uint64_t)pc.Tk * pc.C * 4;
+        if (!buf_holds(bufs[0], q_end) || !buf_holds(bufs[1], kv_end) || !buf_holds(bufs[2], kv_end) ||
+            !buf_holds(bufs[3], q_end))
+            return set_err(ctx, SDVK_E_ARG, name + ": a buffer is smaller than the shape needs");
+        sdvk_attn_desc d{};
+        d.q = buf_ptr(bufs[0]);
+        d.k = buf_ptr(bufs[1]);
+        d.v = buf_ptr(bufs[2]);
+        d.o = buf_mptr(bufs[3]);
+        d.dtype = SDVK_F32;
+        d.o_dtype = SDVK_F32;
+        d.batch = 1;
+        d.heads = pc.heads;
+        d.Tq = pc.Tq;
+        d.Tk = pc.Tk;
+        d.hd = pc.hd;
+        d.ldq = d.ldk = d.ldv = d.ldo = pc.C;
+        d.hq = d.hk = d.hv = d.ho = pc.hd;
+        d.scale = pc.scale;
+        d.causal = (int)pc.causal;
+        return sdvk_attention(ctx, &d);
+    }
+    return set_err(ctx, SDVK_E_KERNEL, "unknown kernel " + name);
+}
+
+}  // extern "C"

@@ -1,0 +1,100 @@
+"""The sdvk hot-path calls on torch CUDA tensors.
+
+torch provides device memory and the stream (the context runs on torch's current stream); the
+arithmetic is libsdvk_b200.so's CUDA kernels.  One Context per device is cached.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional
+
+import torch
+
+from . import BF16, F16, F32, AttnDesc, Context
+
+_CTX: Dict[int, Context] = {}
+_DT = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+
+
+def context(device: Optional[torch.device] = None) -> Context:
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index
+    if dev is None:
+        dev = torch.cuda.current_device()
+    ctx = _CTX.get(dev)
+    if ctx is None:
+        ctx = Context(dev)
+        _CTX[dev] = ctx
+    ctx.set_stream(torch.cuda.current_stream(dev).cuda_stream)
+    return ctx
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype not in _DT:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    return _DT[t.dtype]
+
+
+def gemm_q8_nt(a: torch.Tensor, q: torch.Tensor, s: torch.Tensor, bias: Optional[torch.Tensor] = None,
+               out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32,
+               accumulate: bool = False) -> torch.Tensor:
+    """C[..., M, N] = A[..., M, K] . (q[N, K] * s)^T (+ bias).  A is 2-D or 3-D (batch, M, K)."""
+    assert q.dtype == torch.int8 and s.dtype == torch.float32
+    N, K = q.shape
+    a3 = a if a.dim() == 3 else a.unsqueeze(0)
+    B, M, Ka = a3.shape
+    assert Ka == K and a3.stride(2) == 1
+    if out is None:
+        out = torch.empty((B, M, N) if a.dim() == 3 else (M, N), dtype=out_dtype, device=a.device)
+    o3 = out if out.dim() == 3 else out.unsqueeze(0)
+    ctx = context(a.device)
+    ctx.gemm_q8_nt(a3.data_ptr(), _dt(a3), q.data_ptr(), s.data_ptr(), bias.data_ptr() if bias is not None else None,
+                   o3.data_ptr(), _dt(o3), M, N, K, a3.stride(1), o3.stride(1), B, a3.stride(0) if B > 1 else 0,
+                   o3.stride(0) if B > 1 else 0, accumulate)
+    return out
+
+
+def gemm_q8_nn(q: torch.Tensor, s: torch.Tensor, b: torch.Tensor, bias: Optional[torch.Tensor] = None,
+               out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32,
+               accumulate: bool = False) -> torch.Tensor:
+    """C[..., M, N] = (q[M, K] * s) . B[..., K, N] (+ bias[M])."""
+    assert q.dtype == torch.int8 and s.dtype == torch.float32
+    M, K = q.shape
+    b3 = b if b.dim() == 3 else b.unsqueeze(0)
+    Bt, Kb, N = b3.shape
+    assert Kb == K and b3.stride(2) == 1
+    if out is None:
+        out = torch.empty((Bt, M, N) if b.dim() == 3 else (M, N), dtype=out_dtype, device=b.device)
+    o3 = out if out.dim() == 3 else out.unsqueeze(0)
+    ctx = context(b.device)
+    ctx.gemm_q8_nn(q.data_ptr(), s.data_ptr(), b3.data_ptr(), _dt(b3), bias.data_ptr() if bias is not None else None,
+                   o3.data_ptr(), _dt(o3), M, N, K, q.stride(0), b3.stride(1), o3.stride(1), Bt, 0,
+                   b3.stride(0) if Bt > 1 else 0, o3.stride(0) if Bt > 1 else 0, accumulate)
+    return out
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: Optional[float] = None,
+              causal: bool = False, out: Optional[torch.Tensor] = None,
+              out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Fused attention on token-major activations [B, T, heads*hd] (head h at columns h*hd..)."""
+    q3 = q if q.dim() == 3 else q.unsqueeze(0)
+    k3 = k if k.dim() == 3 else k.unsqueeze(0)
+    v3 = v if v.dim() == 3 else v.unsqueeze(0)
+    B, Tq, C = q3.shape
+    Tk = k3.shape[1]
+    hd = C // heads
+    assert C == heads * hd and k3.shape[2] == C and v3.shape[2] == C
+    if out is None:
+        od = out_dtype or (torch.float32 if q.dtype == torch.float32 else torch.float16)
+        out = torch.empty(q.shape, dtype=od, device=q.device)
+    o3 = out if out.dim() == 3 else out.unsqueeze(0)
+    d = AttnDesc()
+    d.q, d.k, d.v, d.o = q3.data_ptr(), k3.data_ptr(), v3.data_ptr(), o3.data_ptr()
+    d.dtype, d.o_dtype = _dt(q3), _dt(o3)
+    d.batch, d.heads, d.Tq, d.Tk, d.hd = B, heads, Tq, Tk, hd
+    d.ldq, d.ldk, d.ldv, d.ldo = q3.stride(1), k3.stride(1), v3.stride(1), o3.stride(1)
+    d.sq, d.sk, d.sv, d.so = q3.stride(0), k3.stride(0), v3.stride(0), o3.stride(0)
+    d.hq = d.hk = d.hv = d.ho = hd
+    d.scale = (1.0 / math.sqrt(hd)) if scale is None else scale
+    d.causal = int(causal)
+    context(q.device).attention(d)
+    return out

@@ -1,0 +1,197 @@
+"""Q8_0 GEMM parity on the B200: the tcgen05 kernels through the C ABI vs the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import sdvk_b200
+from sdvk_b200 import torch_ops
+from tests._gpu_util import check_gemm, dev, host
+
+pytestmark = pytest.mark.gpu
+
+
+def _x(orc, seed, shape, dtype):
+    if dtype == "f16":
+        return orc.normal_f16(seed, 100, shape)
+    x = orc.normal_f32(seed, 100, shape)
+    if dtype == "bf16":
+        return torch.from_numpy(x).bfloat16().float().numpy()  # values the GPU sees
+    return x
+
+
+def _tt(x, dtype):
+    t = dev(x)
+    return t.bfloat16() if dtype == "bf16" else t
+
+
+def _rows(M, n=192, seed=0):
+    return np.sort(np.random.default_rng(seed).choice(M, size=min(M, n), replace=False))
+
+
+NT_CASES = [
+    # (M, N, K, dtype, bias, out)           where in SDXL
+    (9216, 1280, 1280, "f16", False, "f32"),
+    (2048, 1280, 1280, "f16", False, "f32"),  # to_q/k/v, batch-2 tokens at level 2
+    (2048, 10240, 1280, "f16", True, "f16"),  # GEGLU proj
+    (2048, 1280, 5120, "f16", True, "f32"),  # ff.net.2
+    (154, 1280, 2048, "f16", False, "f16"),  # cross-attn K/V from the 77x2048 context, batch 2
+    (8192, 640, 640, "bf16", True, "f32"),  # level 1 projections
+    (9216, 1280, 1280, "f32", False, "f32"),  # fp32 activations (tf32 tensor cores)
+    (100, 100, 96, "f16", True, "f32"),  # ragged tiles in M, N and K
+    (1, 64, 32, "f16", False, "f32"),  # single row, single K block
+    (130, 260, 160, "f32", True, "f16"),
+]
+
+
+@pytest.mark.parametrize("M,N,K,dt,with_bias,out", NT_CASES)
+def test_gemm_nt(orc, cuda_ok, M, N, K, dt, with_bias, out):
+    x = _x(orc, M + N + K, (M, K), dt)
+    q, _, s = orc.q8_weights(7, N, N, K)
+    bias = orc.normal_f32(3, N, (N,), 0.5) if with_bias else None
+    c = torch_ops.gemm_q8_nt(_tt(x, dt), dev(q), dev(s), dev(bias) if with_bias else None,
+                             out_dtype=torch.float32 if out == "f32" else torch.float16)
+    got = host(c).astype(np.float64)
+    rows = _rows(M)
+    ref = orc.gemm_nt_q8_f64(x[rows].astype(np.float32), q, s, bias)
+    check_gemm(orc, f"nt {M}x{N}x{K} {dt}->{out}", got[rows], ref, "f32" if dt == "f32" else dt)
+
+
+def test_gemm_nt_accumulate_and_batch(orc, cuda_ok):
+    B, M, N, K = 3, 300, 384, 640
+    x = orc.normal_f16(1, 2, (B, M, K))
+    q, _, s = orc.q8_weights(2, 0, N, K)
+    bias = orc.normal_f32(4, 0, (N,))
+    c0 = orc.normal_f32(5, 0, (B, M, N))
+    c = dev(c0)
+    torch_ops.gemm_q8_nt(dev(x), dev(q), dev(s), dev(bias), out=c, accumulate=True)
+    ref = c0 + np.stack([orc.gemm_nt_q8_f64(x[b].astype(np.float32), q, s, bias) for b in range(B)])
+    check_gemm(orc, "nt batch3 accumulate+bias", host(c), ref, "f16")
+
+
+def test_gemm_nt_full_size_properties(orc, cuda_ok):
+    """Config 0 at full size: linearity in A and in the bias, and batch = stacked singles (bitwise)."""
+    M, N, K = 9216, 1280, 1280
+    x = dev(orc.normal_f16(0, 0, (M, K)))
+    q, _, s = orc.q8_weights(0, 0, N, K)
+    qd, sd = dev(q), dev(s)
+    c1 = torch_ops.gemm_q8_nt(x, qd, sd)
+    c2 = torch_ops.gemm_q8_nt(-x, qd, sd)
+    assert torch.equal(c1, -c2)  # sign symmetry is exact
+    b = dev(orc.normal_f32(1, 1, (N,)))
+    c3 = torch_ops.gemm_q8_nt(x, qd, sd, b)
+    assert torch.allclose(c3 - b, c1, rtol=0, atol=1e-5 * float(c1.abs().max()))
+    xb = torch.stack([x[:4608], x[4608:]])
+    cb = torch_ops.gemm_q8_nt(xb, qd, sd)
+    assert torch.equal(cb.reshape(M, N), c1)  # same tiles, same order: bit-identical
+    c4 = torch_ops.gemm_q8_nt(x, qd, sd)
+    assert torch.equal(c1, c4)  # deterministic
+
+
+NN_CASES = [
+    # (M=out ch, N=tokens, K=in ch, dtype, out)
+    (1280, 1024, 1280, "f16", "f32"),  # proj_in / proj_out at level 2 (per image)
+    (640, 4096, 640, "f16", "f16"),  # level 1
+    (320, 16384, 2880, "bf16", "f32"),  # a 3x3 conv via im2col at level 0 (K = 320*9)
+    (1280, 1024, 1280, "f32", "f32"),  # fp32 (tf32) as the reference's conv1 feeds it
+    (100, 104, 96, "f16", "f32"),  # ragged
+]
+
+
+@pytest.mark.parametrize("M,N,K,dt,out", NN_CASES)
+def test_gemm_nn(orc, cuda_ok, M, N, K, dt, out):
+    q, _, s = orc.q8_weights(8, M, M, K)
+    b = _x(orc, M * 3 + N, (K, N), dt)
+    c = torch_ops.gemm_q8_nn(dev(q), dev(s), _tt(b, dt), out_dtype=torch.float32 if out == "f32" else torch.float16)
+    got = host(c).astype(np.float64)
+    rows = _rows(M)
+    ref = orc.gemm_nn_q8_f64(q[rows], s.reshape(M, K // 32)[rows].ravel(), b.astype(np.float32))
+    check_gemm(orc, f"nn {M}x{N}x{K} {dt}->{out}", got[rows], ref, "f32" if dt == "f32" else dt)
+
+
+def test_gemm_nn_bias_accumulate(orc, cuda_ok):
+    M, N, K = 320, 512, 320
+    q, _, s = orc.q8_weights(3, 3, M, K)
+    b = orc.normal_f16(3, 3, (K, N))
+    bias = orc.normal_f32(3, 4, (M,))
+    c0 = orc.normal_f32(3, 5, (M, N))
+    c = dev(c0)
+    torch_ops.gemm_q8_nn(dev(q), dev(s), dev(b), dev(bias), out=c, accumulate=True)
+    ref = c0 + orc.gemm_nn_q8_f64(q, s, b.astype(np.float32)) + bias[:, None]
+    check_gemm(orc, "nn accumulate+bias", host(c), ref, "f16")
+
+
+def _bufs(*ts):
+    return [sdvk_b200.Buf(t.data_ptr(), 0, t.numel() * t.element_size()) for t in ts]
+
+
+@pytest.mark.parametrize("kernel", ["gemm_nt_q8", "gemm_nt_q8_v", "gemm_nt_q8_v_bm128", "gemm_nt_q8_v_bk32",
+                                    "gemm_nt_q8_v_bm128_bk32"])
+def test_dispatch_reference_probe(orc, cuda_ok, kernel):
+    """tests/gemm_q8_bench.cpp's correctness probe (100x100x96, mt19937(7), int8 U[-127,127],
+    A = int8/127, scales 0.01) through Engine::dispatch's replacement, fp32 buffers."""
+    M, N, K = 100, 100, 96
+    rng = orc.MT19937(7)
+    A = (rng.uniform_int(M * K, -127, 127).astype(np.float32) / np.float32(127.0)).reshape(M, K)
+    q = rng.uniform_int(N * K, -127, 127).astype(np.int8).reshape(N, K)
+    s = np.full(N * K // 32, 0.01, np.float32)
+    ctx = torch_ops.context()
+    a, qd, sd = dev(A), dev(q), dev(s)
+    c = torch.full((M, N), float("nan"), device="cuda")
+    ctx.dispatch(kernel, _bufs(a, qd, c, sd), sdvk_b200.pack_pg(M, N, K), (N + 63) // 64, (M + 63) // 64, 1)
+    ref = orc.gemm_nt_q8_f64(A, q, s)
+    st = check_gemm(orc, f"dispatch {kernel} probe", host(c), ref, "f32")
+    shader = orc.gemm_nt_q8_shader(A, q, s)  # the reference's own fp32 math
+    assert orc.err_stats(shader, ref)["rel_max"] < 1e-6
+    assert st["rel_max"] < 5e-3
+
+
+def test_dispatch_bias_mode_and_nn(orc, cuda_ok):
+    ctx = torch_ops.context()
+    M, N, K = 256, 192, 320
+    A = orc.normal_f32(9, 0, (M, K))
+    q, _, s = orc.q8_weights(9, 1, N, K)
+    bias = orc.normal_f32(9, 2, (N,))
+    a, qd, sd, bd = dev(A), dev(q), dev(s), dev(bias)
+    c = torch.zeros((M, N), device="cuda")
+    # mode 0 with bias (gemm_nt_q8_v_bm128_b), then mode 1 accumulates without the bias
+    ctx.dispatch("gemm_nt_q8_v_bm128_b", _bufs(a, qd, c, sd, bd), sdvk_b200.pack_pg(M, N, K, mode=0), 3, 2, 1)
+    ctx.dispatch("gemm_nt_q8_v_bm128_b", _bufs(a, qd, c, sd, bd), sdvk_b200.pack_pg(M, N, K, mode=1), 3, 2, 1)
+    ref = 2 * orc.gemm_nt_q8_f64(A, q, s) + bias
+    check_gemm(orc, "dispatch bias mode0+mode1", host(c), ref, "f32")
+    # gemm_nn_q8_v with ldc = P (conv1, sdvkgen.cpp:1183)
+    Mn, P, Kn = 128, 256, 192
+    qn, _, sn = orc.q8_weights(9, 3, Mn, Kn)
+    B = orc.normal_f32(9, 4, (Kn, P))
+    cn = torch.zeros((Mn, P), device="cuda")
+    ctx.dispatch("gemm_nn_q8_v", _bufs(dev(qn), dev(B), cn, dev(sn)), sdvk_b200.pack_pg(Mn, P, Kn, ldc=P), 4, 2, 1)
+    check_gemm(orc, "dispatch nn", host(cn), orc.gemm_nn_q8_f64(qn, sn, B), "f32")
+
+
+def test_shape_errors(orc, cuda_ok):
+    ctx = torch_ops.context()
+    a = torch.zeros((64, 48), device="cuda", dtype=torch.float16)
+    q = torch.zeros((64, 48), device="cuda", dtype=torch.int8)
+    s = torch.zeros((96,), device="cuda")
+    c = torch.zeros((64, 64), device="cuda")
+    with pytest.raises(sdvk_b200.SdvkError) as e:  # K % 32 != 0
+        ctx.gemm_q8_nt(a.data_ptr(), sdvk_b200.F16, q.data_ptr(), s.data_ptr(), None, c.data_ptr(), sdvk_b200.F32,
+                       64, 64, 48)
+    assert e.value.status == sdvk_b200.E_SHAPE
+    with pytest.raises(sdvk_b200.SdvkError) as e:
+        ctx.dispatch("gemm_nt_q8_v_bogus", _bufs(a, q, c, s), sdvk_b200.pack_pg(64, 64, 32), 1)
+    assert e.value.status == sdvk_b200.E_KERNEL
+    with pytest.raises(sdvk_b200.SdvkError) as e:  # buffer too small for the shape
+        ctx.dispatch("gemm_nt_q8_v", _bufs(a, q, c, s), sdvk_b200.pack_pg(640, 64, 32), 1)
+    assert e.value.status == sdvk_b200.E_ARG
+
+
+def test_k_zero_writes_bias(orc, cuda_ok):
+    a = torch.zeros((16, 32), device="cuda", dtype=torch.float16)
+    q = torch.zeros((64, 32), device="cuda", dtype=torch.int8)
+    s = torch.zeros((64,), device="cuda")
+    bias = torch.arange(64, device="cuda", dtype=torch.float32)
+    c = torch.full((16, 64), 7.0, device="cuda")
+    ctx = torch_ops.context()
+    ctx.gemm_q8_nt(a.data_ptr(), sdvk_b200.F16, q.data_ptr(), s.data_ptr(), bias.data_ptr(), c.data_ptr(),
+                   sdvk_b200.F32, 16, 64, 0, 32, 64)
+    assert torch.equal(c, bias.expand(16, 64))
