@@ -458,7 +458,8 @@ __global__ void __launch_bounds__(512, 1)
     }
 
     // ---------------------------------------------------------------- teardown
-    asm volatile("bar.sync 1, 448;" ::: "memory");  // warps 0, 1, 4-15
+    __syncwarp();  // lanes that skipped a single-thread role wait for it here
+    asm volatile("barrier.sync 1, 448;" ::: "memory");  // warps 0, 1, 4-15 (2-3 left early)
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
