@@ -63,8 +63,11 @@ typedef struct sdvk_buf {
 SDVK_API int sdvk_ctx_create(int device, sdvk_ctx** out);
 /* Engine::destroy (vk_engine.hpp:101). */
 SDVK_API int sdvk_ctx_destroy(sdvk_ctx* ctx);
-/* Run subsequent work on a caller-owned cudaStream_t (NULL restores the context's own stream). */
+/* Run subsequent work on a caller-owned cudaStream_t.  NULL is CUDA's legacy default stream, as
+ * cudaStream_t 0 is everywhere (e.g. torch's default stream).  A new context runs on a private
+ * non-blocking stream; sdvk_ctx_reset_stream() returns to it. */
 SDVK_API int sdvk_ctx_set_stream(sdvk_ctx* ctx, void* cuda_stream);
+SDVK_API int sdvk_ctx_reset_stream(sdvk_ctx* ctx);
 SDVK_API void* sdvk_ctx_stream(sdvk_ctx* ctx);
 /* Deadline for every bounded wait inside the kernels (default 2000 ms). */
 SDVK_API int sdvk_ctx_set_timeout_ms(sdvk_ctx* ctx, uint32_t ms);

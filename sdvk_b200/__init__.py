@@ -58,6 +58,7 @@ SIGNATURES = {
     "sdvk_ctx_create": (_I, [_I, ctypes.POINTER(_P)]),
     "sdvk_ctx_destroy": (_I, [_P]),
     "sdvk_ctx_set_stream": (_I, [_P, _P]),
+    "sdvk_ctx_reset_stream": (_I, [_P]),
     "sdvk_ctx_stream": (_P, [_P]),
     "sdvk_ctx_set_timeout_ms": (_I, [_P, _U32]),
     "sdvk_device_report": (_I, [_P, ctypes.c_char_p, ctypes.c_size_t]),
@@ -139,7 +140,12 @@ class Context:
             pass
 
     def set_stream(self, stream_ptr: Optional[int]) -> None:
+        """Queue work on a cudaStream_t (0/None = CUDA's legacy default stream)."""
         self._check(lib().sdvk_ctx_set_stream(self._h, stream_ptr or None), "set_stream")
+
+    def reset_stream(self) -> None:
+        """Return to the context's private non-blocking stream."""
+        self._check(lib().sdvk_ctx_reset_stream(self._h), "reset_stream")
 
     def set_timeout_ms(self, ms: int) -> None:
         self._check(lib().sdvk_ctx_set_timeout_ms(self._h, ms), "set_timeout_ms")

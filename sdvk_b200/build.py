@@ -21,7 +21,7 @@ CSRC = os.path.join(PKG, "csrc")
 OBJDIR = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libsdvk_b200.so")
 SOURCES = ["sdvk_abi.cu", "gemm_q8.cu", "attention.cu"]
-HEADERS = ["ptx.cuh", "gemm_q8.cuh", "attention.cuh", "backend.hpp"]
+HEADERS = ["ptx.cuh", "gemm_q8.cuh", "gemm_q8_2sm.cuh", "attention.cuh", "backend.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

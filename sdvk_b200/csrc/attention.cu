@@ -41,7 +41,7 @@ __global__ void finite_kernel(const T* x, uint64_t n, uint32_t* flag) {
 }  // namespace
 
 int attention(const sdvk_attn_desc& d, const LaunchEnv& env) {
-    if (!d.q || !d.k || !d.v || !d.o) return fail(env, SDVK_E_ARG, "null pointer");
+    if ((d.Tq && (!d.q || !d.o)) || (d.Tk && (!d.k || !d.v))) return fail(env, SDVK_E_ARG, "null pointer");
     if (d.dtype != SDVK_F32 && d.dtype != SDVK_F16 && d.dtype != SDVK_BF16)
         return fail(env, SDVK_E_ARG, "Q/K/V dtype must be F32, F16 or BF16");
     if (d.o_dtype != SDVK_F32 && d.o_dtype != SDVK_F16) return fail(env, SDVK_E_ARG, "O dtype must be F32 or F16");

@@ -3,10 +3,11 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "backend.hpp"
-#include "gemm_q8.cuh"
+#include "gemm_q8_2sm.cuh"
 
 namespace sdvk {
 namespace {
@@ -96,8 +97,11 @@ int launch(const GemmQ8Desc& d, const LaunchEnv& env) {
         rc = make_map(&tmA, tma_type(d.x_dtype), d.x, d.K, d.xrows, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
                       Cfg::kBM, CU_TENSOR_MAP_SWIZZLE_128B, env, "activation");
     } else {
+        // N-major activation; 32-bit elements need the 32-byte-atom swizzle the tensor core reads
+        // for MN-major tf32 operands.
         rc = make_map(&tmA, tma_type(d.x_dtype), d.x, d.xrows, d.K, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
-                      Cfg::kBK, CU_TENSOR_MAP_SWIZZLE_128B, env, "activation");
+                      Cfg::kBK, es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B, env,
+                      "activation");
     }
     if (rc) return rc;
     rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, d.wq, d.K, d.wrows, d.sw ? d.batch : 1, d.ldw, d.sw,
@@ -138,8 +142,72 @@ int launch(const GemmQ8Desc& d, const LaunchEnv& env) {
     return cuda_check(env, cudaGetLastError(), "gemm_q8_tc_kernel launch");
 }
 
+// CTA-pair variant: 256 x 256 tiles on two SMs (cta_group::2).
+template <class TA, bool NN, class TC>
+int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
+    using Cfg = Gemm2Config<TA>;
+    const int es = sizeof(TA), ces = sizeof(TC);
+    CUtensorMap tmA, tmW, tmC;
+    int rc;
+    if (!NN) {
+        rc = make_map(&tmA, tma_type(d.x_dtype), d.x, d.K, d.xrows, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
+                      Cfg::kBM, CU_TENSOR_MAP_SWIZZLE_128B, env, "activation");
+    } else {
+        rc = make_map(&tmA, tma_type(d.x_dtype), d.x, d.xrows, d.K, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
+                      Cfg::kBK, es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B, env,
+                      "activation");
+    }
+    if (rc) return rc;
+    rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, d.wq, d.K, d.wrows, d.sw ? d.batch : 1, d.ldw, d.sw,
+                  Cfg::kBK, Cfg::kBNC, CU_TENSOR_MAP_SWIZZLE_NONE, env, "weight");
+    if (rc) return rc;
+    if (!NN) {
+        rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.wrows, d.xrows, d.batch, d.ldc * ces, d.sc * ces, 32, 32,
+                      ces == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, env, "output");
+    } else {
+        rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.xrows, d.wrows, d.batch, d.ldc * ces, d.sc * ces, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, env, "output");
+    }
+    if (rc) return rc;
+    GemmQ8Params p{};
+    p.wq = d.wq;
+    p.ws = d.ws;
+    p.bias = d.bias;
+    p.xrows = d.xrows;
+    p.wrows = d.wrows;
+    p.K = d.K;
+    p.batch = d.batch;
+    p.ldw = d.ldw;
+    p.sW = d.sw;
+    p.tiles_x = (d.xrows + 2 * Cfg::kBM - 1) / (2 * Cfg::kBM);
+    p.tiles_w = (d.wrows + Cfg::kBNP - 1) / Cfg::kBNP;
+    p.num_tiles = p.tiles_x * p.tiles_w * d.batch;
+    p.k_stages = (d.K + Cfg::kBK - 1) / Cfg::kBK;
+    p.accumulate = d.accumulate ? 1u : 0u;
+    p.err = env.err_dev;
+    p.timeout_ns = env.timeout_ns;
+    auto kern = gemm_q8_tc2_kernel<TA, NN, TC>;
+    if (!set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, env.device))
+        return fail(env, SDVK_E_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
+    const uint32_t clusters = std::min<uint32_t>(p.num_tiles, (uint32_t)env.num_sms / 2);
+    kern<<<2 * clusters, Cfg::kThreads, Cfg::kSmemBytes, env.stream>>>(tmA, tmW, tmC, p);
+    return cuda_check(env, cudaGetLastError(), "gemm_q8_tc2_kernel launch");
+}
+
+// Kernel choice: the CTA-pair kernel when the problem fills at least about half of the SM pairs
+// with 256 x 256 tiles; otherwise single-CTA tiles (128 x 128 or 128 x 256) give more parallelism.
+// SDVK_GEMM_VARIANT=1sm|2sm forces one of them.
+int variant_override() {
+    const char* e = getenv("SDVK_GEMM_VARIANT");
+    return (e && e[0] == '1') ? 1 : (e && e[0] == '2') ? 2 : 0;
+}
+
 template <class TA, bool NN, class TC>
 int launch_bn(const GemmQ8Desc& d, const LaunchEnv& env) {
+    const uint64_t pair_tiles = (uint64_t)((d.xrows + 255) / 256) * ((d.wrows + 255) / 256) * d.batch;
+    const int forced = variant_override();
+    const bool pair = forced == 2 || (forced == 0 && d.wrows > 128 && pair_tiles * 4 >= (uint64_t)env.num_sms);
+    if (pair) return launch_pair<TA, NN, TC>(d, env);
     if (d.wrows <= 128) return launch<TA, 128, NN, TC>(d, env);
     return launch<TA, 256, NN, TC>(d, env);
 }

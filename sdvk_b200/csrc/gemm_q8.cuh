@@ -339,8 +339,12 @@ __global__ void __launch_bounds__(512, 1)
                         uint64_t adesc;
                         if constexpr (!NN)
                             adesc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-                        else  // MN-major: k advances by kUmmaK rows of 128 B; x chunks kBK*128 B apart
+                        else if constexpr (!OperandTraits<TA>::kTf32)
+                            // MN-major: k advances by kUmmaK rows of 128 B; x chunks kBK*128 B apart
                             adesc = smem_desc_sw128(a_addr + kk * Cfg::kUmmaK * 128, Cfg::kBK * 128, 1024);
+                        else  // MN-major tf32 needs 32-byte swizzle atoms: 4-row K groups (512 B)
+                            adesc = smem_desc(a_addr + kk * Cfg::kUmmaK * 128, Cfg::kBK * 128, 512,
+                                              kLayoutSw128Base32);
                         const uint64_t bdesc = smem_desc_sw128(b_addr + kk * 32, 16, 1024);
                         const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
                         if constexpr (OperandTraits<TA>::kTf32) mma_tf32(d_tmem, adesc, bdesc, idesc, accum);
@@ -362,43 +366,61 @@ __global__ void __launch_bounds__(512, 1)
         const int chunk = ct % Cfg::kChunksPerRow;
         const int row0 = ct / Cfg::kChunksPerRow;
         constexpr int kRowStep = Cfg::kConvThreads / Cfg::kChunksPerRow;
+        constexpr int T = Cfg::kTasksPerThread;
         const uint64_t kblocks = p.K / 32;
         const uint64_t ldw_blocks = p.ldw / 32;
-        uint32_t it = 0, bit = 0;
-        for (uint32_t tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const uint32_t my_tiles = (p.num_tiles > blockIdx.x) ? (p.num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+        const uint32_t my_iters = my_tiles * p.k_stages;
+        // Scales for iteration j, loaded two iterations ahead of use so their L2 latency is hidden.
+        auto load_scales = [&](uint32_t j, float (&sc)[T]) {
+#pragma unroll
+            for (int t = 0; t < T; ++t) sc[t] = 0.0f;
+            if (j >= my_iters) return;
             uint32_t z, xt, wt;
-            decode(tile, z, xt, wt);
+            decode(blockIdx.x + (j / p.k_stages) * gridDim.x, z, xt, wt);
+            const uint64_t kb = ((uint64_t)(j % p.k_stages) * Cfg::kBK + (uint64_t)chunk * 16) / 32;
+            if (kb >= kblocks) return;
             const float* ws = p.ws + (p.sW ? (uint64_t)z * (p.sW / 32) : 0);
-            for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it, ++bit) {
-                const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
-                const uint32_t bslot = bit % Cfg::kBStages, bph = (bit / Cfg::kBStages) & 1;
-                // Scales first: their L2 latency overlaps the barrier waits.
-                const uint64_t kb = ((uint64_t)ks * Cfg::kBK + (uint64_t)chunk * 16) / 32;
-                float sc[Cfg::kTasksPerThread];
 #pragma unroll
-                for (int j = 0; j < Cfg::kTasksPerThread; ++j) {
-                    const uint32_t n = wt * BN + row0 + j * kRowStep;
-                    sc[j] = (n < p.wrows && kb < kblocks) ? __ldg(ws + (uint64_t)n * ldw_blocks + kb) : 0.0f;
-                }
-                if (!mbar_wait(&ld_full[slot], ph, p.timeout_ns) ||
-                    !mbar_wait(&b_empty[bslot], bph ^ 1, p.timeout_ns)) {
-                    fail();
-                    break;
-                }
-                const uint8_t* wsrc = sW + slot * Cfg::kWBytes;
-                uint8_t* bdst = sB + bslot * Cfg::kBBytes;
+            for (int t = 0; t < T; ++t) {
+                const uint32_t n = wt * BN + row0 + t * kRowStep;
+                if (n < p.wrows) sc[t] = __ldg(ws + (uint64_t)n * ldw_blocks + kb);
+            }
+        };
+        float sc0[T], sc1[T], sc2[T];
+        load_scales(0, sc0);
+        load_scales(1, sc1);
+        for (uint32_t it = 0; ok && it < my_iters; ++it) {
+            load_scales(it + 2, sc2);
+            const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+            const uint32_t bslot = it % Cfg::kBStages, bph = (it / Cfg::kBStages) & 1;
+            const bool got =
+                mbar_wait(&ld_full[slot], ph, p.timeout_ns) && mbar_wait(&b_empty[bslot], bph ^ 1, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, got)) {  // the warp leaves the loop together
+                fail();
+                break;
+            }
+            const uint8_t* wsrc = sW + slot * Cfg::kWBytes;
+            uint8_t* bdst = sB + bslot * Cfg::kBBytes;
+            uint4 raw[T];
 #pragma unroll
-                for (int j = 0; j < Cfg::kTasksPerThread; ++j) {
-                    const int r = row0 + j * kRowStep;
-                    const uint4 raw = *reinterpret_cast<const uint4*>(wsrc + r * Cfg::kBK + chunk * 16);
-                    dequant16<TA>(raw, sc[j], bdst + r * 128, r, chunk * Cfg::kES);  // 16 elements = kES chunks
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&w_empty[slot]);
-                    mbar_arrive(&b_full[bslot]);
-                }
+            for (int t = 0; t < T; ++t)
+                raw[t] = *reinterpret_cast<const uint4*>(wsrc + (row0 + t * kRowStep) * Cfg::kBK + chunk * 16);
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+                const int r = row0 + t * kRowStep;
+                dequant16<TA>(raw[t], sc0[t], bdst + r * 128, r, chunk * Cfg::kES);  // 16 elements = kES chunks
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&w_empty[slot]);
+                mbar_arrive(&b_full[bslot]);
+            }
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+                sc0[t] = sc1[t];
+                sc1[t] = sc2[t];
             }
         }
     } else if (warp >= 12) {
@@ -410,7 +432,7 @@ __global__ void __launch_bounds__(512, 1)
             uint32_t z, xt, wt;
             decode(tile, z, xt, wt);
             const uint32_t acc = tcount % Cfg::kAcc, aph = (tcount / Cfg::kAcc) & 1;
-            if (!mbar_wait(&acc_full[acc], aph, p.timeout_ns)) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], aph, p.timeout_ns))) {
                 fail();
                 break;
             }

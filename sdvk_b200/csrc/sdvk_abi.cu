@@ -139,7 +139,13 @@ int sdvk_ctx_destroy(sdvk_ctx* ctx) {
 
 int sdvk_ctx_set_stream(sdvk_ctx* ctx, void* s) {
     if (!ctx) return SDVK_E_ARG;
-    ctx->stream = s ? static_cast<cudaStream_t>(s) : ctx->own_stream;
+    ctx->stream = static_cast<cudaStream_t>(s);  // NULL: the legacy default stream
+    return SDVK_OK;
+}
+
+int sdvk_ctx_reset_stream(sdvk_ctx* ctx) {
+    if (!ctx) return SDVK_E_ARG;
+    ctx->stream = ctx->own_stream;
     return SDVK_OK;
 }
 

@@ -39,7 +39,7 @@ NT_CASES = [
     (9216, 1280, 1280, "f32", False, "f32"),  # fp32 activations (tf32 tensor cores)
     (100, 100, 96, "f16", True, "f32"),  # ragged tiles in M, N and K
     (1, 64, 32, "f16", False, "f32"),  # single row, single K block
-    (130, 260, 160, "f32", True, "f16"),
+    (130, 264, 160, "f32", True, "f16"),
 ]
 
 
@@ -54,6 +54,26 @@ def test_gemm_nt(orc, cuda_ok, M, N, K, dt, with_bias, out):
     rows = _rows(M)
     ref = orc.gemm_nt_q8_f64(x[rows].astype(np.float32), q, s, bias)
     check_gemm(orc, f"nt {M}x{N}x{K} {dt}->{out}", got[rows], ref, "f32" if dt == "f32" else dt)
+
+
+@pytest.mark.parametrize("variant", ["1sm", "2sm"])
+@pytest.mark.parametrize("nn", [False, True])
+@pytest.mark.parametrize("dt", ["f16", "f32"])
+def test_gemm_variants(orc, cuda_ok, monkeypatch, variant, nn, dt):
+    """Both kernels (single CTA, CTA pair) on ragged shapes, NT and NN, f16 and tf32."""
+    monkeypatch.setenv("SDVK_GEMM_VARIANT", variant)
+    M, N, K = 600, 520, 480  # tails in every dimension for both tilings
+    q, _, s = orc.q8_weights(4, 4, N, K)
+    bias = orc.normal_f32(4, 5, (N,))
+    if not nn:
+        x = _x(orc, 11, (M, K), dt)
+        c = torch_ops.gemm_q8_nt(_tt(x, dt), dev(q), dev(s), dev(bias))
+        ref = orc.gemm_nt_q8_f64(x.astype(np.float32), q, s, bias)
+    else:
+        b = _x(orc, 12, (K, M), dt)
+        c = torch_ops.gemm_q8_nn(dev(q), dev(s), _tt(b, dt), dev(bias))
+        ref = orc.gemm_nn_q8_f64(q, s, b.astype(np.float32)) + bias[:, None]
+    check_gemm(orc, f"variant {variant} {'nn' if nn else 'nt'} {dt}", host(c), ref, dt)
 
 
 def test_gemm_nt_accumulate_and_batch(orc, cuda_ok):
@@ -176,6 +196,11 @@ def test_shape_errors(orc, cuda_ok):
     with pytest.raises(sdvk_b200.SdvkError) as e:  # K % 32 != 0
         ctx.gemm_q8_nt(a.data_ptr(), sdvk_b200.F16, q.data_ptr(), s.data_ptr(), None, c.data_ptr(), sdvk_b200.F32,
                        64, 64, 48)
+    assert e.value.status == sdvk_b200.E_SHAPE
+    c16 = torch.zeros((64, 66), device="cuda", dtype=torch.float16)
+    with pytest.raises(sdvk_b200.SdvkError) as e:  # fp16 output rows of 132 bytes: not 16-byte multiples
+        ctx.gemm_q8_nt(a.data_ptr(), sdvk_b200.F16, q.data_ptr(), s.data_ptr(), None, c16.data_ptr(), sdvk_b200.F16,
+                       64, 66, 32, 48, 66)
     assert e.value.status == sdvk_b200.E_SHAPE
     with pytest.raises(sdvk_b200.SdvkError) as e:
         ctx.dispatch("gemm_nt_q8_v_bogus", _bufs(a, q, c, s), sdvk_b200.pack_pg(64, 64, 32), 1)
