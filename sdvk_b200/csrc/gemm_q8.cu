@@ -133,6 +133,9 @@ int launch(const GemmQ8Desc& d, const LaunchEnv& env) {
     p.accumulate = d.accumulate ? 1u : 0u;
     p.err = env.err_dev;
     p.timeout_ns = env.timeout_ns;
+    p.c = d.c;
+    p.ldc = d.ldc;
+    p.sc = d.sc;
 
     auto kern = gemm_q8_tc_kernel<TA, BN, NN, TC>;
     if (!set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, env.device))
@@ -142,10 +145,15 @@ int launch(const GemmQ8Desc& d, const LaunchEnv& env) {
     return cuda_check(env, cudaGetLastError(), "gemm_q8_tc_kernel launch");
 }
 
-// CTA-pair variant: 256 x 256 tiles on two SMs (cta_group::2).
-template <class TA, bool NN, class TC>
+bool pdl_enabled() {
+    const char* e = getenv("SDVK_PDL");
+    return !(e && e[0] == '0');
+}
+
+// CTA-pair variant: 256 x BNP tiles on two SMs (cta_group::2).
+template <class TA, int BNP, bool NN, class TC>
 int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
-    using Cfg = Gemm2Config<TA>;
+    using Cfg = Gemm2Config<TA, BNP>;
     const int es = sizeof(TA), ces = sizeof(TC);
     CUtensorMap tmA, tmW, tmC;
     int rc;
@@ -186,12 +194,45 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     p.accumulate = d.accumulate ? 1u : 0u;
     p.err = env.err_dev;
     p.timeout_ns = env.timeout_ns;
-    auto kern = gemm_q8_tc2_kernel<TA, NN, TC>;
+    p.c = d.c;
+    p.ldc = d.ldc;
+    p.sc = d.sc;
+    auto kern = gemm_q8_tc2_kernel<TA, BNP, NN, TC>;
     if (!set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, env.device))
         return fail(env, SDVK_E_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
     const uint32_t clusters = std::min<uint32_t>(p.num_tiles, (uint32_t)env.num_sms / 2);
-    kern<<<2 * clusters, Cfg::kThreads, Cfg::kSmemBytes, env.stream>>>(tmA, tmW, tmC, p);
-    return cuda_check(env, cudaGetLastError(), "gemm_q8_tc2_kernel launch");
+    // Programmatic stream serialisation: this grid's prologue may overlap the previous kernel's
+    // tail; the kernel waits (griddepcontrol.wait) before its first global access.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = env.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_check(env, cudaLaunchKernelEx(&cfg, kern, tmA, tmW, tmC, p), "gemm_q8_tc2_kernel launch");
+}
+
+// Pair-tile width (tensor-core N): the candidate minimising waves x per-tile cost, where a tile
+// costs its N plus a fixed share (activation traffic and per-tile overheads do not shrink with N).
+int pick_pair_bn(const GemmQ8Desc& d, int num_sms) {
+    const int clusters = num_sms / 2;
+    const uint64_t xt = (d.xrows + 255) / 256;
+    int best = 256;
+    uint64_t best_cost = ~0ull;
+    for (int bn : {256, 160, 128}) {
+        const uint64_t tiles = xt * ((d.wrows + bn - 1) / bn) * d.batch;
+        const uint64_t waves = (tiles + clusters - 1) / clusters;
+        const uint64_t cost = waves * (uint64_t)(bn + 256);  // measured: the fixed per-tile share ~ N=256
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
 }
 
 // Kernel choice: the CTA-pair kernel when the problem fills at least about half of the SM pairs
@@ -207,7 +248,13 @@ int launch_bn(const GemmQ8Desc& d, const LaunchEnv& env) {
     const uint64_t pair_tiles = (uint64_t)((d.xrows + 255) / 256) * ((d.wrows + 255) / 256) * d.batch;
     const int forced = variant_override();
     const bool pair = forced == 2 || (forced == 0 && d.wrows > 128 && pair_tiles * 4 >= (uint64_t)env.num_sms);
-    if (pair) return launch_pair<TA, NN, TC>(d, env);
+    if (pair) {
+        const char* e = getenv("SDVK_GEMM_PAIR_BN");
+        const int bn = e ? atoi(e) : pick_pair_bn(d, env.num_sms);
+        if (bn == 160) return launch_pair<TA, 160, NN, TC>(d, env);
+        if (bn == 128) return launch_pair<TA, 128, NN, TC>(d, env);
+        return launch_pair<TA, 256, NN, TC>(d, env);
+    }
     if (d.wrows <= 128) return launch<TA, 128, NN, TC>(d, env);
     return launch<TA, 256, NN, TC>(d, env);
 }

@@ -8,12 +8,13 @@
 // accumulator is D[x][w]; the NN epilogue stores it transposed.
 //
 // Per CTA (persistent, one per SM, 16 warps):
-//   warp 0      TMA producer: activation tile (128 x 128B, 128B-swizzled) + raw int8 weight tile
+//   warp 0      activation TMA producer (128 x 128B tiles, 128B-swizzled)
 //   warp 1      TMEM allocator and the single MMA-issuing thread
+//   warp 2      raw int8 weight TMA producer (its own ring, so weights stream ahead of the MMA)
 //   warps 4-11  dequantisers: int8 smem tile * per-32-block scale -> f16/bf16/f32 operand tile in
 //               the 128B-swizzled K-major layout the tensor core reads
 //   warps 12-15 epilogue: TMEM -> registers (+bias) -> swizzled smem -> TMA store / TMA reduce-add
-// Rings: 4 activation/raw-weight stages, 2 dequantised-weight stages, 2 TMEM accumulators, so
+// Rings: 4 activation stages, 4 raw-weight stages, 2 dequantised-weight stages, 2 TMEM accumulators, so
 // loads, dequantisation, MMA and the previous tile's epilogue all overlap.
 //
 // Every mbarrier wait is bounded (GemmQ8Params::timeout_ns): a wait that runs out records
@@ -38,6 +39,8 @@ struct GemmQ8Params {
     uint32_t accumulate;    // 0: C = result, 1: C += result (TMA reduce-add)
     uint32_t* err;          // device error word
     uint64_t timeout_ns;
+    void* c;                // output (direct-store epilogue): NT C[z][x][w], NN C[z][w][x]
+    uint64_t ldc, sc;       // output row and batch strides (elements)
 };
 
 template <class TA>
@@ -77,7 +80,7 @@ struct GemmQ8Config {
     static constexpr int kOffW = kOffB + kBStages * kBBytes;
     static constexpr int kOffEpi = kOffW + kStages * kWBytes;
     static constexpr int kOffBar = kOffEpi + kEpiBytes;
-    static constexpr int kNumBars = 3 * kStages + 2 * kBStages + 2 * kAcc + 1;
+    static constexpr int kNumBars = 4 * kStages + 2 * kBStages + 2 * kAcc + 1;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // +1024: manual alignment
     static constexpr int kThreads = 512;
     static constexpr int kConvThreads = 256;
@@ -166,6 +169,136 @@ __device__ __forceinline__ void dequant16<float>(const uint4 raw, float scale, u
     }
 }
 
+// Walks a CTA's (tile, k-stage) sequence in order and fetches, for each stage, what a
+// dequantising thread needs: for T weight rows (row0 + t*row_step of the tile's weight window),
+// the scale of the 32-block holding K column k_off of the stage and, optionally, the 16 int8 at
+// that column.  One tile decode per tile, no division per stage.
+template <int T>
+struct WeightCursor {
+    const GemmQ8Params* p;
+    uint32_t tile, tile_step, ks;
+    uint32_t n0;          // first weight row of this thread in the current tile
+    const float* ws;      // scale base of the current tile's batch
+    const int8_t* wq;     // payload base of the current tile's batch
+    bool valid;
+    int row_step, bk, k_off, rows_per_tile;
+    uint32_t tiles_x;
+    uint32_t w_window;
+    int row0, rows_mine;  // this thread's first row within the CTA's window, and the window size
+
+    __device__ void set_tile() {
+        valid = tile < p->num_tiles;
+        if (!valid) return;
+        const uint32_t wt = tile % p->tiles_w;
+        const uint32_t rest = tile / p->tiles_w;
+        const uint32_t z = rest / tiles_x;
+        n0 = wt * rows_per_tile + w_window;
+        ws = p->ws + (p->sW ? (uint64_t)z * (p->sW / 32) : 0);
+        wq = p->wq + (p->sW ? (uint64_t)z * p->sW : 0);
+        ks = 0;
+    }
+    __device__ void init(const GemmQ8Params* params, uint32_t first_tile, uint32_t step, int row0_, int rstep, int bk_,
+                         int koff, int rows_tile, uint32_t window, int rows_window) {
+        p = params;
+        row0 = row0_;
+        rows_mine = rows_window;
+        tile = first_tile;
+        tile_step = step;
+        row_step = rstep;
+        bk = bk_;
+        k_off = koff;
+        rows_per_tile = rows_tile;
+        tiles_x = params->tiles_x;
+        w_window = window + row0_;
+        set_tile();
+    }
+    template <bool kWithRaw>
+    __device__ void load(float (&sc)[T], uint4 (&raw)[T]) const {
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            sc[t] = 0.0f;
+            if (kWithRaw) raw[t] = make_uint4(0, 0, 0, 0);
+        }
+        if (!valid) return;
+        const uint32_t k = ks * bk + k_off;
+        if (k >= p->K) return;  // K is a multiple of 32: a 16-column chunk is wholly in or out
+        const uint32_t kb = k >> 5;
+        const uint64_t ldb = p->ldw >> 5;
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            const uint32_t n = n0 + t * row_step;
+            if (n < p->wrows && row0 + t * row_step < rows_mine) {
+                sc[t] = __ldg(ws + (uint64_t)n * ldb + kb);
+                if (kWithRaw) raw[t] = __ldg(reinterpret_cast<const uint4*>(wq + (uint64_t)n * p->ldw + k));
+            }
+        }
+    }
+    __device__ void advance() {
+        if (!valid) return;
+        if (++ks == p->k_stages) {
+            tile += tile_step;
+            set_tile();
+        }
+    }
+};
+
+// Direct epilogue store of one 32-column accumulator block: this thread holds activation row x
+// and weight columns w0..w0+31 in v.  NT writes C[z][x][w] (128 contiguous bytes per thread, fp32);
+// NN writes C[z][w][x] (consecutive lanes hold consecutive x, so every store is coalesced).
+template <class TC, bool NN>
+__device__ __forceinline__ void store_direct(const GemmQ8Params& p, uint32_t z, uint32_t x, uint32_t w0,
+                                             const float (&v)[32]) {
+    if (x >= p.xrows) return;
+    TC* C = reinterpret_cast<TC*>(p.c) + (uint64_t)z * p.sc;
+    if constexpr (NN) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (w0 + j < p.wrows) {
+                TC* dst = C + (uint64_t)(w0 + j) * p.ldc + x;
+                if constexpr (sizeof(TC) == 4) *dst = p.accumulate ? *dst + v[j] : v[j];
+                else *dst = __float2half_rn(v[j]);
+            }
+        }
+    } else {
+        TC* row = C + (uint64_t)x * p.ldc + w0;
+        if constexpr (sizeof(TC) == 4) {
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+                float4 o = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+                if (w0 + 4 * c4 + 3 < p.wrows) {
+                    float4* dst = reinterpret_cast<float4*>(row + 4 * c4);
+                    if (p.accumulate) {
+                        const float4 old = *dst;
+                        o.x += old.x, o.y += old.y, o.z += old.z, o.w += old.w;
+                    }
+                    *dst = o;
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (w0 + 4 * c4 + e < p.wrows) row[4 * c4 + e] = p.accumulate ? row[4 * c4 + e] + v[4 * c4 + e] : v[4 * c4 + e];
+                }
+            }
+        } else {
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+                if (w0 + 8 * c8 + 7 < p.wrows) {
+                    __half2 h0 = __floats2half2_rn(v[8 * c8 + 0], v[8 * c8 + 1]);
+                    __half2 h1 = __floats2half2_rn(v[8 * c8 + 2], v[8 * c8 + 3]);
+                    __half2 h2 = __floats2half2_rn(v[8 * c8 + 4], v[8 * c8 + 5]);
+                    __half2 h3 = __floats2half2_rn(v[8 * c8 + 6], v[8 * c8 + 7]);
+                    *reinterpret_cast<uint4*>(row + 8 * c8) =
+                        make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                                   *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        if (w0 + 8 * c8 + e < p.wrows) row[8 * c8 + e] = __float2half_rn(v[8 * c8 + e]);
+                }
+            }
+        }
+    }
+}
+
 template <class TC>
 __device__ __forceinline__ void store_epi_row(uint8_t* buf, int lane, const float (&v)[32]);
 
@@ -216,9 +349,10 @@ __global__ void __launch_bounds__(512, 1)
     uint8_t* sW = smem + Cfg::kOffW;
     uint8_t* sEpi = smem + Cfg::kOffEpi;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
-    uint64_t* ld_full = bars;                                // [kStages] TMA tx (activation + raw weight)
-    uint64_t* a_empty = ld_full + Cfg::kStages;              // [kStages] MMA commit
-    uint64_t* w_empty = a_empty + Cfg::kStages;              // [kStages] 8 dequant warps
+    uint64_t* a_full = bars;                                 // [kStages] activation TMA tx
+    uint64_t* a_empty = a_full + Cfg::kStages;               // [kStages] MMA commit
+    uint64_t* w_full = a_empty + Cfg::kStages;               // [kStages] raw weight TMA tx
+    uint64_t* w_empty = w_full + Cfg::kStages;               // [kStages] 8 dequant warps
     uint64_t* b_full = w_empty + Cfg::kStages;               // [kBStages] 8 dequant warps
     uint64_t* b_empty = b_full + Cfg::kBStages;              // [kBStages] MMA commit
     uint64_t* acc_full = b_empty + Cfg::kBStages;            // [kAcc] MMA commit
@@ -231,8 +365,9 @@ __global__ void __launch_bounds__(512, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < Cfg::kStages; ++i) {
-            mbar_init(&ld_full[i], 1);
+            mbar_init(&a_full[i], 1);
             mbar_init(&a_empty[i], 1);
+            mbar_init(&w_full[i], 1);
             mbar_init(&w_empty[i], 8);
         }
         for (int i = 0; i < Cfg::kBStages; ++i) {
@@ -260,7 +395,7 @@ __global__ void __launch_bounds__(512, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 2 || warp == 3) return;  // spare warps take no part in the pipeline
+    if (warp == 3) return;  // spare warp takes no part in the pipeline
 
     bool ok = true;
     auto fail = [&]() {
@@ -275,7 +410,36 @@ __global__ void __launch_bounds__(512, 1)
     };
 
     if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
+        // ------------------------------------------------------------ activation TMA producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (uint32_t tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+                uint32_t z, xt, wt;
+                decode(tile, z, xt, wt);
+                for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
+                    const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
+                    if (!mbar_wait(&a_empty[slot], ph ^ 1, p.timeout_ns)) {
+                        fail();
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&a_full[slot], Cfg::kABytes);
+                    const int k0 = (int)(ks * Cfg::kBK);
+                    uint8_t* a_dst = sA + slot * Cfg::kABytes;
+                    if constexpr (!NN) {
+                        tma_load_3d(a_dst, &tmA, &a_full[slot], k0, (int)(xt * Cfg::kBM), (int)z);
+                    } else {
+                        // N-major activation: kBM/kBK boxes of [kBK k-rows][kBK x-elements].
+#pragma unroll
+                        for (int j = 0; j < Cfg::kBM / Cfg::kBK; ++j)
+                            tma_load_3d(a_dst + j * Cfg::kBK * 128, &tmA, &a_full[slot],
+                                        (int)(xt * Cfg::kBM) + j * Cfg::kBK, k0, (int)z);
+                    }
+                }
+            }
+            // The activation loads are drained by the MMA (it waits for every one it consumes).
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ weight TMA producer
         if (lane == 0) {
             uint32_t it = 0;
             for (uint32_t tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
@@ -284,30 +448,18 @@ __global__ void __launch_bounds__(512, 1)
                 const int zw = p.sW ? (int)z : 0;
                 for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
                     const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
-                    if (!mbar_wait(&a_empty[slot], ph ^ 1, p.timeout_ns) ||
-                        !mbar_wait(&w_empty[slot], ph ^ 1, p.timeout_ns)) {
+                    if (!mbar_wait(&w_empty[slot], ph ^ 1, p.timeout_ns)) {
                         fail();
                         break;
                     }
-                    mbar_arrive_expect_tx(&ld_full[slot], Cfg::kABytes + Cfg::kWBytes);
-                    const int k0 = (int)(ks * Cfg::kBK);
-                    uint8_t* a_dst = sA + slot * Cfg::kABytes;
-                    if constexpr (!NN) {
-                        tma_load_3d(a_dst, &tmA, &ld_full[slot], k0, (int)(xt * Cfg::kBM), (int)z);
-                    } else {
-                        // N-major activation: kBM/kBK boxes of [kBK k-rows][kBK x-elements].
-#pragma unroll
-                        for (int j = 0; j < Cfg::kBM / Cfg::kBK; ++j)
-                            tma_load_3d(a_dst + j * Cfg::kBK * 128, &tmA, &ld_full[slot],
-                                        (int)(xt * Cfg::kBM) + j * Cfg::kBK, k0, (int)z);
-                    }
-                    tma_load_3d(sW + slot * Cfg::kWBytes, &tmW, &ld_full[slot], k0, (int)(wt * BN), zw);
+                    mbar_arrive_expect_tx(&w_full[slot], Cfg::kWBytes);
+                    tma_load_3d(sW + slot * Cfg::kWBytes, &tmW, &w_full[slot], (int)(ks * Cfg::kBK), (int)(wt * BN),
+                                zw);
                 }
             }
-            // Drain: make sure no load this CTA issued is still landing in shared memory.
-            const uint32_t issued = it;
-            for (uint32_t i = (issued > Cfg::kStages ? issued - Cfg::kStages : 0); i < issued; ++i)
-                if (!mbar_wait(&ld_full[i % Cfg::kStages], (i / Cfg::kStages) & 1, p.timeout_ns)) fail();
+            // Drain: no raw-weight load may still be landing in shared memory at exit.
+            for (uint32_t i = (it > Cfg::kStages ? it - Cfg::kStages : 0); i < it; ++i)
+                if (!mbar_wait(&w_full[i % Cfg::kStages], (i / Cfg::kStages) & 1, p.timeout_ns)) fail();
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -326,7 +478,7 @@ __global__ void __launch_bounds__(512, 1)
                 for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it, ++bit) {
                     const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
                     const uint32_t bslot = bit % Cfg::kBStages, bph = (bit / Cfg::kBStages) & 1;
-                    if (!mbar_wait(&ld_full[slot], ph, p.timeout_ns) ||
+                    if (!mbar_wait(&a_full[slot], ph, p.timeout_ns) ||
                         !mbar_wait(&b_full[bslot], bph, p.timeout_ns)) {
                         fail();
                         break;
@@ -367,35 +519,24 @@ __global__ void __launch_bounds__(512, 1)
         const int row0 = ct / Cfg::kChunksPerRow;
         constexpr int kRowStep = Cfg::kConvThreads / Cfg::kChunksPerRow;
         constexpr int T = Cfg::kTasksPerThread;
-        const uint64_t kblocks = p.K / 32;
-        const uint64_t ldw_blocks = p.ldw / 32;
         const uint32_t my_tiles = (p.num_tiles > blockIdx.x) ? (p.num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
         const uint32_t my_iters = my_tiles * p.k_stages;
-        // Scales for iteration j, loaded two iterations ahead of use so their L2 latency is hidden.
-        auto load_scales = [&](uint32_t j, float (&sc)[T]) {
-#pragma unroll
-            for (int t = 0; t < T; ++t) sc[t] = 0.0f;
-            if (j >= my_iters) return;
-            uint32_t z, xt, wt;
-            decode(blockIdx.x + (j / p.k_stages) * gridDim.x, z, xt, wt);
-            const uint64_t kb = ((uint64_t)(j % p.k_stages) * Cfg::kBK + (uint64_t)chunk * 16) / 32;
-            if (kb >= kblocks) return;
-            const float* ws = p.ws + (p.sW ? (uint64_t)z * (p.sW / 32) : 0);
-#pragma unroll
-            for (int t = 0; t < T; ++t) {
-                const uint32_t n = wt * BN + row0 + t * kRowStep;
-                if (n < p.wrows) sc[t] = __ldg(ws + (uint64_t)n * ldw_blocks + kb);
-            }
-        };
+        // Scales are loaded two stages ahead of use so their L2 latency is hidden.
+        WeightCursor<T> cur;
+        cur.init(&p, blockIdx.x, gridDim.x, row0, kRowStep, Cfg::kBK, chunk * 16, BN, 0, BN);
         float sc0[T], sc1[T], sc2[T];
-        load_scales(0, sc0);
-        load_scales(1, sc1);
+        uint4 unused[T];
+        cur.load<false>(sc0, unused);
+        cur.advance();
+        cur.load<false>(sc1, unused);
+        cur.advance();
         for (uint32_t it = 0; ok && it < my_iters; ++it) {
-            load_scales(it + 2, sc2);
+            cur.load<false>(sc2, unused);
+            cur.advance();
             const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
             const uint32_t bslot = it % Cfg::kBStages, bph = (it / Cfg::kBStages) & 1;
             const bool got =
-                mbar_wait(&ld_full[slot], ph, p.timeout_ns) && mbar_wait(&b_empty[bslot], bph ^ 1, p.timeout_ns);
+                mbar_wait(&w_full[slot], ph, p.timeout_ns) && mbar_wait(&b_empty[bslot], bph ^ 1, p.timeout_ns);
             if (!__all_sync(0xffffffffu, got)) {  // the warp leaves the loop together
                 fail();
                 break;
@@ -481,7 +622,7 @@ __global__ void __launch_bounds__(512, 1)
 
     // ---------------------------------------------------------------- teardown
     __syncwarp();  // lanes that skipped a single-thread role wait for it here
-    asm volatile("barrier.sync 1, 448;" ::: "memory");  // warps 0, 1, 4-15 (2-3 left early)
+    asm volatile("barrier.sync 1, 480;" ::: "memory");  // warps 0-2, 4-15 (3 left early)
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();

@@ -1,75 +1,77 @@
 // gemm_q8_2sm.cuh -- the Q8_0 GEMM on CTA pairs (tcgen05 cta_group::2).
 //
-// A cluster of two CTAs on one TPC computes a 256 (x rows) x 256 (w rows) tile with one
+// A cluster of two CTAs on one TPC computes a 256 (x rows) x BNP (w rows) tile with one
 // tcgen05.mma.cta_group::2 per 16-element K step, issued by the even CTA.  Each CTA stages its own
-// 128 activation rows and dequantises only its own 128 weight rows, so per SM the dequantisation
+// 128 activation rows and dequantises only its own BNP/2 weight rows, so per SM the dequantisation
 // work and the weight traffic are half of the single-CTA kernel's for the same tensor-core work.
 // The accumulator rows each CTA owns land in its own TMEM; each CTA runs its own epilogue.
 //
-// Cross-CTA signalling (all waits bounded, see GemmQ8Params::timeout_ns):
-//   a_full   (even CTA)  both CTAs' activation TMA loads complete_tx here (cta_group::2 TMA)
-//   b_full   (even CTA)  the 16 dequant warps of both CTAs arrive here
-//   acc_empty(even CTA)  the 8 epilogue warps of both CTAs arrive here
-//   a_empty, b_empty, acc_full (each CTA)  the MMA commit multicasts to both CTAs
-//   w_full, w_empty (each CTA)  the local raw-weight ring
+// The tensor pipe idles whenever the issuing thread polls a barrier that is not yet complete, so
+// its per-stage control path is one CTA-scope poll of one barrier and one commit:
+//   full[s]   (even CTA)  activation TMA bytes of both CTAs (cta_group::2 TMA) + the 16
+//                         dequantiser warps of both CTAs; the even CTA's producer sets the tx count
+//   empty[s]  (each CTA)  one MMA commit multicast to both CTAs frees activation and operand slot s
+//   acc_full  (each CTA)  MMA commit multicast;  acc_empty (even CTA): the 8 epilogue warps
+//   w_full, w_empty (each CTA)  the local raw int8 weight ring (TMA -> dequantisers)
+// Warp roles per CTA: 0 activation TMA, 1 TMEM + MMA (even CTA issues), 2 weight TMA,
+// 4-11 dequantisers, 12-15 epilogue (3 idle).
+//
+// Every wait is bounded (GemmQ8Params::timeout_ns): a wait that runs out records kErrTimeout, the
+// CTA drains what it issued, both CTAs meet at the final cluster barrier and free TMEM.
 #pragma once
 
 #include "gemm_q8.cuh"
 
 namespace sdvk {
 
-template <class TA>
+template <class TA, int BNP>
 struct Gemm2Config {
-    static constexpr int kBM = 128;      // activation rows per CTA (pair: 256)
-    static constexpr int kBNP = 256;     // weight rows per pair tile
-    static constexpr int kBNC = 128;     // weight rows dequantised by each CTA
+    static constexpr int kBM = 128;       // activation rows per CTA (pair: 256)
+    static constexpr int kBNP = BNP;      // weight rows per pair tile (tensor-core N)
+    static constexpr int kBNC = BNP / 2;  // weight rows dequantised by each CTA
     static constexpr int kES = sizeof(TA);
     static constexpr int kBK = 128 / kES;
     static constexpr int kUmmaK = 32 / kES;
-    static constexpr int kSA = 5;        // activation stages
-    static constexpr int kSW = 4;        // raw int8 weight stages
-    static constexpr int kSB = 4;        // dequantised weight stages
+    static constexpr int kS = 5;          // stages of (activation tile, dequantised weight tile)
+    static constexpr int kSW = 4;         // raw int8 weight stages
     static constexpr int kAcc = 2;
     static constexpr int kABytes = kBM * 128;
-    static constexpr int kWBytes = kBNC * kBK;
     static constexpr int kBBytes = kBNC * 128;
-    static constexpr int kEpiBytes = 4 * 2 * 4096;
+    static constexpr int kStageBytes = kABytes + ((kBBytes + 1023) / 1024) * 1024;
+    static constexpr int kWBytes = kBNC * kBK;
+    static constexpr int kEpiBytes = 4 * 2 * 4096;  // 4 epilogue warps x 2 buffers x 32x32 fp32
     static constexpr uint32_t kTmemCols = 512;
-    static constexpr int kOffA = 0;
-    static constexpr int kOffB = kOffA + kSA * kABytes;
-    static constexpr int kOffW = kOffB + kSB * kBBytes;
-    static constexpr int kOffEpi = kOffW + kSW * kWBytes;
+    static constexpr int kOffStage = 0;
+    static constexpr int kOffW = kOffStage + kS * kStageBytes;
+    static constexpr int kOffEpi = kOffW + ((kSW * kWBytes + 1023) / 1024) * 1024;
     static constexpr int kOffBar = kOffEpi + kEpiBytes;
-    static constexpr int kNumBars = 2 * kSA + 2 * kSW + 2 * kSB + 2 * kAcc + 1;
+    static constexpr int kNumBars = 2 * kS + 2 * kSW + 2 * kAcc + 1;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
     static constexpr int kThreads = 512;
     static constexpr int kConvThreads = 256;
     static constexpr int kChunksPerRow = kBK / 16;
-    static constexpr int kTasksPerThread = kBNC * kChunksPerRow / kConvThreads;
+    static constexpr int kTasksPerThread = (kBNC * kChunksPerRow + kConvThreads - 1) / kConvThreads;
     static constexpr int kRowStep = kConvThreads / kChunksPerRow;
     static_assert(kSmemBytes <= 232448, "shared memory");
-    static_assert(kTasksPerThread >= 1 && (kBNC * kChunksPerRow) % kConvThreads == 0, "dequant split");
+    static_assert(BNP % 32 == 0 && BNP >= 128 && BNP <= 256, "pair tile N");
 };
 
-template <class TA, bool NN, class TC>
+template <class TA, int BNP, bool NN, class TC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     gemm_q8_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmC, const GemmQ8Params p) {
-    using Cfg = Gemm2Config<TA>;
+    using Cfg = Gemm2Config<TA, BNP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem + Cfg::kOffA;
-    uint8_t* sB = smem + Cfg::kOffB;
+    uint8_t* sStage = smem + Cfg::kOffStage;  // stage s: activation tile, then dequantised weights
     uint8_t* sW = smem + Cfg::kOffW;
     uint8_t* sEpi = smem + Cfg::kOffEpi;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
-    uint64_t* a_full = bars;
-    uint64_t* a_empty = a_full + Cfg::kSA;
-    uint64_t* w_full = a_empty + Cfg::kSA;
+    uint64_t* full = bars;
+    uint64_t* empty = full + Cfg::kS;
+    uint64_t* w_full = empty + Cfg::kS;
     uint64_t* w_empty = w_full + Cfg::kSW;
-    uint64_t* b_full = w_empty + Cfg::kSW;
-    uint64_t* b_empty = b_full + Cfg::kSB;
-    uint64_t* acc_full = b_empty + Cfg::kSB;
+    uint64_t* acc_full = w_empty + Cfg::kSW;
     uint64_t* acc_empty = acc_full + Cfg::kAcc;
     uint64_t* mma_done = acc_empty + Cfg::kAcc;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -81,17 +83,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     const uint32_t cid = cluster_id_x(), ncl = nclusters_x();
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < Cfg::kSA; ++i) {
-            mbar_init(&a_full[i], 1);
-            mbar_init(&a_empty[i], 1);
+        for (int i = 0; i < Cfg::kS; ++i) {
+            mbar_init(&full[i], 1 + 16);  // producer's expect_tx + 16 dequantiser warps
+            mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < Cfg::kSW; ++i) {
             mbar_init(&w_full[i], 1);
             mbar_init(&w_empty[i], 8);
-        }
-        for (int i = 0; i < Cfg::kSB; ++i) {
-            mbar_init(&b_full[i], 16);
-            mbar_init(&b_empty[i], 1);
         }
         for (int i = 0; i < Cfg::kAcc; ++i) {
             mbar_init(&acc_full[i], 1);
@@ -114,13 +112,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything above overlaps the previous kernel's tail; global memory is touched only after it.
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     bool ok = true;
     auto fail = [&]() {
         atomicOr(p.err, kErrTimeout);
         ok = false;
     };
-    // Pair tiles: tiles_x counts 256-row pair tiles here.
+    // Pair tiles: tiles_x counts 256-row pair tiles.
     auto decode = [&](uint32_t tile, uint32_t& z, uint32_t& xt, uint32_t& wt) {
         wt = tile % p.tiles_w;
         const uint32_t rest = tile / p.tiles_w;
@@ -131,43 +132,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     const uint32_t my_iters = my_tiles * p.k_stages;
 
     if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer (both CTAs)
+        // ------------------------------------------------------------ activation TMA producer (both CTAs)
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (uint32_t i = 0; ok && i < my_tiles; ++i) {
+                uint32_t z, xt, wt;
+                decode(cid + i * ncl, z, xt, wt);
+                const int x0 = (int)(xt * 2 * Cfg::kBM + rank * Cfg::kBM);
+                for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
+                    const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
+                    const int k0 = (int)(ks * Cfg::kBK);
+                    if (!mbar_wait(&empty[s], ph ^ 1, p.timeout_ns)) {
+                        fail();
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kABytes);  // both CTAs' bytes
+                    const uint32_t full_l = mapa_shared(&full[s], 0);
+                    uint8_t* a_dst = sStage + s * Cfg::kStageBytes;
+                    if constexpr (!NN) {
+                        tma_load_3d_pair(a_dst, &tmA, full_l, k0, x0, (int)z);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < Cfg::kBM / Cfg::kBK; ++j)
+                            tma_load_3d_pair(a_dst + j * Cfg::kBK * 128, &tmA, full_l, x0 + j * Cfg::kBK, k0, (int)z);
+                    }
+                }
+            }
+            // The activation loads are drained by the MMA (it waits for every one it consumes).
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ raw weight TMA producer (both CTAs)
         if (lane == 0) {
             uint32_t it = 0;
             for (uint32_t i = 0; ok && i < my_tiles; ++i) {
                 uint32_t z, xt, wt;
                 decode(cid + i * ncl, z, xt, wt);
                 const int zw = p.sW ? (int)z : 0;
-                const int x0 = (int)(xt * 2 * Cfg::kBM + rank * Cfg::kBM);
                 for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
-                    const uint32_t sa = it % Cfg::kSA, pa = (it / Cfg::kSA) & 1;
                     const uint32_t sw = it % Cfg::kSW, pw = (it / Cfg::kSW) & 1;
-                    const int k0 = (int)(ks * Cfg::kBK);
-                    if (!mbar_wait(&a_empty[sa], pa ^ 1, p.timeout_ns)) {
-                        fail();
-                        break;
-                    }
-                    if (leader) mbar_arrive_expect_tx(&a_full[sa], 2 * Cfg::kABytes);  // both CTAs' bytes
-                    const uint32_t afull_l = mapa_shared(&a_full[sa], 0);
-                    uint8_t* a_dst = sA + sa * Cfg::kABytes;
-                    if constexpr (!NN) {
-                        tma_load_3d_pair(a_dst, &tmA, afull_l, k0, x0, (int)z);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < Cfg::kBM / Cfg::kBK; ++j)
-                            tma_load_3d_pair(a_dst + j * Cfg::kBK * 128, &tmA, afull_l, x0 + j * Cfg::kBK, k0, (int)z);
-                    }
                     if (!mbar_wait(&w_empty[sw], pw ^ 1, p.timeout_ns)) {
                         fail();
                         break;
                     }
                     mbar_arrive_expect_tx(&w_full[sw], Cfg::kWBytes);
-                    tma_load_3d(sW + sw * Cfg::kWBytes, &tmW, &w_full[sw], k0,
+                    tma_load_3d(sW + sw * Cfg::kWBytes, &tmW, &w_full[sw], (int)(ks * Cfg::kBK),
                                 (int)(wt * Cfg::kBNP + rank * Cfg::kBNC), zw);
                 }
             }
-            // Drain this CTA's raw-weight loads (the activation loads are drained by the MMA).
-            for (uint32_t i = (it > Cfg::kSW ? it - Cfg::kSW : 0); i < it; ++i)
+            for (uint32_t i = (it > Cfg::kSW ? it - Cfg::kSW : 0); i < it; ++i)  // drain
                 if (!mbar_wait(&w_full[i % Cfg::kSW], (i / Cfg::kSW) & 1, p.timeout_ns)) fail();
         }
     } else if (warp == 1) {
@@ -178,23 +190,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             uint32_t it = 0;
             for (uint32_t i = 0; ok && i < my_tiles; ++i) {
                 const uint32_t acc = i % Cfg::kAcc, aph = (i / Cfg::kAcc) & 1;
-                if (!mbar_wait_cluster(&acc_empty[acc], aph ^ 1, p.timeout_ns)) {
+                if (!mbar_wait(&acc_empty[acc], aph ^ 1, p.timeout_ns)) {
                     fail();
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * Cfg::kBNP;
                 for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
-                    const uint32_t sa = it % Cfg::kSA, pa = (it / Cfg::kSA) & 1;
-                    const uint32_t sb = it % Cfg::kSB, pb = (it / Cfg::kSB) & 1;
-                    if (!mbar_wait_cluster(&a_full[sa], pa, p.timeout_ns) ||
-                        !mbar_wait_cluster(&b_full[sb], pb, p.timeout_ns)) {
+                    const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
+                    if (!mbar_wait(&full[s], ph, p.timeout_ns)) {
                         fail();
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sA + sa * Cfg::kABytes);
-                    const uint32_t b_addr = smem_u32(sB + sb * Cfg::kBBytes);
+                    const uint32_t a_addr = smem_u32(sStage + s * Cfg::kStageBytes);
+                    const uint32_t b_addr = a_addr + Cfg::kABytes;
 #pragma unroll
                     for (int kk = 0; kk < Cfg::kBK / Cfg::kUmmaK; ++kk) {
                         uint64_t adesc;
@@ -209,8 +219,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                         if constexpr (OperandTraits<TA>::kTf32) mma_tf32_pair(d_tmem, adesc, bdesc, idesc, accum);
                         else mma_f16_pair(d_tmem, adesc, bdesc, idesc, accum);
                     }
-                    mma_commit_pair_mc(&a_empty[sa], 0x3);
-                    mma_commit_pair_mc(&b_empty[sb], 0x3);
+                    mma_commit_pair_mc(&empty[s], 0x3);
                 }
                 if (!ok) break;
                 mma_commit_pair_mc(&acc_full[acc], 0x3);
@@ -223,53 +232,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         const int ct = threadIdx.x - 128;
         const int chunk = ct % Cfg::kChunksPerRow;
         const int row0 = ct / Cfg::kChunksPerRow;
-        const uint64_t kblocks = p.K / 32;
-        const uint64_t ldw_blocks = p.ldw / 32;
         constexpr int T = Cfg::kTasksPerThread;
-        // Scales for iteration j (two iterations ahead of use, so their L2 latency is hidden).
-        auto load_scales = [&](uint32_t j, float (&sc)[T]) {
-#pragma unroll
-            for (int t = 0; t < T; ++t) sc[t] = 0.0f;
-            if (j >= my_iters) return;
-            uint32_t z, xt, wt;
-            decode(cid + (j / p.k_stages) * ncl, z, xt, wt);
-            const uint64_t kb = ((uint64_t)(j % p.k_stages) * Cfg::kBK + (uint64_t)chunk * 16) / 32;
-            if (kb >= kblocks) return;
-            const float* ws = p.ws + (p.sW ? (uint64_t)z * (p.sW / 32) : 0);
-#pragma unroll
-            for (int t = 0; t < T; ++t) {
-                const uint32_t n = wt * Cfg::kBNP + rank * Cfg::kBNC + row0 + t * Cfg::kRowStep;
-                if (n < p.wrows) sc[t] = __ldg(ws + (uint64_t)n * ldw_blocks + kb);
-            }
-        };
+        // Scales come from L2 two stages ahead of use (latency hidden).
+        WeightCursor<T> cur;
+        cur.init(&p, cid, ncl, row0, Cfg::kRowStep, Cfg::kBK, chunk * 16, Cfg::kBNP, rank * Cfg::kBNC, Cfg::kBNC);
         float sc0[T], sc1[T], sc2[T];
-        load_scales(0, sc0);
-        load_scales(1, sc1);
+        uint4 unused[T];
+        cur.load<false>(sc0, unused);
+        cur.advance();
+        cur.load<false>(sc1, unused);
+        cur.advance();
         for (uint32_t it = 0; ok && it < my_iters; ++it) {
-            load_scales(it + 2, sc2);
+            cur.load<false>(sc2, unused);
+            cur.advance();
+            const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
             const uint32_t sw = it % Cfg::kSW, pw = (it / Cfg::kSW) & 1;
-            const uint32_t sb = it % Cfg::kSB, pb = (it / Cfg::kSB) & 1;
-            const bool got = mbar_wait(&w_full[sw], pw, p.timeout_ns) && mbar_wait(&b_empty[sb], pb ^ 1, p.timeout_ns);
+            const bool got = mbar_wait(&w_full[sw], pw, p.timeout_ns) && mbar_wait(&empty[s], ph ^ 1, p.timeout_ns);
             if (!__all_sync(0xffffffffu, got)) {  // the warp leaves the loop together
                 fail();
                 break;
             }
             const uint8_t* wsrc = sW + sw * Cfg::kWBytes;
-            uint8_t* bdst = sB + sb * Cfg::kBBytes;
+            uint8_t* bdst = sStage + s * Cfg::kStageBytes + Cfg::kABytes;
             uint4 raw[T];
-#pragma unroll
-            for (int t = 0; t < T; ++t)
-                raw[t] = *reinterpret_cast<const uint4*>(wsrc + (row0 + t * Cfg::kRowStep) * Cfg::kBK + chunk * 16);
 #pragma unroll
             for (int t = 0; t < T; ++t) {
                 const int r = row0 + t * Cfg::kRowStep;
-                dequant16<TA>(raw[t], sc0[t], bdst + r * 128, r, chunk * Cfg::kES);
+                raw[t] = (r < Cfg::kBNC) ? *reinterpret_cast<const uint4*>(wsrc + r * Cfg::kBK + chunk * 16)
+                                         : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+                const int r = row0 + t * Cfg::kRowStep;
+                if (r < Cfg::kBNC) dequant16<TA>(raw[t], sc0[t], bdst + r * 128, r, chunk * Cfg::kES);
             }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&w_empty[sw]);
-                mbar_arrive_cluster(mapa_shared(&b_full[sb], 0));
+                mbar_arrive_cluster(mapa_shared(&full[s], 0));
             }
 #pragma unroll
             for (int t = 0; t < T; ++t) {
@@ -298,6 +299,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 uint32_t raw[32];
                 tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * Cfg::kBNP + cc * 32, raw);
                 tmem_wait_ld();
+                if (cc + 1 == Cfg::kBNP / 32) {  // accumulator fully read: hand it back to the MMA
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+                }
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
@@ -309,7 +315,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                     }
                 }
                 uint8_t* buf = ebuf + (nstore & 1) * 4096;
-                if (lane == 0) bulk_wait_read<1>();
+                if (lane == 0) bulk_wait_read<1>();  // the store that last used `buf` has read it
                 __syncwarp();
                 if constexpr (!NN) store_epi_row<TC>(buf, lane, v);
                 else store_epi_col<TC>(buf, lane, v);
@@ -326,9 +332,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                     bulk_commit();
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
         }
         if (lane == 0) bulk_wait_all();
     }

@@ -73,6 +73,29 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
         if (global_ns() - t0 > timeout_ns) return false;
     }
 }
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait by spinning on the non-suspending test_wait: for the single thread that issues MMAs, whose
+// reaction time to a completing phase is tensor-pipe idle time.  Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_spin_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 256; ++i)
+            if (mbar_test_wait(bar, parity)) return true;
+        if (global_ns() - t0 > timeout_ns) return false;
+    }
+}
 // Wait for the phase with the given parity to complete.  Returns false once `timeout_ns` of
 // global time has passed, so a missing arrival turns into an error status instead of a hang.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
@@ -97,6 +120,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
             smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
+}
+// Bring a tensor tile into L2 ahead of its TMA load (no shared memory involved).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
 }
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
     asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
@@ -207,8 +237,10 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
     return r;
 }
+// Arrive on an mbarrier given by its shared::cluster address (possibly in the peer CTA).  The
+// producer orders its shared-memory writes for the tensor core with fence.proxy.async first.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // TMA load into this CTA's shared memory whose completion is counted on an mbarrier that may
 // live in the peer CTA of the pair (cta_group::2).
@@ -261,6 +293,13 @@ __device__ __forceinline__ void mma_commit_pair_mc(uint64_t* bar, uint16_t cta_m
 __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
+}
+
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may
+// start (prologue) while its predecessor drains; it must wait before touching global memory.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ------------------------------------------------------------------ UMMA descriptors
