@@ -1,18 +1,28 @@
-"""Benchmark of the sdvk-b200 hot path: the Q8_0 dequant GEMM
-Y[9216,1280] = X[9216,1280] . dequant(W[1280,1280])^T, fp16 X, GGUF Q8_0 W, fp32 Y.
+"""Benchmark of the sdvk-b200 hot path on one B200 per rank.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sdvk|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sdvk|reference] [--workload NAME]
 
-One step = one GEMM launch over one set of synthetic inputs.  Four rotating input/output sets
-(4 x 72 MB, larger than the 126 MB L2) keep every step's operands out of L2.  Steps are captured in
-CUDA graphs and replayed; the timed region is bracketed by a barrier and a device synchronize and
-timed with CUDA events on the launching stream; the job time is the max over ranks.  Multi-GPU
-runs are independent replicas (images sharded one per GPU): weak scaling, no collective on the
-data path.  Rank 0 prints one JSON line.
+Workloads (BASELINE configs 0 and 1, synthetic seeded inputs of the stated shapes):
+  gemm             (default) Q8_0 dequant GEMM Y[9216,1280] = X[9216,1280] . dequant(W[1280,1280])^T,
+                   fp16 X, GGUF Q8_0 W (int8 + per-32 scale), fp32 Y
+  attn-self-4096   fused attention, batch 2, 4096 tokens, 10 heads x 64, fp16
+  attn-self-1024   fused attention, batch 2, 1024 tokens, 20 heads x 64, fp16
+  attn-cross-77    fused attention, batch 2, 1024 queries x 77 keys, 20 heads x 64, fp16
 
---impl reference times the reference's own GEMM arithmetic (the C++ restatement of
-gemm_nt_q8_v.comp in oracle/, which is what the reference's Vulkan path computes; the Vulkan path
-itself needs a graphics stack this machine does not have) on the host cores.
+One step = one launch of the hot-path kernel over one set of inputs.  Rotating input/output sets
+whose total exceeds the 126 MB L2 keep every step's operands out of L2.  Steps are captured in CUDA
+graphs and replayed; the timed region is bracketed by a barrier and a device synchronize and timed
+with CUDA events on the launching stream; the job time is the max over ranks.  Multi-GPU runs are
+independent replicas (one image per GPU): weak scaling, no collective on the data path.  Rank 0
+prints one JSON line.
+
+`e2e` is the same metric through the C ABI with pinned host buffers: each step uploads that step's
+inputs, runs the kernel and downloads the result, all inside the timed region.
+
+--impl reference times the reference's own arithmetic for the workload (the C++ restatement of
+gemm_nt_q8_v.comp / fused_attn_tiled.comp / fused_attn.comp in oracle/, which is what the
+reference's Vulkan path computes; the Vulkan path itself needs a graphics stack this machine does
+not have) on the host cores.
 """
 from __future__ import annotations
 
@@ -29,12 +39,8 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-M, N, K = 9216, 1280, 1280
-FLOP = 2.0 * M * N * K
-METRIC = "Q8_0 GEMM TFLOP/s @9216x1280x1280"
-WORKLOAD = "Q8_0 dequant GEMM 9216x1280x1280 (BASELINE config 0): fp16 X ~N(0,1), Q8_0 W (int8 U[-127,127], scale |N(0,0.02)|/127), fp32 Y"
-ROTATE = 4
 GRAPH_LEN = 50
+L2_BYTES = 126 << 20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
@@ -48,11 +54,12 @@ def peaks():
         return dict(FALLBACK_PEAKS, bf16_tflops_sustained=FALLBACK_PEAKS["bf16_tflops"]), "fallback"
 
 
-def profile_traffic():
-    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary, if present."""
+def profile_traffic(workload: str):
+    """DRAM bytes (read + write) per launch of the workload's kernel, from the committed ncu
+    summary profiles/traffic.json, if present."""
     try:
-        with open(os.path.join(ROOT, "profiles", "gemm_q8_nt_9216x1280x1280.json")) as f:
-            return float(json.load(f)["dram_bytes_per_launch"])
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return float(json.load(f)[workload]["dram_bytes_per_launch"])
     except Exception:
         return None
 
@@ -112,67 +119,202 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3] not in ("", "[N/A]"))}
 
 
-def make_inputs(torch, device, seed):
-    """Config-0 inputs generated on the device with torch's RNG (seeded per rank and set)."""
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    x = torch.randn((M, K), generator=g, device=device, dtype=torch.float32).half()
-    q = torch.randint(-127, 128, (N, K), generator=g, device=device, dtype=torch.int8)
-    sc = (torch.randn((N * K // 32,), generator=g, device=device).abs() * 0.02 / 127).half().float()
-    y = torch.empty((M, N), device=device, dtype=torch.float32)
-    return x, q, sc, y
 
 
-def cpu_reference(x_np, q_np, s_np, budget_s):
-    """Time the reference arithmetic (oracle restatement of gemm_nt_q8_v.comp, fp32) on a bounded
-    row sample of the workload; returns (TFLOP/s, rows, threads, seconds)."""
+# ------------------------------------------------------------------------------------------ workloads
+class GemmWorkload:
+    """the Q8_0 NT GEMM (gemm_nt_q8_v.comp's operator)."""
+
+    name = "gemm"
+    M, N, K = 9216, 1280, 1280
+    metric = "Q8_0 GEMM TFLOP/s @9216x1280x1280"
+    describe = ("Q8_0 dequant GEMM 9216x1280x1280 (BASELINE config 0): fp16 X ~N(0,1), Q8_0 W (int8 U[-127,127], "
+                "scale |N(0,0.02)|/127), fp32 Y")
+    bound = "tensor"
+    dtype = "f16"
+
+    def __init__(self):
+        M, N, K = self.M, self.N, self.K
+        self.flop = 2.0 * M * N * K
+        self.bytes = M * K * 2 + M * N * 4 + N * K + N * K // 32 * 4
+        self.rotate = max(2, -(-2 * L2_BYTES // self.bytes))
+
+    def make_set(self, torch, device, seed):
+        M, N, K = self.M, self.N, self.K
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        x = torch.randn((M, K), generator=g, device=device, dtype=torch.float32).half()
+        q = torch.randint(-127, 128, (N, K), generator=g, device=device, dtype=torch.int8)
+        sc = (torch.randn((N * K // 32,), generator=g, device=device).abs() * 0.02 / 127).half().float()
+        y = torch.empty((M, N), device=device, dtype=torch.float32)
+        return x, q, sc, y
+
+    def step(self, torch_ops, st):
+        x, q, s, y = st
+        torch_ops.gemm_q8_nt(x, q, s, out=y)
+
+    def e2e(self, sdvk_b200, ctx, torch, st):
+        """Per step: pinned X -> device, GEMM, device Y -> pinned host."""
+        x, q, s, y = st
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x.cpu())
+        yh = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        M, N, K = self.M, self.N, self.K
+
+        def run():
+            ctx.upload_async(x.data_ptr(), xh.data_ptr(), xh.numel() * 2)
+            ctx.gemm_q8_nt(x.data_ptr(), sdvk_b200.F16, q.data_ptr(), s.data_ptr(), None, y.data_ptr(),
+                           sdvk_b200.F32, M, N, K, K, N)
+            ctx.download_async(yh.data_ptr(), y.data_ptr(), yh.numel() * 4)
+
+        return run, xh.numel() * 2, yh.numel() * 4, "sdvk_upload_async + sdvk_gemm_q8_nt + sdvk_download_async"
+
+    def host_inputs(self):
+        M, N, K = self.M, self.N, self.K
+        rng = np.random.default_rng(0)
+        x = rng.standard_normal((M, K), dtype=np.float32).astype(np.float16).astype(np.float32)
+        q = rng.integers(-127, 128, (N, K), dtype=np.int8)
+        s = (np.abs(rng.standard_normal(N * K // 32)) * 0.02 / 127).astype(np.float16).astype(np.float32)
+        return x, q, s
+
+    def cpu_run(self, inputs, rows):
+        """The reference arithmetic on the first `rows` rows of X; returns the FLOP it did."""
+        from oracle import pyoracle
+
+        x, q, s = inputs
+        pyoracle.gemm_nt_q8_shader(np.ascontiguousarray(x[:rows]), q, s)
+        return 2.0 * rows * self.N * self.K
+
+    cpu_units = M
+    cpu_what = "rows of X (fp32 restatement of gemm_nt_q8_v.comp, OpenMP over 128x64 output tiles)"
+
+
+class AttnWorkload:
+    """fusedAttention (fused_attn_tiled.comp / fused_attn.comp's operator)."""
+
+    dtype = "f16"
+
+    def __init__(self, name, B, Tq, Tk, heads, hd=64):
+        self.name, self.B, self.Tq, self.Tk, self.heads, self.hd = name, B, Tq, Tk, heads, hd
+        self.C = heads * hd
+        self.flop = 4.0 * B * heads * Tq * Tk * hd
+        self.bytes = 2 * (2 * B * Tq * self.C + 2 * B * Tk * self.C)
+        self.bound = "tensor" if self.flop / self.bytes > 300 else "hbm"
+        kind = "self" if Tq == Tk else "cross"
+        self.metric = f"fused attention TFLOP/s @B{B} {kind} Tq{Tq} Tk{Tk} {heads}x{hd}"
+        self.describe = (f"fused {kind}-attention (BASELINE config 1): batch {B}, Tq {Tq}, Tk {Tk}, {heads} heads x "
+                         f"{hd}, fp16 Q/K/V ~N(0,1) token-major [B, T, {self.C}], scale 1/sqrt({hd}), fp16 O")
+        self.rotate = max(2, -(-2 * L2_BYTES // self.bytes))
+        self.cpu_units = Tq
+        self.cpu_what = (f"query rows of batch 0, all {heads} heads (fp32 restatement of "
+                         f"{'fused_attn_tiled.comp' if hd == 64 and Tk >= 256 else 'fused_attn.comp'})")
+
+    def make_set(self, torch, device, seed):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        B, C = self.B, self.C
+        q = torch.randn((B, self.Tq, C), generator=g, device=device, dtype=torch.float32).half()
+        k = torch.randn((B, self.Tk, C), generator=g, device=device, dtype=torch.float32).half()
+        v = torch.randn((B, self.Tk, C), generator=g, device=device, dtype=torch.float32).half()
+        o = torch.empty((B, self.Tq, C), device=device, dtype=torch.float16)
+        return q, k, v, o
+
+    def step(self, torch_ops, st):
+        q, k, v, o = st
+        torch_ops.attention(q, k, v, self.heads, out=o)
+
+    def e2e(self, sdvk_b200, ctx, torch, st):
+        """Per step: pinned Q, K, V -> device, attention, device O -> pinned host."""
+        q, k, v, o = st
+        hosts = []
+        for t in (q, k, v):
+            h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            h.copy_(t.cpu())
+            hosts.append(h)
+        oh = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+        d = sdvk_b200.AttnDesc()
+        d.q, d.k, d.v, d.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+        d.dtype = d.o_dtype = sdvk_b200.F16
+        d.batch, d.heads, d.Tq, d.Tk, d.hd = self.B, self.heads, self.Tq, self.Tk, self.hd
+        d.ldq = d.ldk = d.ldv = d.ldo = self.C
+        d.sq, d.so = self.Tq * self.C, self.Tq * self.C
+        d.sk = d.sv = self.Tk * self.C
+        d.hq = d.hk = d.hv = d.ho = self.hd
+        d.scale = 1.0 / math.sqrt(self.hd)
+        d.causal = 0
+
+        def run():
+            for h, t in zip(hosts, (q, k, v)):
+                ctx.upload_async(t.data_ptr(), h.data_ptr(), h.numel() * 2)
+            ctx.attention(d)
+            ctx.download_async(oh.data_ptr(), o.data_ptr(), oh.numel() * 2)
+
+        h2d = sum(h.numel() * 2 for h in hosts)
+        return run, h2d, oh.numel() * 2, "3x sdvk_upload_async + sdvk_attention + sdvk_download_async"
+
+    def host_inputs(self):
+        rng = np.random.default_rng(1)
+        C = self.C
+        f16 = lambda a: a.astype(np.float16).astype(np.float32)
+        return (f16(rng.standard_normal((self.Tq, C), dtype=np.float32)),
+                f16(rng.standard_normal((self.Tk, C), dtype=np.float32)),
+                f16(rng.standard_normal((self.Tk, C), dtype=np.float32)))
+
+    def cpu_run(self, inputs, rows):
+        from oracle import pyoracle
+
+        q, k, v = inputs
+        pyoracle.fused_attention(np.ascontiguousarray(q[:rows]), k, v, rows, self.Tk, self.C, self.heads)
+        return 4.0 * self.heads * rows * self.Tk * self.hd
+
+
+WORKLOADS = {
+    "gemm": GemmWorkload,
+    "attn-self-4096": lambda: AttnWorkload("attn-self-4096", 2, 4096, 4096, 10),
+    "attn-self-1024": lambda: AttnWorkload("attn-self-1024", 2, 1024, 1024, 20),
+    "attn-cross-77": lambda: AttnWorkload("attn-cross-77", 2, 1024, 77, 20),
+}
+
+
+def cpu_sample(wl, budget_s, steps=None):
+    """Time the reference arithmetic on a bounded sample of the workload.  With `steps` given (the
+    reference arm), each step runs the same number of whole units (rows of X, query rows), sized
+    from a probe so that the steps take about `budget_s` together.  Without it, whole workloads (or
+    the largest unit count that fits) repeat until `budget_s` has passed.  Returns
+    (FLOP per s, units per run, runs, seconds, threads)."""
     from oracle import pyoracle
 
     threads = pyoracle.num_threads()
-    a = np.ascontiguousarray(x_np.astype(np.float32))
-    pyoracle.gemm_nt_q8_shader(a[:64], q_np, s_np)  # warm-up
-    reps, t0 = 0, time.perf_counter()
-    while True:  # whole GEMMs until the budget is spent
-        pyoracle.gemm_nt_q8_shader(a, q_np, s_np)
-        reps += 1
+    inputs = wl.host_inputs()
+    probe = min(wl.cpu_units, 64)
+    t0 = time.perf_counter()
+    wl.cpu_run(inputs, probe)
+    per_unit = (time.perf_counter() - t0) / probe
+    per_run = budget_s / (steps or 1)
+    units = int(max(8, min(wl.cpu_units, per_run / max(per_unit, 1e-9))))
+    wl.cpu_run(inputs, units)  # warm-up at the timed size
+    flop, runs, t0 = 0.0, 0, time.perf_counter()
+    while True:
+        flop += wl.cpu_run(inputs, units)
+        runs += 1
         dt = time.perf_counter() - t0
-        if dt >= budget_s:
+        if (steps is not None and runs >= steps) or (steps is None and dt >= budget_s):
             break
-    return 2.0 * M * N * K * reps / dt / 1e12, reps, threads, dt
+    return flop / dt, units, runs, dt, threads
 
 
-def run_reference(args, rank, world):
+def run_reference(args, rank, world, wl):
     if rank != 0:
         return 0
-    rng = np.random.default_rng(0)
-    x = rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)
-    q = rng.integers(-127, 128, (N, K), dtype=np.int8)
-    s = (np.abs(rng.standard_normal(N * K // 32)) * 0.02 / 127).astype(np.float16).astype(np.float32)
-    from oracle import pyoracle
-
-    threads = pyoracle.num_threads()
-    # each step: a bounded row sample, sized so the whole run takes about a minute
-    budget = 60.0 / max(1, args.steps + args.warmup)
-    rows = 16
-    a = np.ascontiguousarray(x[:rows].astype(np.float32))
-    t0 = time.perf_counter()
-    pyoracle.gemm_nt_q8_shader(a, q, s)
-    per_row = (time.perf_counter() - t0) / rows
-    rows = int(max(8, min(M, budget / max(per_row, 1e-9))))
-    a = np.ascontiguousarray(x[:rows].astype(np.float32))
-    for _ in range(args.warmup):
-        pyoracle.gemm_nt_q8_shader(a, q, s)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        pyoracle.gemm_nt_q8_shader(a, q, s)
-    dt = time.perf_counter() - t0
-    value = 2.0 * rows * N * K * args.steps / dt / 1e12
-    sample = f"{rows} of {M} rows per step (fp32 restatement of gemm_nt_q8_v.comp, BM128 variant's per-element order)"
+    budget = 60.0
+    fps, units, _, dt, threads = cpu_sample(wl, budget, steps=args.steps)
+    value = fps / 1e12
+    sample = f"{units} of {wl.cpu_units} {wl.cpu_what} per step"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "impl": "reference", "metric": wl.metric, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "sample_rows": rows},
+        "data": "synthetic", "config": {"workload": wl.describe, "sample_units": units},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference Vulkan path unavailable on this box (no graphics stack); its shader arithmetic is timed "
@@ -185,19 +327,22 @@ def run_reference(args, rank, world):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: about 1 s of GPU work)")
     ap.add_argument("--warmup", type=int, default=100)
     ap.add_argument("--impl", default="sdvk", choices=["sdvk", "reference"])
+    ap.add_argument("--workload", default="gemm", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
-    if args.warmup < 3:
-        args.warmup = 3
+    args.warmup = max(3, args.warmup)
+    wl = WORKLOADS[args.workload]()
+    if args.steps is None:
+        args.steps = 3 if args.impl == "reference" else 20000 if wl.flop < 5e10 else 5000
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        return run_reference(args, rank, world)
+        return run_reference(args, rank, world, wl)
 
     import torch
     import torch.distributed as dist
@@ -212,12 +357,11 @@ def main(argv=None):
     import sdvk_b200
     from sdvk_b200 import torch_ops
 
-    sets = [make_inputs(torch, device, 1000 * rank + i) for i in range(ROTATE)]
+    sets = [wl.make_set(torch, device, 1000 * rank + i) for i in range(wl.rotate)]
     ctx = torch_ops.context(device)
 
     def step(i):
-        x, q, s, y = sets[i % ROTATE]
-        torch_ops.gemm_q8_nt(x, q, s, out=y)
+        wl.step(torch_ops, sets[i % wl.rotate])
 
     # warm-up (also the first launch's attribute setup), then graphs of GRAPH_LEN steps
     for i in range(args.warmup):
@@ -266,67 +410,57 @@ def main(argv=None):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ms_per_step = ms_max / args.steps
-    value = world * FLOP * args.steps / (ms_max * 1e-3) / 1e12
+    value = world * wl.flop * args.steps / (ms_max * 1e-3) / 1e12
 
-    # ---- end to end through the C ABI: pinned host X -> device, GEMM, device Y -> pinned host
+    # ---- end to end through the C ABI with pinned host buffers
     e2e_steps = min(args.steps, 100)
-    xh = torch.empty((M, K), dtype=torch.float16, pin_memory=True)
-    xh.copy_(sets[0][0].cpu())
-    yh = torch.empty((M, N), dtype=torch.float32, pin_memory=True)
-    xd, qd, sd, yd = sets[0]
     ctx.set_stream(torch.cuda.current_stream(device).cuda_stream)
-
-    def e2e_step():
-        ctx.upload_async(xd.data_ptr(), xh.data_ptr(), xh.numel() * 2)
-        ctx.gemm_q8_nt(xd.data_ptr(), sdvk_b200.F16, qd.data_ptr(), sd.data_ptr(), None, yd.data_ptr(),
-                       sdvk_b200.F32, M, N, K, K, N)
-        ctx.download_async(yh.data_ptr(), yd.data_ptr(), yh.numel() * 4)
-
+    run_e2e, h2d, d2h, path = wl.e2e(sdvk_b200, ctx, torch, sets[0])
     for _ in range(3):
-        e2e_step()
+        run_e2e()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     ev0.record()
     for _ in range(e2e_steps):
-        e2e_step()
+        run_e2e()
     ev1.record()
     torch.cuda.synchronize()
     t = torch.tensor([ev0.elapsed_time(ev1)], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item()) / e2e_steps
-    e2e_value = world * FLOP / (e2e_ms * 1e-3) / 1e12
+    e2e_value = world * wl.flop / (e2e_ms * 1e-3) / 1e12
 
-    # ---- CPU baseline (rank 0, N = 1 only)
+    # ---- CPU baseline (rank 0, N = 1 only): a bounded sample of the same workload
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        x_np = sets[0][0].cpu().numpy()
-        q_np = sets[0][1].cpu().numpy()
-        s_np = sets[0][2].cpu().numpy()
-        tf, reps, threads, secs = cpu_reference(x_np, q_np, s_np, budget_s=10.0)
-        cpu = {"value": tf, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": f"{reps} whole {M}x{N}x{K} GEMMs on the same inputs (fp32 restatement of "
-                         f"gemm_nt_q8_v.comp, OpenMP over tiles), {secs:.1f} s"}
+        fps, units, runs, secs, threads = cpu_sample(wl, budget_s=15.0)
+        cpu = {"value": fps / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{runs} x {units} of {wl.cpu_units} {wl.cpu_what}, {secs:.1f} s"}
 
     pk, pk_kind = peaks()
-    achieved = FLOP / (ms_per_step * 1e-3) / 1e12
+    achieved_tf = wl.flop / (ms_per_step * 1e-3) / 1e12
+    achieved_gbs = wl.bytes / (ms_per_step * 1e-3) / 1e9
+    if wl.bound == "tensor":
+        roof = {"bound": "tensor", "achieved": achieved_tf, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved_tf / pk["bf16_tflops"], "peak_kind": f"{pk_kind} dense bf16 burst"}
+    else:
+        roof = {"bound": "hbm", "achieved": achieved_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved_gbs / pk["hbm_gbs"], "peak_kind": f"{pk_kind} HBM copy"}
+    roof.update({"traffic": profile_traffic(wl.name), "algorithmic_flop_per_launch": wl.flop,
+                 "algorithmic_bytes_per_launch": wl.bytes})
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "metric": wl.metric, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "parallelism": f"replicas x{world}",
-                       "l2": f"{ROTATE} rotating input/output sets ({ROTATE * 72} MB > 126 MB L2)",
+            "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+            "config": {"workload": wl.describe, "parallelism": f"replicas x{world}",
+                       "l2": f"{wl.rotate} rotating input/output sets ({wl.rotate * wl.bytes / 1e6:.0f} MB > 126 MB L2)",
                        "timing": f"CUDA events over CUDA-graph replays of {GRAPH_LEN} launches"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": achieved / pk["bf16_tflops"], "traffic": profile_traffic(),
-                         "peak_kind": f"{pk_kind} dense bf16 burst",
-                         "algorithmic_flop_per_launch": FLOP,
-                         "algorithmic_bytes_per_launch": M * K * 2 + M * N * 4 + N * K + N * K // 32 * 4},
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 2,
-                    "d2h_bytes_per_step": M * N * 4, "ms_per_step": e2e_ms,
-                    "path": "sdvk_upload_async + sdvk_gemm_q8_nt + sdvk_download_async, pinned host buffers"},
+            "roofline": roof,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms, "path": path + ", pinned host buffers"},
             "gpu_launches": args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
