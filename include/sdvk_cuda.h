@@ -90,6 +90,8 @@ SDVK_API int sdvk_download(sdvk_ctx* ctx, void* dst_host, const void* src_dev, u
 /* Stream-ordered copies (the staged in-step uploads/readbacks, vk_engine.hpp:136-153). */
 SDVK_API int sdvk_upload_async(sdvk_ctx* ctx, void* dst_dev, const void* src_host, uint64_t bytes);
 SDVK_API int sdvk_download_async(sdvk_ctx* ctx, void* dst_host, const void* src_dev, uint64_t bytes);
+/* Engine::copyBuf (vk_engine.hpp:115): stream-ordered device-to-device copy. */
+SDVK_API int sdvk_copy(sdvk_ctx* ctx, void* dst_dev, const void* src_dev, uint64_t bytes);
 /* Engine::fill (vk_engine.hpp:114): fill with a 32-bit pattern, bytes % 4 == 0. */
 SDVK_API int sdvk_fill_u32(sdvk_ctx* ctx, void* dst_dev, uint32_t value, uint64_t bytes);
 

@@ -72,6 +72,7 @@ SIGNATURES = {
     "sdvk_download": (_I, [_P, _P, _P, _U64]),
     "sdvk_upload_async": (_I, [_P, _P, _P, _U64]),
     "sdvk_download_async": (_I, [_P, _P, _P, _U64]),
+    "sdvk_copy": (_I, [_P, _P, _P, _U64]),
     "sdvk_fill_u32": (_I, [_P, _P, _U32, _U64]),
     "sdvk_step_begin": (_I, [_P]),
     "sdvk_step_end": (_I, [_P]),
@@ -183,6 +184,9 @@ class Context:
 
     def download_async(self, dst_host: int, src: int, nbytes: int) -> None:
         self._check(lib().sdvk_download_async(self._h, dst_host, src, nbytes), "download_async")
+
+    def copy(self, dst: int, src: int, nbytes: int) -> None:
+        self._check(lib().sdvk_copy(self._h, dst, src, nbytes), "copy")
 
     def synchronize(self) -> None:
         self._check(lib().sdvk_synchronize(self._h), "synchronize")

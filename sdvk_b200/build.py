@@ -20,6 +20,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJDIR = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libsdvk_b200.so")
+HOST = os.path.join(PKG, "host")
+ENGINE_LIB = os.path.join(PKG, "libsdvk_engine.so")  # C++ ofc::gpu::Engine mirror over the C ABI
 SOURCES = ["sdvk_abi.cu", "gemm_q8.cu", "attention.cu"]
 HEADERS = ["ptx.cuh", "gemm_q8.cuh", "gemm_q8_2sm.cuh", "attention.cuh", "backend.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -60,8 +62,22 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), SOURCES))
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < _newest(objs):
         # Static cudart keeps the library independent of which libcudart the host process loaded.
-        subprocess.run([nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-lcuda"], check=True)
+        subprocess.run([nvcc(), *ARCH, "-shared", "-Xlinker", "-soname=libsdvk_b200.so", "-o", LIB, *objs, "-lcuda"],
+                       check=True)
+    build_engine(force)
     return LIB
+
+
+def build_engine(force: bool = False) -> str:
+    """The C++ engine mirror (host/engine.cpp) as libsdvk_engine.so, linked against libsdvk_b200.so."""
+    src = os.path.join(HOST, "engine.cpp")
+    deps = [src, LIB, os.path.join(ROOT, "include", "sdvk_cuda.h"),
+            os.path.join(HOST, "Modules", "GPU", "vk_engine.hpp"), os.path.join(HOST, "Modules", "GPU", "fused_attn.hpp")]
+    if force or not os.path.exists(ENGINE_LIB) or os.path.getmtime(ENGINE_LIB) < _newest(deps):
+        cxx = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else (shutil.which("g++") or "g++")
+        subprocess.run([cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-I", os.path.join(ROOT, "include"), "-I", HOST,
+                        "-o", ENGINE_LIB, src, "-L", PKG, "-lsdvk_b200", "-Wl,-rpath,$ORIGIN"], check=True)
+    return ENGINE_LIB
 
 
 def main(argv=None) -> int:

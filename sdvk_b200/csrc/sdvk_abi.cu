@@ -233,6 +233,12 @@ int sdvk_download_async(sdvk_ctx* ctx, void* dst, const void* src, uint64_t byte
     return cuda_err(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "download_async");
 }
 
+int sdvk_copy(sdvk_ctx* ctx, void* dst, const void* src, uint64_t bytes) {
+    if (!ctx || (!dst && bytes) || (!src && bytes)) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return cuda_err(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx->stream), "copy");
+}
+
 int sdvk_fill_u32(sdvk_ctx* ctx, void* dst, uint32_t value, uint64_t bytes) {
     if (!ctx || !dst || bytes % 4) return SDVK_E_ARG;
     if (int rc = use_device(ctx)) return rc;
