@@ -271,6 +271,11 @@ int sdvk_step_wait(sdvk_ctx* ctx, uint32_t timeout_ms) {
     if (!ctx) return SDVK_E_ARG;
     if (!ctx->step_recorded) return set_err(ctx, SDVK_E_STATE, "step_wait without a finished step");
     const auto t0 = std::chrono::steady_clock::now();
+    if (timeout_ms == 0) {  // no deadline: block in the driver (no polling latency)
+        if (int rc = cuda_err(ctx, cudaEventSynchronize(ctx->step_done), "step wait")) return rc;
+        ctx->step_recorded = false;
+        return collect_device_error(ctx);
+    }
     while (true) {
         cudaError_t e = cudaEventQuery(ctx->step_done);
         if (e == cudaSuccess) break;
