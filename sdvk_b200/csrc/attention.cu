@@ -1,7 +1,10 @@
 // attention.cu -- host side of the fused attention kernel (attention.cuh) and the finite check.
 #include <cmath>
+#include <cstdlib>
+#include <string>
 
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "backend.hpp"
 
 namespace sdvk {
@@ -29,6 +32,75 @@ int launch_out(const AttnParams& p, int o_dtype, bool async, const LaunchEnv& en
 }
 
 bool a16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// 4-D tiled map over one operand: {hd (contiguous), tokens, heads, batch}, box {64, 128, 1, 1},
+// 128-byte swizzle (the UMMA K-major / MN-major SW128 operand layout).
+int make_attn_map(CUtensorMap* m, int dtype, const void* base, uint32_t T, uint32_t heads, uint32_t batch,
+                  uint64_t ld, uint64_t hs, uint64_t bs, const LaunchEnv& env, const char* what) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return fail(env, SDVK_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const uint64_t es = 2;
+    // a dimension of extent 1 is never stepped: give it a legal stride
+    if (heads == 1) hs = ld * T;
+    if (batch == 1) bs = hs * heads;
+    cuuint64_t dims[4] = {64, T, heads, batch};
+    cuuint64_t strides[3] = {ld * es, hs * es, bs * es};
+    cuuint32_t box[4] = {64, 128, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(m, dtype == SDVK_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(env, SDVK_E_SHAPE, std::string("attention tensor map rejected: ") + what);
+    return SDVK_OK;
+}
+
+// The tensor-core kernel takes head dim 64, 16-bit Q/K/V, a positive scale, and TMA-legal layouts
+// (16-byte aligned bases and strides) with an output that takes 16-byte vector stores.
+// SDVK_ATTN_KERNEL=mma forces the warp-level kernel (attention.cuh).
+bool tc_eligible(const sdvk_attn_desc& d) {
+    const char* e = getenv("SDVK_ATTN_KERNEL");
+    if (e && e[0] == 'm') return false;
+    const uint64_t es = 2, eo = d.o_dtype == SDVK_F32 ? 4 : 2;
+    auto s16 = [](uint64_t bytes) { return bytes % 16 == 0 && bytes < (1ull << 40); };
+    return (d.dtype == SDVK_F16 || d.dtype == SDVK_BF16) && d.hd == 64 && d.scale > 0.0f && d.Tk > 0 &&
+           a16(d.q) && a16(d.k) && a16(d.v) && a16(d.o) && s16(d.ldq * es) && s16(d.ldk * es) && s16(d.ldv * es) &&
+           s16(d.hq * es) && s16(d.hk * es) && s16(d.hv * es) && s16(d.sq * es) && s16(d.sk * es) &&
+           s16(d.sv * es) && s16(d.ldo * eo) && s16(d.ho * eo) && s16(d.so * eo) && d.heads <= 65535 &&
+           d.batch <= 65535;
+}
+
+template <class T, class TO>
+int launch_tc(const sdvk_attn_desc& d, const LaunchEnv& env) {
+    CUtensorMap mq, mk, mv;
+    if (int rc = make_attn_map(&mq, d.dtype, d.q, d.Tq, d.heads, d.batch, d.ldq, d.hq, d.sq, env, "Q")) return rc;
+    if (int rc = make_attn_map(&mk, d.dtype, d.k, d.Tk, d.heads, d.batch, d.ldk, d.hk, d.sk, env, "K")) return rc;
+    if (int rc = make_attn_map(&mv, d.dtype, d.v, d.Tk, d.heads, d.batch, d.ldv, d.hv, d.sv, env, "V")) return rc;
+    TcAttnParams p{};
+    p.o = d.o;
+    p.ldo = d.ldo;
+    p.so = d.so;
+    p.ho = d.ho;
+    p.Tq = d.Tq;
+    p.Tk = d.Tk;
+    p.heads = d.heads;
+    p.batch = d.batch;
+    p.scale_log2 = d.scale * 1.4426950408889634f;
+    p.causal = d.causal ? 1u : 0u;
+    p.err = env.err_dev;
+    p.timeout_ns = env.timeout_ns;
+    auto kern = attn_tc_kernel<T, TO>;
+    if (!kernel_smem_attr(reinterpret_cast<const void*>(kern), TcAttnCfg::kSmemBytes, env.device))
+        return fail(env, SDVK_E_CUDA, "attn_tc_kernel: shared memory opt-in failed");
+    dim3 grid((d.Tq + TcAttnCfg::kBM - 1) / TcAttnCfg::kBM, d.heads, d.batch);
+    kern<<<grid, TcAttnCfg::kThreads, TcAttnCfg::kSmemBytes, env.stream>>>(mq, mk, mv, p);
+    return cuda_check(env, cudaGetLastError(), "attn_tc_kernel launch");
+}
+
+template <class T>
+int launch_tc_out(const sdvk_attn_desc& d, const LaunchEnv& env) {
+    if (d.o_dtype == SDVK_F32) return launch_tc<T, float>(d, env);
+    return launch_tc<T, __half>(d, env);
+}
 
 template <class T>
 __global__ void finite_kernel(const T* x, uint64_t n, uint32_t* flag) {
@@ -72,6 +144,10 @@ int attention(const sdvk_attn_desc& d, const LaunchEnv& env) {
     p.ho = d.ho;
     p.scale_log2 = d.scale * 1.4426950408889634f;
     p.causal = d.causal ? 1u : 0u;
+    if (tc_eligible(d)) {
+        if (d.dtype == SDVK_F16) return launch_tc_out<__half>(d, env);
+        return launch_tc_out<__nv_bfloat16>(d, env);
+    }
     // cp.async staging needs 16-byte aligned rows and whole 8-element chunks of the head.
     const uint64_t es = 2;
     const bool async = d.dtype != SDVK_F32 && d.hd % 8 == 0 && a16(d.q) && a16(d.k) && a16(d.v) &&

@@ -1,6 +1,7 @@
 // backend.hpp -- internal interface between the C ABI (sdvk_abi.cu) and the kernel launchers.
 #pragma once
 
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -40,6 +41,10 @@ struct GemmQ8Desc {
 };
 
 int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env);
+// cuTensorMapEncodeTiled from the driver (null if unavailable), and the per-device dynamic
+// shared-memory opt-in for a kernel (done once per kernel and device).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+bool kernel_smem_attr(const void* kern, int bytes, int device);
 int attention(const sdvk_attn_desc& d, const LaunchEnv& env);
 int check_finite(const void* x, int dtype, uint64_t n, uint32_t* flag_dev, const LaunchEnv& env);
 

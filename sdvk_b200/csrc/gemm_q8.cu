@@ -278,6 +278,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
+bool kernel_smem_attr(const void* kern, int bytes, int device) { return set_smem_attr(kern, bytes, device); }
+
 int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env) {
     if (!d.x || !d.wq || !d.ws || !d.c) return fail(env, SDVK_E_ARG, "null pointer");
     if (d.x_dtype != SDVK_F32 && d.x_dtype != SDVK_F16 && d.x_dtype != SDVK_BF16)

@@ -122,3 +122,33 @@ def test_attention_unsupported_head_dim(orc, cuda_ok):
     with pytest.raises(sdvk_b200.SdvkError) as e:
         ctx.fused_attention(q.data_ptr(), q.data_ptr(), q.data_ptr(), q.data_ptr(), 4, 4, 1280, 10)  # hd 128
     assert e.value.status == sdvk_b200.E_SHAPE
+
+
+KERNEL_CASES = [
+    # (B, Tq, Tk, heads, causal, dtype, out)   head dim 64: the tensor-core (tcgen05) kernel's domain
+    (2, 4096, 4096, 10, False, "f16", "f16"),
+    (1, 1000, 77, 20, False, "f16", "f32"),
+    (1, 300, 300, 4, True, "f16", "f32"),
+    (2, 257, 129, 3, False, "bf16", "f32"),
+    (1, 640, 640, 2, True, "bf16", "f16"),
+    (3, 1, 2, 1, False, "f16", "f32"),
+]
+
+
+@pytest.mark.parametrize("kernel", ["tc", "mma"])
+@pytest.mark.parametrize("B,Tq,Tk,heads,causal,dt,out", KERNEL_CASES)
+def test_attention_kernel_variants(orc, cuda_ok, monkeypatch, kernel, B, Tq, Tk, heads, causal, dt, out):
+    """Both attention kernels (SDVK_ATTN_KERNEL=tc: tcgen05/TMEM; =mma: warp-level) against fp64."""
+    monkeypatch.setenv("SDVK_ATTN_KERNEL", kernel)
+    C = heads * 64
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16}[dt]
+    qt, kt, vt = (dev(orc.normal_f32(5, i, (B, T, C))).to(tdt) for i, T in enumerate((Tq, Tk, Tk)))
+    q, k, v = (t.float().cpu().numpy() for t in (qt, kt, vt))
+    o = torch_ops.attention(qt, kt, vt, heads, causal=causal,
+                            out_dtype=torch.float32 if out == "f32" else torch.float16)
+    got = host(o).astype(np.float64)
+    rows = np.arange(Tq) if (causal or Tq <= 256) else np.sort(
+        np.random.default_rng(1).choice(Tq, size=256, replace=False))
+    ref = orc.attn_f64(q, k, v, heads, True) if causal else orc.attn_f64(q[:, rows], k, v, heads, False)
+    check_attn(orc, f"attn[{kernel}] B{B} Tq{Tq} Tk{Tk} h{heads} causal={causal} {dt}->{out}", got[:, rows],
+               ref if not causal else ref[:, rows], dt)
