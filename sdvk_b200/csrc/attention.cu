@@ -55,11 +55,14 @@ int make_attn_map(CUtensorMap* m, int dtype, const void* base, uint32_t T, uint3
 }
 
 // The tensor-core kernel takes head dim 64, 16-bit Q/K/V, a positive scale, and TMA-legal layouts
-// (16-byte aligned bases and strides) with an output that takes 16-byte vector stores.
-// SDVK_ATTN_KERNEL=mma forces the warp-level kernel (attention.cuh).
+// (16-byte aligned bases and strides) with an output that takes 16-byte vector stores.  It is
+// chosen when the keys span more than one 128-key tile; a single tile (the 77-token
+// cross-attention) runs faster on the warp-level kernel (attention.cuh), whose CTAs are smaller.
+// SDVK_ATTN_KERNEL=mma or =tc forces one of them (tc only where eligible).
 bool tc_eligible(const sdvk_attn_desc& d) {
     const char* e = getenv("SDVK_ATTN_KERNEL");
     if (e && e[0] == 'm') return false;
+    if (!(e && e[0] == 't') && d.Tk <= 128) return false;
     const uint64_t es = 2, eo = d.o_dtype == SDVK_F32 ? 4 : 2;
     auto s16 = [](uint64_t bytes) { return bytes % 16 == 0 && bytes < (1ull << 40); };
     return (d.dtype == SDVK_F16 || d.dtype == SDVK_BF16) && d.hd == 64 && d.scale > 0.0f && d.Tk > 0 &&

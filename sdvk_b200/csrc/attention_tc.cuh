@@ -5,20 +5,25 @@
 // CTA = 128 query rows of one (batch, head).  The key/value sequence streams through shared memory
 // in 128-key tiles loaded by TMA; tile t goes to softmax group t % 2, so two groups of 128 threads
 // work on alternate tiles while the tensor core serves the other one:
-//   warp 8     TMA: the Q tile once, then K/V tiles into a 4-stage ring
-//   warp 9     TMEM allocation and the MMA issuer (one thread) (warps 10-11 only hold registers back):
+//   warp 8     TMA: the Q tile once, then K tiles into a 5-stage ring
+//   warp 10    TMA: V tiles into a 7-stage ring (a K tile is free once S is computed, a V tile only
+//              after P.V, so the two rings are separate to keep both far enough ahead)
+//   warp 9     TMEM allocation and the MMA issuer (one thread) (warp 11 only holds registers back):
 //                S_g = Q . K_t^T            (M 128, N 128, K 64; A and B from shared memory)
 //                O_g += P_g . V_t           (M 128, N 64, K 128; A = P from tensor memory)
 //   warps 0-3  softmax group A (even tiles), warps 4-7 group B (odd tiles): thread = one query row
 //              = one TMEM lane.  It reads its row of S from TMEM, applies the mask and the online
 //              softmax (exp2 domain), writes P as 16-bit values back over S in TMEM, and rescales
 //              its O row in TMEM only when the running maximum grew by more than 2^8.
-// TMEM columns: S_A [0,128), S_B [128,256), O_A [256,320), O_B [320,384).
+// S is triple-buffered (tile t in buffer t % 3), so the MMA computes S for the next tile of a group
+// while that group is still turning its current S into P: a group waits for the tensor core only
+// when the tensor core is behind.
+// TMEM columns: S buffers [0,128), [128,256), [256,384); O_A [384,448), O_B [448,512).
 // At the end the two groups merge (O_A, m_A, l_A) and (O_B, m_B, l_B) row by row, normalise by
 // 1/l (0 for a row that saw no key, as the reference) and store O with vector stores.
 // Registers: 384 threads launch with 168 each (64512).  The control warpgroup (warps 8-11) drops to
-// 56 and the two softmax warpgroups rise to 224, which holds a full 128-column row of S in
-// registers: 2 x 128 x 224 + 128 x 56 = 64512, exactly the launch's pool.
+// 72 and the two softmax warpgroups rise to 216, which holds a full 128-column row of S in
+// registers: 2 x 128 x 216 + 128 x 72 = 64512, exactly the launch's pool.
 // Every wait is bounded by p.timeout_ns: on expiry the kernel records kErrTimeout, drains what it
 // issued and frees TMEM.
 #pragma once
@@ -59,20 +64,21 @@ struct TcAttnCfg {
     static constexpr int kBM = 128;  // query rows per CTA
     static constexpr int kBN = 128;  // keys per tile
     static constexpr int kHD = 64;
-    static constexpr int kStages = 4;
+    static constexpr int kKStages = 5, kVStages = 7;
     static constexpr int kTileBytes = kBN * kHD * 2;  // 16 KB (K or V tile; also the Q tile)
     static constexpr int kOffQ = 0;
-    static constexpr int kOffKV = kOffQ + kTileBytes;
-    static constexpr int kOffBar = kOffKV + kStages * 2 * kTileBytes;
-    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 1;
+    static constexpr int kOffK = kOffQ + kTileBytes;
+    static constexpr int kOffV = kOffK + kKStages * kTileBytes;
+    static constexpr int kOffBar = kOffV + kVStages * kTileBytes;
+    static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 2 + 1;
     static constexpr int kOffX = kOffBar + kNumBars * 8 + 8;  // TMEM slot + per-row (m, l) exchange
     static constexpr int kSmemBytes = kOffX + 4 * kBM * 4 + 1024;
     static constexpr int kThreads = 384;
-    static constexpr uint32_t kRegsSoftmax = 224, kRegsControl = 56;
+    static constexpr uint32_t kRegsSoftmax = 216, kRegsControl = 72;
     static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsControl <= kThreads * 168, "register split exceeds the pool");
-    // TMEM columns of group g's S (and P) and O
-    static __device__ __forceinline__ uint32_t col_s(uint32_t g) { return g * 128u; }
-    static __device__ __forceinline__ uint32_t col_o(uint32_t g) { return 256u + g * 64u; }
+    // TMEM columns of S (and P) buffer b, and of group g's O
+    static __device__ __forceinline__ uint32_t col_s(uint32_t b) { return b * 128u; }
+    static __device__ __forceinline__ uint32_t col_o(uint32_t g) { return 384u + g * 64u; }
 };
 
 template <class T, class TO>
@@ -83,13 +89,17 @@ __global__ void __launch_bounds__(384, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem + Cfg::kOffQ;
-    uint8_t* sKV = smem + Cfg::kOffKV;  // stage s: K at s*32K, V at s*32K + 16K
+    uint8_t* sK = smem + Cfg::kOffK;
+    uint8_t* sV = smem + Cfg::kOffV;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = q_full + 1;
-    uint64_t* kv_empty = kv_full + Cfg::kStages;
-    uint64_t* s_full = kv_empty + Cfg::kStages;
-    uint64_t* p_full = s_full + 2;
+    uint64_t* k_full = q_full + 1;
+    uint64_t* k_empty = k_full + Cfg::kKStages;
+    uint64_t* v_full = k_empty + Cfg::kKStages;
+    uint64_t* v_empty = v_full + Cfg::kVStages;
+    // k_empty[s] completing for tile t also says S(t) is in TMEM, and v_empty[s] completing says
+    // P(t).V is in O: the softmax groups wait on those instead of on extra commits.
+    uint64_t* p_full = v_empty + Cfg::kVStages;  // per group
     uint64_t* o_final = p_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 1);
     float* xm = reinterpret_cast<float*>(smem + Cfg::kOffX);  // [2][128] running maxima
@@ -103,14 +113,15 @@ __global__ void __launch_bounds__(384, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < Cfg::kStages; ++i) {
-            mbar_init(&kv_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+        for (int i = 0; i < Cfg::kKStages; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
         }
-        for (int g = 0; g < 2; ++g) {
-            mbar_init(&s_full[g], 1);
-            mbar_init(&p_full[g], 4);  // one arrival per softmax warp
+        for (int i = 0; i < Cfg::kVStages; ++i) {
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
         }
+        for (int g = 0; g < 2; ++g) mbar_init(&p_full[g], 4);  // one arrival per softmax warp
         mbar_init(o_final, 1);
         fence_mbar_init();
     }
@@ -135,65 +146,85 @@ __global__ void __launch_bounds__(384, 1)
 
     if (warp >= 8) {
         regs_decrease<Cfg::kRegsControl>();
-        if (warp == 8 && lane == 0) {
-            // -------------------------------------------------------------- TMA producer
-            mbar_arrive_expect_tx(q_full, Cfg::kTileBytes);
-            tma_load_4d(sQ, &tmQ, q_full, 0, (int)q0, (int)head, (int)b);
+        if ((warp == 8 || warp == 10) && lane == 0) {
+            // -------------------------------------------------------------- TMA producers (K; V)
+            const bool is_k = warp == 8;
+            const uint32_t nst = is_k ? Cfg::kKStages : Cfg::kVStages;
+            uint64_t* full = is_k ? k_full : v_full;
+            uint64_t* empty = is_k ? k_empty : v_empty;
+            uint8_t* ring = is_k ? sK : sV;
+            const CUtensorMap* map = is_k ? &tmK : &tmV;
+            if (is_k) {
+                mbar_arrive_expect_tx(q_full, Cfg::kTileBytes);
+                tma_load_4d(sQ, &tmQ, q_full, 0, (int)q0, (int)head, (int)b);
+            }
             uint32_t t = 0;
             for (; t < n_kv; ++t) {
-                const uint32_t s = t % Cfg::kStages, ph = (t / Cfg::kStages) & 1;
-                if (!mbar_wait(&kv_empty[s], ph ^ 1, p.timeout_ns)) {
+                const uint32_t s = t % nst, ph = (t / nst) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, p.timeout_ns)) {
                     fail();
                     break;
                 }
-                uint8_t* dst = sKV + s * 2 * Cfg::kTileBytes;
-                mbar_arrive_expect_tx(&kv_full[s], 2 * Cfg::kTileBytes);
-                tma_load_4d(dst, &tmK, &kv_full[s], 0, (int)(t * Cfg::kBN), (int)head, (int)b);
-                tma_load_4d(dst + Cfg::kTileBytes, &tmV, &kv_full[s], 0, (int)(t * Cfg::kBN), (int)head, (int)b);
+                mbar_arrive_expect_tx(&full[s], Cfg::kTileBytes);
+                tma_load_4d(ring + s * Cfg::kTileBytes, map, &full[s], 0, (int)(t * Cfg::kBN), (int)head, (int)b);
             }
             // drain: every load issued has landed before the CTA can exit
-            if (!mbar_wait(q_full, 0, p.timeout_ns)) fail();
-            for (uint32_t i = (t > Cfg::kStages ? t - Cfg::kStages : 0); i < t; ++i)
-                if (!mbar_wait(&kv_full[i % Cfg::kStages], (i / Cfg::kStages) & 1, p.timeout_ns)) fail();
+            if (is_k && !mbar_wait(q_full, 0, p.timeout_ns)) fail();
+            for (uint32_t i = (t > nst ? t - nst : 0); i < t; ++i)
+                if (!mbar_wait(&full[i % nst], (i / nst) & 1, p.timeout_ns)) fail();
         } else if (warp == 9 && lane == 0) {
             // -------------------------------------------------------------- MMA issuer
             constexpr uint32_t fmt = OperandTraits<T>::kFmt;
             constexpr uint32_t idesc_s = make_idesc(fmt, fmt, 0, 0, Cfg::kBM, Cfg::kBN);
             constexpr uint32_t idesc_o = make_idesc(fmt, fmt, 0, 1, Cfg::kBM, Cfg::kHD);
-            const uint32_t q_addr = smem_u32(sQ);
-            auto issue_s = [&](uint32_t t) -> bool {
-                const uint32_t s = t % Cfg::kStages;
-                if (!mbar_wait(&kv_full[s], (t / Cfg::kStages) & 1, p.timeout_ns)) return false;
+            // Descriptors are built once; a K step advances the start-address field (16-byte
+            // units) by 2 for K-major Q/K (32 bytes) and by 128 for MN-major V (16 rows of 128 B).
+            const uint64_t q_desc = smem_desc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t k_desc0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
+            const uint64_t v_desc0 = smem_desc_sw128(smem_u32(sV), Cfg::kTileBytes, 1024);
+            constexpr uint64_t kTileDesc = Cfg::kTileBytes >> 4;
+            // The issuing thread keeps no divisions on its path: stage indices and phases advance
+            // incrementally (every cycle it spends here the tensor pipe may sit idle).
+            uint32_t ks = 0, kph = 0;  // K stage / phase of the next S to issue
+            uint32_t vs = 0, vph = 0;  // V stage / phase of tile t
+            auto issue_s = [&](uint32_t buf) -> bool {
+                if (!mbar_spin_wait(&k_full[ks], kph, p.timeout_ns)) return false;
                 tc_fence_after();
-                const uint32_t k_addr = smem_u32(sKV + s * 2 * Cfg::kTileBytes);
+                const uint64_t k_desc = k_desc0 + ks * kTileDesc;
+                const uint32_t d = tmem + Cfg::col_s(buf);
 #pragma unroll
                 for (int kk = 0; kk < Cfg::kHD / 16; ++kk)
-                    mma_f16(tmem + Cfg::col_s(t & 1), smem_desc_sw128(q_addr + kk * 32, 16, 1024),
-                            smem_desc_sw128(k_addr + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-                mma_commit(&s_full[t & 1]);
+                    mma_f16(d, q_desc + 2 * kk, k_desc + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+                mma_commit(&k_empty[ks]);
+                if (++ks == Cfg::kKStages) ks = 0, kph ^= 1;
                 return true;
             };
             if (!mbar_wait(q_full, 0, p.timeout_ns)) fail();
-            for (uint32_t t = 0; ok && t < n_kv && t < 2; ++t)
+            for (uint32_t t = 0; ok && t < n_kv && t < 3; ++t)
                 if (!issue_s(t)) fail();
+            uint32_t sb = 0;  // S buffer of tile t (t % 3)
             for (uint32_t t = 0; ok && t < n_kv; ++t) {
                 const uint32_t g = t & 1, i = t >> 1;
-                if (!mbar_wait(&p_full[g], i & 1, p.timeout_ns)) {
+                if (!mbar_spin_wait(&p_full[g], i & 1, p.timeout_ns) ||
+                    !mbar_spin_wait(&v_full[vs], vph, p.timeout_ns)) {
                     fail();
                     break;
                 }
                 tc_fence_after();
-                const uint32_t v_addr = smem_u32(sKV + (t % Cfg::kStages) * 2 * Cfg::kTileBytes + Cfg::kTileBytes);
+                const uint64_t v_desc = v_desc0 + vs * kTileDesc;
+                const uint32_t d = tmem + Cfg::col_o(g), a = tmem + Cfg::col_s(sb);
 #pragma unroll
                 for (int kk = 0; kk < Cfg::kBN / 16; ++kk)
-                    mma_f16_ts(tmem + Cfg::col_o(g), tmem + Cfg::col_s(g) + kk * 8,
-                               smem_desc_sw128(v_addr + kk * 2048, Cfg::kTileBytes, 1024), idesc_o,
-                               (i > 0 || kk > 0) ? 1u : 0u);
-                mma_commit(&kv_empty[t % Cfg::kStages]);
-                if (t + 2 < n_kv && !issue_s(t + 2)) {
+                    mma_f16_ts(d, a + kk * 8, v_desc + 128 * kk, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&v_empty[vs]);
+                if (++vs == Cfg::kVStages) vs = 0, vph ^= 1;
+                // S(t + 3) reuses this buffer: the tensor core runs in issue order, so P(t) is read
+                // by the P.V above before S(t + 3) overwrites it.
+                if (t + 3 < n_kv && !issue_s(sb)) {
                     fail();
                     break;
                 }
+                sb = sb == 2 ? 0 : sb + 1;
             }
             mma_commit(o_final);
             if (!mbar_wait(o_final, 0, p.timeout_ns)) fail();
@@ -208,7 +239,11 @@ __global__ void __launch_bounds__(384, 1)
         const float sl = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.0f;
         for (uint32_t t = g, i = 0; t < n_kv; t += 2, ++i) {
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[g], i & 1, p.timeout_ns))) {
+            const uint32_t sb = t % 3;
+            // S(t) has landed when K stage t % kKStages is released (at most that phase is pending:
+            // S(t + kKStages) needs P(t + 2) of this group first).
+            if (!__all_sync(0xffffffffu, mbar_wait(&k_empty[t % Cfg::kKStages], (t / Cfg::kKStages) & 1,
+                                                   p.timeout_ns))) {
                 fail();
                 break;
             }
@@ -216,7 +251,7 @@ __global__ void __launch_bounds__(384, 1)
             uint32_t sr[128];
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-                tmem_ld_32x32b_x32(tmem + lane_bits + Cfg::col_s(g) + c * 32,
+                tmem_ld_32x32b_x32(tmem + lane_bits + Cfg::col_s(sb) + c * 32,
                                    *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
             tmem_wait_ld();
             float* s = reinterpret_cast<float*>(sr);
@@ -228,16 +263,30 @@ __global__ void __launch_bounds__(384, 1)
                     if (key >= p.Tk || (p.causal && key > qrow)) s[j] = -INFINITY;
                 }
             }
-            float mx = s[0];
+            float m8[8];  // eight independent chains instead of one 128-long dependency chain
 #pragma unroll
-            for (int j = 1; j < 128; ++j) mx = fmaxf(mx, s[j]);
+            for (int c = 0; c < 8; ++c) m8[c] = s[c];
+#pragma unroll
+            for (int j = 8; j < 128; ++j) m8[j & 7] = fmaxf(m8[j & 7], s[j]);
+            const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             const float m_new = fmaxf(m_run, mx * sl);
             // Rescale only when the maximum grew by more than 2^8; P values up to 2^8 are exact
             // enough in 16 bits and the final 1/l uses the same stale maximum.
             const bool need = m_new - m_run > 8.0f;  // false for NaN (row still fully masked)
             if (__any_sync(0xffffffffu, need)) {
                 const float f = need ? ex2_approx(m_run - m_new) : 1.0f;
+                // O holds this group's P.V up to its previous tile t - 2, which may still be running
+                // (S(t) can complete before it); its V stage's release says it is done.  Only that
+                // phase can be pending: P.V(t - 2 + kVStages) needs P(t + 2) of this group first.
+                const uint32_t pt = t - 2;
+                if (i > 0 && !__all_sync(0xffffffffu, mbar_wait(&v_empty[pt % Cfg::kVStages],
+                                                                (pt / Cfg::kVStages) & 1, p.timeout_ns))) {
+                    fail();
+                    break;
+                }
                 if (i > 0) {
+                    tc_fence_after();
                     uint32_t o[32];
 #pragma unroll
                     for (int c = 0; c < 2; ++c) {
@@ -253,7 +302,7 @@ __global__ void __launch_bounds__(384, 1)
                 if (need) m_run = m_new;
             }
             const float mb = (m_run == -INFINITY) ? 0.0f : m_run;
-            float sum = 0.0f;
+            float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int h = 0; h < 2; ++h) {  // P over S: 16-bit pairs, columns [32h, 32h + 32)
                 uint32_t pk[32];
@@ -262,11 +311,11 @@ __global__ void __launch_bounds__(384, 1)
                     const float p0 = ex2_approx(fmaf(s[64 * h + 2 * j], sl, -mb));
                     const float p1 = ex2_approx(fmaf(s[64 * h + 2 * j + 1], sl, -mb));
                     pk[j] = Half16Pack<T>::pack(p0, p1);
-                    sum += p0 + p1;
+                    sum8[j & 7] += p0 + p1;
                 }
-                tmem_st_32x32b_x32(tmem + lane_bits + Cfg::col_s(g) + 32 * h, pk);
+                tmem_st_32x32b_x32(tmem + lane_bits + Cfg::col_s(sb) + 32 * h, pk);
             }
-            l_run += sum;
+            l_run += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
