@@ -172,8 +172,10 @@ __global__ void __launch_bounds__(384, 1)
             if (is_k && !mbar_wait(q_full, 0, p.timeout_ns)) fail();
             for (uint32_t i = (t > nst ? t - nst : 0); i < t; ++i)
                 if (!mbar_wait(&full[i % nst], (i / nst) & 1, p.timeout_ns)) fail();
-        } else if (warp == 9 && lane == 0) {
+        } else if (warp == 9) {
             // -------------------------------------------------------------- MMA issuer
+            // The whole warp runs the loop (warp-uniform control flow and operands); one elected
+            // lane issues each tcgen05 instruction.
             constexpr uint32_t fmt = OperandTraits<T>::kFmt;
             constexpr uint32_t idesc_s = make_idesc(fmt, fmt, 0, 0, Cfg::kBM, Cfg::kBN);
             constexpr uint32_t idesc_o = make_idesc(fmt, fmt, 0, 1, Cfg::kBM, Cfg::kHD);
@@ -188,35 +190,41 @@ __global__ void __launch_bounds__(384, 1)
             uint32_t ks = 0, kph = 0;  // K stage / phase of the next S to issue
             uint32_t vs = 0, vph = 0;  // V stage / phase of tile t
             auto issue_s = [&](uint32_t buf) -> bool {
-                if (!mbar_spin_wait(&k_full[ks], kph, p.timeout_ns)) return false;
+                if (!__all_sync(0xffffffffu, mbar_spin_wait(&k_full[ks], kph, p.timeout_ns))) return false;
                 tc_fence_after();
                 const uint64_t k_desc = k_desc0 + ks * kTileDesc;
                 const uint32_t d = tmem + Cfg::col_s(buf);
+                if (elect_one()) {
 #pragma unroll
-                for (int kk = 0; kk < Cfg::kHD / 16; ++kk)
-                    mma_f16(d, q_desc + 2 * kk, k_desc + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
-                mma_commit(&k_empty[ks]);
+                    for (int kk = 0; kk < Cfg::kHD / 16; ++kk)
+                        mma_f16(d, q_desc + 2 * kk, k_desc + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+                    mma_commit(&k_empty[ks]);
+                }
+                __syncwarp();
                 if (++ks == Cfg::kKStages) ks = 0, kph ^= 1;
                 return true;
             };
-            if (!mbar_wait(q_full, 0, p.timeout_ns)) fail();
+            if (!__all_sync(0xffffffffu, mbar_wait(q_full, 0, p.timeout_ns))) fail();
             for (uint32_t t = 0; ok && t < n_kv && t < 3; ++t)
                 if (!issue_s(t)) fail();
             uint32_t sb = 0;  // S buffer of tile t (t % 3)
             for (uint32_t t = 0; ok && t < n_kv; ++t) {
                 const uint32_t g = t & 1, i = t >> 1;
-                if (!mbar_spin_wait(&p_full[g], i & 1, p.timeout_ns) ||
-                    !mbar_spin_wait(&v_full[vs], vph, p.timeout_ns)) {
+                if (!__all_sync(0xffffffffu, mbar_spin_wait(&p_full[g], i & 1, p.timeout_ns) &&
+                                                 mbar_spin_wait(&v_full[vs], vph, p.timeout_ns))) {
                     fail();
                     break;
                 }
                 tc_fence_after();
                 const uint64_t v_desc = v_desc0 + vs * kTileDesc;
                 const uint32_t d = tmem + Cfg::col_o(g), a = tmem + Cfg::col_s(sb);
+                if (elect_one()) {
 #pragma unroll
-                for (int kk = 0; kk < Cfg::kBN / 16; ++kk)
-                    mma_f16_ts(d, a + kk * 8, v_desc + 128 * kk, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
-                mma_commit(&v_empty[vs]);
+                    for (int kk = 0; kk < Cfg::kBN / 16; ++kk)
+                        mma_f16_ts(d, a + kk * 8, v_desc + 128 * kk, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+                    mma_commit(&v_empty[vs]);
+                }
+                __syncwarp();
                 if (++vs == Cfg::kVStages) vs = 0, vph ^= 1;
                 // S(t + 3) reuses this buffer: the tensor core runs in issue order, so P(t) is read
                 // by the P.V above before S(t + 3) overwrites it.
@@ -226,8 +234,9 @@ __global__ void __launch_bounds__(384, 1)
                 }
                 sb = sb == 2 ? 0 : sb + 1;
             }
-            mma_commit(o_final);
-            if (!mbar_wait(o_final, 0, p.timeout_ns)) fail();
+            if (elect_one()) mma_commit(o_final);
+            __syncwarp();
+            if (!__all_sync(0xffffffffu, mbar_wait(o_final, 0, p.timeout_ns))) fail();
         }
     } else {
         // ------------------------------------------------------------------ softmax groups
@@ -263,13 +272,13 @@ __global__ void __launch_bounds__(384, 1)
                     if (key >= p.Tk || (p.causal && key > qrow)) s[j] = -INFINITY;
                 }
             }
-            float m8[8];  // eight independent chains instead of one 128-long dependency chain
+            // The softmax warps share each SMSP's issue slots with the MMA-issuing warp, so their
+            // instruction count is what paces the tensor core: three-input max, packed f32x2
+            // FMA/add, one convert per pair.
+            float m4[4] = {s[0], s[1], s[2], s[3]};  // four independent chains
 #pragma unroll
-            for (int c = 0; c < 8; ++c) m8[c] = s[c];
-#pragma unroll
-            for (int j = 8; j < 128; ++j) m8[j & 7] = fmaxf(m8[j & 7], s[j]);
-            const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            for (int j = 4; j < 128; j += 2) m4[(j >> 1) & 3] = fmax3(m4[(j >> 1) & 3], s[j], s[j + 1]);
+            const float mx = fmaxf(fmax3(m4[0], m4[1], m4[2]), m4[3]);
             const float m_new = fmaxf(m_run, mx * sl);
             // Rescale only when the maximum grew by more than 2^8; P values up to 2^8 are exact
             // enough in 16 bits and the final 1/l uses the same stale maximum.
@@ -302,20 +311,24 @@ __global__ void __launch_bounds__(384, 1)
                 if (need) m_run = m_new;
             }
             const float mb = (m_run == -INFINITY) ? 0.0f : m_run;
-            float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            const uint64_t sl2 = f2_pack(sl, sl), nmb2 = f2_pack(-mb, -mb);
+            uint64_t sum2[4] = {0, 0, 0, 0};  // packed pairs of partial sums (0 bits = 0.0f, 0.0f)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {  // P over S: 16-bit pairs, columns [32h, 32h + 32)
                 uint32_t pk[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const float p0 = ex2_approx(fmaf(s[64 * h + 2 * j], sl, -mb));
-                    const float p1 = ex2_approx(fmaf(s[64 * h + 2 * j + 1], sl, -mb));
+                    float x0, x1;
+                    f2_unpack(ffma2(f2_pack(s[64 * h + 2 * j], s[64 * h + 2 * j + 1]), sl2, nmb2), x0, x1);
+                    const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
                     pk[j] = Half16Pack<T>::pack(p0, p1);
-                    sum8[j & 7] += p0 + p1;
+                    sum2[j & 3] = fadd2(sum2[j & 3], f2_pack(p0, p1));
                 }
                 tmem_st_32x32b_x32(tmem + lane_bits + Cfg::col_s(sb) + 32 * h, pk);
             }
-            l_run += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+            float s_lo, s_hi;
+            f2_unpack(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), s_lo, s_hi);
+            l_run += s_lo + s_hi;
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
