@@ -184,48 +184,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (even CTA)
-        if (leader && lane == 0) {
+        // The whole warp runs the loop (warp-uniform control flow and operands, no divisions on
+        // the path); one elected lane issues each tcgen05 instruction.  Every cycle this warp
+        // spends between MMAs can be tensor-pipe idle time.
+        if (leader) {
             constexpr uint32_t idesc =
                 make_idesc(OperandTraits<TA>::kFmt, OperandTraits<TA>::kFmt, NN ? 1 : 0, 0, 2 * Cfg::kBM, Cfg::kBNP);
-            uint32_t it = 0;
+            // Operand descriptors of stage 0; a stage adds kStageBytes, a K step of kUmmaK elements
+            // adds 32 bytes (K-major) or kUmmaK rows of 128 bytes (MN-major activations).
+            const uint32_t a0 = smem_u32(sStage);
+            uint64_t adesc0;
+            if constexpr (!NN) adesc0 = smem_desc_sw128(a0, 16, 1024);
+            else if constexpr (!OperandTraits<TA>::kTf32) adesc0 = smem_desc_sw128(a0, Cfg::kBK * 128, 1024);
+            else adesc0 = smem_desc(a0, Cfg::kBK * 128, 512, kLayoutSw128Base32);
+            const uint64_t bdesc0 = smem_desc_sw128(a0 + Cfg::kABytes, 16, 1024);
+            constexpr uint64_t kStageDesc = Cfg::kStageBytes >> 4;
+            constexpr uint64_t kAStep = NN ? (Cfg::kUmmaK * 128) >> 4 : 2;
+            uint32_t s = 0, ph = 0;
             for (uint32_t i = 0; ok && i < my_tiles; ++i) {
-                const uint32_t acc = i % Cfg::kAcc, aph = (i / Cfg::kAcc) & 1;
-                if (!mbar_wait(&acc_empty[acc], aph ^ 1, p.timeout_ns)) {
+                const uint32_t acc = i & (Cfg::kAcc - 1), aph = (i / Cfg::kAcc) & 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[acc], aph ^ 1, p.timeout_ns))) {
                     fail();
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * Cfg::kBNP;
-                for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
-                    const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
-                    if (!mbar_wait(&full[s], ph, p.timeout_ns)) {
+                for (uint32_t ks = 0; ks < p.k_stages; ++ks) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.timeout_ns))) {
                         fail();
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sStage + s * Cfg::kStageBytes);
-                    const uint32_t b_addr = a_addr + Cfg::kABytes;
+                    const uint64_t ad = adesc0 + s * kStageDesc, bd = bdesc0 + s * kStageDesc;
+                    if (elect_one()) {
 #pragma unroll
-                    for (int kk = 0; kk < Cfg::kBK / Cfg::kUmmaK; ++kk) {
-                        uint64_t adesc;
-                        if constexpr (!NN)
-                            adesc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-                        else if constexpr (!OperandTraits<TA>::kTf32)
-                            adesc = smem_desc_sw128(a_addr + kk * Cfg::kUmmaK * 128, Cfg::kBK * 128, 1024);
-                        else
-                            adesc = smem_desc(a_addr + kk * Cfg::kUmmaK * 128, Cfg::kBK * 128, 512, kLayoutSw128Base32);
-                        const uint64_t bdesc = smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-                        const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
-                        if constexpr (OperandTraits<TA>::kTf32) mma_tf32_pair(d_tmem, adesc, bdesc, idesc, accum);
-                        else mma_f16_pair(d_tmem, adesc, bdesc, idesc, accum);
+                        for (int kk = 0; kk < Cfg::kBK / Cfg::kUmmaK; ++kk) {
+                            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
+                            if constexpr (OperandTraits<TA>::kTf32)
+                                mma_tf32_pair(d_tmem, ad + kk * kAStep, bd + 2 * kk, idesc, accum);
+                            else mma_f16_pair(d_tmem, ad + kk * kAStep, bd + 2 * kk, idesc, accum);
+                        }
+                        mma_commit_pair_mc(&empty[s], 0x3);
                     }
-                    mma_commit_pair_mc(&empty[s], 0x3);
+                    __syncwarp();
+                    if (++s == Cfg::kS) s = 0, ph ^= 1;
                 }
                 if (!ok) break;
-                mma_commit_pair_mc(&acc_full[acc], 0x3);
+                if (elect_one()) mma_commit_pair_mc(&acc_full[acc], 0x3);
+                __syncwarp();
             }
-            mma_commit_pair(mma_done);
-            if (!mbar_wait(mma_done, 0, p.timeout_ns)) fail();
+            if (elect_one()) mma_commit_pair(mma_done);
+            __syncwarp();
+            if (!__all_sync(0xffffffffu, mbar_wait(mma_done, 0, p.timeout_ns))) fail();
         }
     } else if (warp >= 4 && warp < 12) {
         // ------------------------------------------------------------ dequantisers (both CTAs)
