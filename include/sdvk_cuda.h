@@ -114,6 +114,7 @@ SDVK_API int sdvk_synchronize(sdvk_ctx* ctx);
  *   "gemm_nt_q8_v_b", "gemm_nt_q8_v_bm128_b"  bufs {A, Bq, C, S, bias}  push Pg
  *   "gemm_nn_q8", "gemm_nn_q8_v"        bufs {Aq, B, C, S}        push Pg
  *   "fused_attn", "fused_attn_tiled"    bufs {Q, K, V, O}         push FaPush (36 B)
+ *   "layernorm_fwd"                     bufs {X, gamma, beta, Y}  push {rows, d, eps, affine} (16 B)
  * Pg = {M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, pad} (sdvkgen.cpp:901-903);
  * FaPush = {Tq, Tk, C, heads, hd, causal, pad0, pad1, scale} (fused_attn.cpp:15-26).
  * The grid (gx, gy, gz) the caller computed for the Vulkan tiling is accepted and ignored: each
@@ -171,6 +172,48 @@ typedef struct sdvk_attn_desc {
     int causal;
 } sdvk_attn_desc;
 SDVK_API int sdvk_attention(sdvk_ctx* ctx, const sdvk_attn_desc* desc);
+
+/* ---- the transformer block and its non-GEMM operators --------------------------------------- */
+/* LayerNorm over the last dim (layernorm_fwd.comp, dispatched by layernorm(), sdvkgen.cpp:1094-1103):
+ * y[r][j] = (x[r][j] - mean_r) / sqrt(var_r + eps) * gamma[j] + beta[j], two-pass mean/variance.
+ * x fp32 [rows][ldx]; y F32 or F16 [rows][ldy]; gamma/beta fp32 [d] or NULL (1 / 0).
+ * Requirements: d, ldx, ldy multiples of 4, d <= 3072, 16-byte aligned bases. */
+SDVK_API int sdvk_layernorm(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, void* y, int y_dtype,
+                   uint32_t rows, uint32_t d, uint64_t ldx, uint64_t ldy, float eps);
+/* diffusers GEGLU on the ff.net.0.proj output (geglu(), sdvkgen.cpp:1710-1720): f16 h [rows][ldh]
+ * holds [a | gate] of width 2F; y[r][j] = a[r][j] * gelu_erf(gate[r][j]), f16 [rows][ldy].
+ * Requirements: F, ldh, ldy multiples of 8, 16-byte aligned bases. */
+SDVK_API int sdvk_geglu(sdvk_ctx* ctx, const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint64_t ldy);
+
+/* One Q8_0 linear layer: int8 weight [N][K] (row stride K), fp32 scale per 32 weights, optional
+ * fp32 bias [N] (the loader's split layout, Gguf.cpp:559-583). */
+typedef struct sdvk_q8_linear {
+    const int8_t* q;
+    const float* s;
+    const float* bias;
+} sdvk_q8_linear;
+
+/* One SDXL BasicTransformerBlock (spatialTransformer's layer body, sdvkgen.cpp:1739-1763) over
+ * `batch` images at once:
+ *   x += attn1(LN1(x));  x += attn2(LN2(x), ctx);  x += ff2(geglu(ff1(LN3(x))))
+ * where attnN = to_out(fusedAttention(to_q, to_k, to_v)) with heads of C/heads <= 64.
+ * x: fp32 [batch][T][C], updated in place.  ctx: [batch][Tctx][Cctx] in ctx_dtype (F16, BF16, F32).
+ * ff1 has 2*ff_inner rows ([a | gate]); ff2 has K = ff_inner.  Q/K/V (and attn2's K/V) run as one
+ * GEMM when their weights (and biases) lie back to back in memory.  eps <= 0 means 1e-5.
+ * The workspace (fp16 intermediates) is the caller's: sdvk_transformer_block_workspace() bytes,
+ * 256-byte aligned.  No counterpart exists as one call in the reference, which dispatches the same
+ * sequence kernel by kernel. */
+typedef struct sdvk_block_desc {
+    float* x;
+    const void* ctx;
+    int ctx_dtype;
+    uint32_t batch, T, C, heads, Tctx, Cctx, ff_inner;
+    const float *ln1_w, *ln1_b, *ln2_w, *ln2_b, *ln3_w, *ln3_b;
+    sdvk_q8_linear q, k, v, o, q2, k2, v2, o2, ff1, ff2;
+    float eps;
+} sdvk_block_desc;
+SDVK_API uint64_t sdvk_transformer_block_workspace(const sdvk_block_desc* desc);
+SDVK_API int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, void* workspace, uint64_t workspace_bytes);
 
 /* NaN/Inf check of n fp32 or f16 values (the reference aborts on a non-finite UNet output,
  * sdvkgen.cpp:3819-3823): returns SDVK_E_NOT_FINITE if any value is not finite. */

@@ -278,6 +278,65 @@ def gelu_erf_shader(x):
     return y
 
 
+def _gelu64(x):
+    from scipy.special import erf
+
+    return 0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))
+
+
+def block_f64(x, ctx, heads, W, rows=None, eps=1e-5):
+    """fp64 truth of one BasicTransformerBlock (spatialTransformer's layer body,
+    src/Modules/Diffusion/sdvkgen.cpp:1739-1763; geglu :1710-1720; crossAttention :1283-1290) on
+    x [B, T, C] and ctx [B, Tctx, Cctx]: LN1 -> to_q/k/v -> attention -> to_out (+bias) -> +res,
+    LN2 -> cross-attention against ctx -> +res, LN3 -> GEGLU (gate = second half) -> ff.net.2 -> +res.
+    W maps ln{1,2,3}_{w,b} to fp32 arrays and q,k,v,o,q2,k2,v2,o2,ff1,ff2 to (int8, scales, bias|None).
+    `rows` (query-token indices) limits the output rows; keys/values still cover every token.
+    Values pass between the fp64 stages as fp32 (the f64 kernels take fp32 operands)."""
+    B, T, C = x.shape
+    rows = np.arange(T) if rows is None else np.asarray(rows)
+    f32 = lambda a: np.ascontiguousarray(a, np.float32)
+    lin = lambda a, w: gemm_nt_q8_f64(f32(a), w[0], w[1], w[2])
+    out = np.empty((B, len(rows), C))
+    for b in range(B):
+        xb = np.asarray(x[b], np.float64)
+        n = layernorm_f64(xb, W["ln1_w"], W["ln1_b"], eps)
+        q, k, v = lin(n[rows], W["q"]), lin(n, W["k"]), lin(n, W["v"])
+        a = attn_f64(f32(q), f32(k), f32(v), heads)
+        x1 = xb[rows] + lin(a, W["o"])
+        n = layernorm_f64(x1, W["ln2_w"], W["ln2_b"], eps)
+        q, k, v = lin(n, W["q2"]), lin(ctx[b], W["k2"]), lin(ctx[b], W["v2"])
+        x2 = x1 + lin(attn_f64(f32(q), f32(k), f32(v), heads), W["o2"])
+        n = layernorm_f64(x2, W["ln3_w"], W["ln3_b"], eps)
+        g = lin(n, W["ff1"])
+        F = g.shape[1] // 2
+        out[b] = x2 + lin(g[:, :F] * _gelu64(g[:, F:]), W["ff2"])
+    return out
+
+
+def block_shader(x, ctx, heads, W, rows=None, eps=1e-5):
+    """The reference's own fp32 arithmetic for the same block, kernel by kernel as sdvkgen.cpp
+    dispatches it: layernorm_fwd, gemm_nt_q8_v(+bias), fusedAttention, unary_fwd erf-GELU, mul2, add2.
+    `rows` as in block_f64."""
+    B, T, C = x.shape
+    rows = np.arange(T) if rows is None else np.asarray(rows)
+    lin = lambda a, w: gemm_nt_q8_shader(np.ascontiguousarray(a, np.float32), w[0], w[1], w[2])
+    out = np.empty((B, len(rows), C), np.float32)
+    for b in range(B):
+        xb = np.ascontiguousarray(x[b], np.float32)
+        n = layernorm_shader(xb, W["ln1_w"], W["ln1_b"], eps)
+        q, k, v = lin(n[rows], W["q"]), lin(n, W["k"]), lin(n, W["v"])
+        a = fused_attention(q, k, v, len(rows), T, C, heads)
+        x1 = xb[rows] + lin(a, W["o"])
+        n = layernorm_shader(x1, W["ln2_w"], W["ln2_b"], eps)
+        q, k, v = lin(n, W["q2"]), lin(ctx[b], W["k2"]), lin(ctx[b], W["v2"])
+        x2 = x1 + lin(fused_attention(q, k, v, len(rows), k.shape[0], C, heads), W["o2"])
+        n = layernorm_shader(x2, W["ln3_w"], W["ln3_b"], eps)
+        g = lin(n, W["ff1"])
+        F = g.shape[1] // 2
+        out[b] = x2 + lin(np.ascontiguousarray(g[:, :F]) * gelu_erf_shader(np.ascontiguousarray(g[:, F:])), W["ff2"])
+    return out
+
+
 def num_threads() -> int:
     return lib().orc_num_threads()
 

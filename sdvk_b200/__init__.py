@@ -52,6 +52,28 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+class Q8Linear(ctypes.Structure):
+    """sdvk_q8_linear: int8 weight [N][K], fp32 scale per 32 weights, optional fp32 bias [N]."""
+
+    _fields_ = [("q", ctypes.c_void_p), ("s", ctypes.c_void_p), ("bias", ctypes.c_void_p)]
+
+
+class BlockDesc(ctypes.Structure):
+    """sdvk_block_desc: one SDXL BasicTransformerBlock (spatialTransformer's layer body)."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("ctx", ctypes.c_void_p), ("ctx_dtype", ctypes.c_int),
+        ("batch", ctypes.c_uint32), ("T", ctypes.c_uint32), ("C", ctypes.c_uint32), ("heads", ctypes.c_uint32),
+        ("Tctx", ctypes.c_uint32), ("Cctx", ctypes.c_uint32), ("ff_inner", ctypes.c_uint32),
+        ("ln1_w", ctypes.c_void_p), ("ln1_b", ctypes.c_void_p), ("ln2_w", ctypes.c_void_p),
+        ("ln2_b", ctypes.c_void_p), ("ln3_w", ctypes.c_void_p), ("ln3_b", ctypes.c_void_p),
+        ("q", Q8Linear), ("k", Q8Linear), ("v", Q8Linear), ("o", Q8Linear),
+        ("q2", Q8Linear), ("k2", Q8Linear), ("v2", Q8Linear), ("o2", Q8Linear),
+        ("ff1", Q8Linear), ("ff2", Q8Linear),
+        ("eps", ctypes.c_float),
+    ]
+
+
 # name -> (restype, argtypes) for every symbol include/sdvk_cuda.h declares
 _P, _U32, _U64, _I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
 SIGNATURES = {
@@ -86,6 +108,10 @@ SIGNATURES = {
                              _U64, _U64, _U64, _I]),
     "sdvk_attention": (_I, [_P, ctypes.POINTER(AttnDesc)]),
     "sdvk_check_finite": (_I, [_P, _P, _I, _U64]),
+    "sdvk_layernorm": (_I, [_P, _P, _P, _P, _P, _I, _U32, _U32, _U64, _U64, ctypes.c_float]),
+    "sdvk_geglu": (_I, [_P, _P, _P, _U32, _U32, _U64, _U64]),
+    "sdvk_transformer_block_workspace": (_U64, [ctypes.POINTER(BlockDesc)]),
+    "sdvk_transformer_block": (_I, [_P, ctypes.POINTER(BlockDesc), _P, _U64]),
 }
 
 
@@ -230,6 +256,21 @@ class Context:
         self._check(lib().sdvk_dispatch(self._h, kernel.encode(), arr, len(bufs), pbuf, len(push), gx, gy, gz),
                     f"dispatch({kernel})")
 
+    def layernorm(self, x: int, gamma: Optional[int], beta: Optional[int], y: int, y_dtype: int, rows: int, d: int,
+                  ldx: int = 0, ldy: int = 0, eps: float = 1e-5) -> None:
+        self._check(lib().sdvk_layernorm(self._h, x, gamma or None, beta or None, y, y_dtype, rows, d, ldx or d,
+                                         ldy or d, eps), "layernorm")
+
+    def geglu(self, h: int, y: int, rows: int, F: int, ldh: int = 0, ldy: int = 0) -> None:
+        self._check(lib().sdvk_geglu(self._h, h, y, rows, F, ldh or 2 * F, ldy or F), "geglu")
+
+    @staticmethod
+    def block_workspace(desc: "BlockDesc") -> int:
+        return int(lib().sdvk_transformer_block_workspace(ctypes.byref(desc)))
+
+    def transformer_block(self, desc: "BlockDesc", workspace: int, nbytes: int) -> None:
+        self._check(lib().sdvk_transformer_block(self._h, ctypes.byref(desc), workspace, nbytes), "transformer_block")
+
     def check_finite(self, ptr: int, dtype: int, n: int) -> bool:
         st = lib().sdvk_check_finite(self._h, ptr, dtype, n)
         if st == E_NOT_FINITE:
@@ -241,6 +282,11 @@ class Context:
 def pack_pg(M, N, K, mode=0, sA=0, sB=0, sC=0, batch=1, lda=0, ldb=0, ldc=0) -> bytes:
     """Pg push constants of the Q8 GEMM kernels (sdvkgen.cpp:901-903)."""
     return struct.pack("<12I", M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, 0)
+
+
+def pack_ln(rows, d, eps=1e-5, affine=1) -> bytes:
+    """layernorm_fwd push constants {rows, d, eps, affine} (sdvkgen.cpp:1096-1100)."""
+    return struct.pack("<IIfI", rows, d, eps, affine)
 
 
 def pack_fa(Tq, Tk, C, heads, hd, causal, scale) -> bytes:

@@ -46,6 +46,11 @@ int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env);
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 bool kernel_smem_attr(const void* kern, int bytes, int device);
 int attention(const sdvk_attn_desc& d, const LaunchEnv& env);
+int layernorm(const float* x, const float* gamma, const float* beta, void* y, int y_dtype, uint32_t rows, uint32_t d,
+              uint64_t ldx, uint64_t ldy, float eps, const LaunchEnv& env);
+int geglu(const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint64_t ldy, const LaunchEnv& env);
+uint64_t block_workspace_bytes(const sdvk_block_desc& d);
+int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, const LaunchEnv& env);
 int check_finite(const void* x, int dtype, uint64_t n, uint32_t* flag_dev, const LaunchEnv& env);
 
 inline int dtype_size(int dt) { return dt == SDVK_F32 ? 4 : (dt == SDVK_F16 || dt == SDVK_BF16) ? 2 : 0; }

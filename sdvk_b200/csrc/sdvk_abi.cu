@@ -37,7 +37,13 @@ struct FaPush {
     uint32_t Tq, Tk, C, heads, hd, causal, pad0, pad1;
     float scale;
 };
+struct LnPush {  // layernorm_fwd.comp push constants (sdvkgen.cpp:1096-1100)
+    uint32_t rows, d;
+    float eps;
+    uint32_t affine;
+};
 static_assert(sizeof(Pg) == 48, "Pg layout");
+static_assert(sizeof(LnPush) == 16, "LnPush layout");
 static_assert(sizeof(FaPush) == 36, "FaPush layout");
 
 int set_err(sdvk_ctx* ctx, int code, const std::string& msg) {
@@ -403,6 +409,30 @@ int sdvk_check_finite(sdvk_ctx* ctx, const void* x, int dtype, uint64_t n) {
     return flag ? set_err(ctx, SDVK_E_NOT_FINITE, "non-finite value found") : SDVK_OK;
 }
 
+// ------------------------------------------------------------------ transformer block
+int sdvk_layernorm(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, void* y, int y_dtype,
+                   uint32_t rows, uint32_t d, uint64_t ldx, uint64_t ldy, float eps) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::layernorm(x, gamma, beta, y, y_dtype, rows, d, ldx, ldy, eps, env_of(ctx));
+}
+
+int sdvk_geglu(sdvk_ctx* ctx, const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint64_t ldy) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::geglu(h, y, rows, F, ldh, ldy, env_of(ctx));
+}
+
+uint64_t sdvk_transformer_block_workspace(const sdvk_block_desc* desc) {
+    return desc ? sdvk::block_workspace_bytes(*desc) : 0;
+}
+
+int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, void* workspace, uint64_t workspace_bytes) {
+    if (!ctx || !desc) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::transformer_block(*desc, workspace, workspace_bytes, env_of(ctx));
+}
+
 // ------------------------------------------------------------------ name dispatch
 int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint32_t nbufs, const void* push,
                   uint32_t push_bytes, uint32_t gx, uint32_t gy, uint32_t gz) {
@@ -452,6 +482,20 @@ int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint3
                                static_cast<const float*>(buf_ptr(bufs[3])), buf_ptr(bufs[1]), SDVK_F32, nullptr,
                                buf_mptr(bufs[2]), SDVK_F32, pc.M, pc.N, pc.K, (uint32_t)lda, (uint32_t)ldb,
                                (uint32_t)ldc, batch, pc.sA, pc.sB, pc.sC, pc.mode != 0);
+    }
+    if (is({"layernorm_fwd"})) {
+        if (push_bytes < sizeof(LnPush) || nbufs < 4u)
+            return set_err(ctx, SDVK_E_ARG, name + ": needs 4 buffers and a 16-byte push");
+        LnPush pc;
+        std::memcpy(&pc, push, sizeof(pc));
+        const uint64_t xy_end = (uint64_t)pc.rows * pc.d * 4;
+        if (!buf_holds(bufs[0], xy_end) || !buf_holds(bufs[3], xy_end) ||
+            (pc.affine && (!buf_holds(bufs[1], (uint64_t)pc.d * 4) || !buf_holds(bufs[2], (uint64_t)pc.d * 4))))
+            return set_err(ctx, SDVK_E_ARG, name + ": a buffer is smaller than the shape needs");
+        return sdvk_layernorm(ctx, static_cast<const float*>(buf_ptr(bufs[0])),
+                              pc.affine ? static_cast<const float*>(buf_ptr(bufs[1])) : nullptr,
+                              pc.affine ? static_cast<const float*>(buf_ptr(bufs[2])) : nullptr, buf_mptr(bufs[3]),
+                              SDVK_F32, pc.rows, pc.d, pc.d, pc.d, pc.eps);
     }
     if (is({"fused_attn", "fused_attn_tiled"})) {
         if (push_bytes < sizeof(FaPush) || nbufs < 4u)

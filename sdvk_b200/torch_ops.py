@@ -10,7 +10,7 @@ from typing import Dict, Optional
 
 import torch
 
-from . import BF16, F16, F32, AttnDesc, Context
+from . import BF16, F16, F32, AttnDesc, BlockDesc, Context, Q8Linear
 
 _CTX: Dict[int, Context] = {}
 _DT = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
@@ -98,3 +98,58 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, sca
     d.causal = int(causal)
     context(q.device).attention(d)
     return out
+
+
+def layernorm(x: torch.Tensor, gamma: Optional[torch.Tensor], beta: Optional[torch.Tensor], eps: float = 1e-5,
+              out_dtype: torch.dtype = torch.float16, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LayerNorm over the last dim of fp32 x (layernorm_fwd.comp)."""
+    assert x.dtype == torch.float32 and x.stride(-1) == 1
+    d = x.shape[-1]
+    x2 = x.reshape(-1, d)
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    o2 = out.view(-1, d)
+    context(x.device).layernorm(x2.data_ptr(), gamma.data_ptr() if gamma is not None else None,
+                                beta.data_ptr() if beta is not None else None, o2.data_ptr(), _dt(o2), x2.shape[0], d,
+                                x2.stride(0), o2.stride(0), eps)
+    return out
+
+
+def geglu(h: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = h[..., :F] * gelu_erf(h[..., F:]) on f16 h of width 2F."""
+    assert h.dtype == torch.float16 and h.stride(-1) == 1
+    F = h.shape[-1] // 2
+    h2 = h.reshape(-1, 2 * F)
+    if out is None:
+        out = torch.empty(h.shape[:-1] + (F,), dtype=torch.float16, device=h.device)
+    o2 = out.view(-1, F)
+    context(h.device).geglu(h2.data_ptr(), o2.data_ptr(), h2.shape[0], F, h2.stride(0), o2.stride(0))
+    return out
+
+
+def q8_linear(q: torch.Tensor, s: torch.Tensor, bias: Optional[torch.Tensor] = None) -> Q8Linear:
+    return Q8Linear(q.data_ptr(), s.data_ptr(), bias.data_ptr() if bias is not None else None)
+
+
+def transformer_block(x: torch.Tensor, ctx: torch.Tensor, heads: int, weights: dict,
+                      workspace: Optional[torch.Tensor] = None, eps: float = 1e-5) -> torch.Tensor:
+    """One BasicTransformerBlock on fp32 x [B, T, C] in place.  `weights` maps ln1_w ... ln3_b to fp32
+    tensors and q, k, v, o, q2, k2, v2, o2, ff1, ff2 to (int8 [N, K], fp32 scales, fp32 bias or None)."""
+    assert x.dtype == torch.float32 and x.is_contiguous() and ctx.is_contiguous()
+    B, T, C = x.shape
+    d = BlockDesc()
+    d.x, d.ctx, d.ctx_dtype = x.data_ptr(), ctx.data_ptr(), _dt(ctx)
+    d.batch, d.T, d.C, d.heads = B, T, C, heads
+    d.Tctx, d.Cctx = ctx.shape[1], ctx.shape[2]
+    d.ff_inner = weights["ff2"][0].shape[1]
+    for name in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "ln3_w", "ln3_b"):
+        t = weights.get(name)
+        setattr(d, name, t.data_ptr() if t is not None else None)
+    for name in ("q", "k", "v", "o", "q2", "k2", "v2", "o2", "ff1", "ff2"):
+        setattr(d, name, q8_linear(*weights[name]))
+    d.eps = eps
+    need = Context.block_workspace(d)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    context(x.device).transformer_block(d, workspace.data_ptr(), workspace.numel() * workspace.element_size())
+    return x

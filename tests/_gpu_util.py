@@ -30,11 +30,16 @@ def host(t: torch.Tensor) -> np.ndarray:
     return t.cpu().numpy()
 
 
-def record(name: str, stats: dict) -> None:
-    """Append a parity line (used to build the published parity table)."""
+def record(name: str, stats: dict, reference_stats: dict = None) -> None:
+    """Append a parity line (used to build the published parity table); `reference_stats` is the
+    restated reference fp32 arithmetic's error against the same truth, where the test has it."""
+    line = {"case": name, **stats}
+    if reference_stats is not None:
+        line["reference_fp32"] = reference_stats
+    print("PARITY", json.dumps(line))
     if REPORT:
         with open(REPORT, "a") as f:
-            f.write(json.dumps({"case": name, **stats}) + "\n")
+            f.write(json.dumps(line) + "\n")
 
 
 def check_gemm(orc, name, got, ref, kind):

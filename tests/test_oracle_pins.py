@@ -213,3 +213,25 @@ def test_layernorm_and_gelu_restatements(orc):
     xs = np.linspace(-8, 8, 10001).astype(np.float32)
     ref = np.array([0.5 * t * (1 + math.erf(t / math.sqrt(2))) for t in xs.astype(np.float64)])
     assert np.max(np.abs(orc.gelu_erf_shader(xs) - ref)) < 2e-6 * 8  # A&S 7.1.26: |eps| <= 1.5e-7 in erf
+
+
+def test_block_restatement_vs_f64(orc):
+    """The reference's fp32 block arithmetic (kernel by kernel) against the fp64 block composition on a
+    small BasicTransformerBlock: the two oracle paths agree to fp32 rounding."""
+    rng_seed, C, Cc, F, heads, T, Tc = 31, 128, 64, 96, 2, 70, 9
+    W = {}
+    for i, (name, n, k, bias) in enumerate([("q", C, C, False), ("k", C, C, False), ("v", C, C, False),
+                                             ("o", C, C, True), ("q2", C, C, False), ("k2", C, Cc, False),
+                                             ("v2", C, Cc, False), ("o2", C, C, True), ("ff1", 2 * F, C, True),
+                                             ("ff2", C, F, True)]):
+        q, _, s = orc.q8_weights(rng_seed, i, n, k)
+        W[name] = (q, s, orc.normal_f32(rng_seed, 50 + i, (n,)) * 0.05 if bias else None)
+    for i in (1, 2, 3):
+        W[f"ln{i}_w"] = orc.normal_f32(rng_seed, 60 + i, (C,)) * 0.1 + 1
+        W[f"ln{i}_b"] = orc.normal_f32(rng_seed, 70 + i, (C,)) * 0.1
+    x = orc.normal_f32(rng_seed, 80, (1, T, C))
+    ctx = orc.normal_f32(rng_seed, 81, (1, Tc, Cc))
+    ref = orc.block_f64(x, ctx, heads, W)
+    got = orc.block_shader(x, ctx, heads, W)
+    st = orc.err_stats(got - x, ref - x)
+    assert st["rel_rms"] < 1e-5 and st["rel_max_rms"] < 1e-4, st
