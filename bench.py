@@ -2,14 +2,16 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sdvk|reference] [--workload NAME]
 
-Workloads (BASELINE configs 0 and 1, synthetic seeded inputs of the stated shapes):
+Workloads (synthetic seeded inputs of the stated shapes):
   gemm             (default) Q8_0 dequant GEMM Y[9216,1280] = X[9216,1280] . dequant(W[1280,1280])^T,
                    fp16 X, GGUF Q8_0 W (int8 + per-32 scale), fp32 Y
+  block            one SDXL BasicTransformerBlock, batch 2 x 1024 tokens x 1280 channels (13 launches)
   attn-self-4096   fused attention, batch 2, 4096 tokens, 10 heads x 64, fp16
   attn-self-1024   fused attention, batch 2, 1024 tokens, 20 heads x 64, fp16
   attn-cross-77    fused attention, batch 2, 1024 queries x 77 keys, 20 heads x 64, fp16
 
-One step = one launch of the hot-path kernel over one set of inputs.  Rotating input/output sets
+One step = one launch of the hot-path kernel (for `block`, the block's 13 launches) over one set of
+inputs.  Rotating input/output sets
 whose total exceeds the 126 MB L2 keep every step's operands out of L2.  Steps are captured in CUDA
 graphs and replayed; the timed region is bracketed by a barrier and a device synchronize and timed
 with CUDA events on the launching stream; the job time is the max over ranks.  Multi-GPU runs are
@@ -268,8 +270,136 @@ class AttnWorkload:
         return 4.0 * self.heads * rows * self.Tk * self.hd
 
 
+class BlockWorkload:
+    """one SDXL BasicTransformerBlock (spatialTransformer's layer body)."""
+
+    name = "block"
+    B, T, C, H, Tc, Cc, F = 2, 1024, 1280, 20, 77, 2048, 5120
+    metric = "BasicTransformerBlock TFLOP/s @B2 T1024 C1280"
+    describe = ("SDXL BasicTransformerBlock (BASELINE config 2): batch 2, 1024 tokens, 1280 channels, 20x64 heads, "
+                "77x2048 context, GEGLU 1280->10240->1280; random Q8_0 weights (config-0 distribution), fp32 residual "
+                "x ~N(0,1), fp16 context ~N(0,1), LN gamma 1 beta 0")
+    bound = "tensor"
+    dtype = "f16"
+    # LN, QKV GEMM, attention, out GEMM; LN, Q GEMM, K|V GEMM, attention, out GEMM; LN, FF1, GEGLU, FF2
+    launches_per_step = 13
+
+    def __init__(self):
+        B, T, C, H, Tc, Cc, F = self.B, self.T, self.C, self.H, self.Tc, self.Cc, self.F
+        rows = B * T
+        self.flop = (2.0 * rows * (3 * C * C + 3 * C * C + 2 * F * C + C * F) + 2.0 * B * Tc * 2 * C * Cc
+                     + 4.0 * B * H * T * T * 64 + 4.0 * B * H * T * Tc * 64)
+        self.weights = None
+        # weights (34 MB int8) + per-step activations and workspace (~110 MB) exceed L2 with 2 sets
+        self.bytes = int((3 * C * C + 3 * C * C + 2 * C * Cc + 3 * F * C) * 1.03 + rows * C * 8 + B * Tc * Cc * 2)
+        self.rotate = 2
+        self.l2_note = ("2 rotating sets; each step moves ~250 MB (34 MB of weights, x read/written 9x, 89 MB of fp16 "
+                        "intermediates) > 126 MB L2")
+        self.cpu_units = T
+        self.cpu_what = ("query rows of image 0 (fp32 restatement of the reference's kernels: layernorm_fwd, "
+                         "gemm_nt_q8_v(+bias), fused_attn(_tiled), unary_fwd GELU, mul2, add2)")
+
+    def _make_weights(self, torch, device):
+        g = torch.Generator(device=device)
+        g.manual_seed(4)
+        B, T, C, H, Tc, Cc, F = self.B, self.T, self.C, self.H, self.Tc, self.Cc, self.F
+
+        def q8(n, k, bias):
+            q = torch.randint(-127, 128, (n, k), generator=g, device=device, dtype=torch.int8)
+            s = (torch.randn((n * k // 32,), generator=g, device=device).abs() * 0.02 / 127).half().float()
+            b = torch.randn((n,), generator=g, device=device) * 0.02 if bias else None
+            return q, s, b
+
+        W = {}
+        qkv = q8(3 * C, C, False)  # q, k, v back to back: one GEMM
+        for i, n in enumerate(("q", "k", "v")):
+            W[n] = (qkv[0][i * C:(i + 1) * C], qkv[1][i * C * C // 32:(i + 1) * C * C // 32], None)
+        kv = q8(2 * C, Cc, False)
+        for i, n in enumerate(("k2", "v2")):
+            W[n] = (kv[0][i * C:(i + 1) * C], kv[1][i * C * Cc // 32:(i + 1) * C * Cc // 32], None)
+        W["o"], W["q2"], W["o2"] = q8(C, C, True), q8(C, C, False), q8(C, C, True)
+        W["ff1"], W["ff2"] = q8(2 * F, C, True), q8(C, F, True)
+        for i in (1, 2, 3):
+            W[f"ln{i}_w"] = torch.ones(C, device=device)
+            W[f"ln{i}_b"] = torch.zeros(C, device=device)
+        return W
+
+    def make_set(self, torch, device, seed):
+        if self.weights is None:
+            self.weights = self._make_weights(torch, device)
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        x = torch.randn((self.B, self.T, self.C), generator=g, device=device)
+        ctx = torch.randn((self.B, self.Tc, self.Cc), generator=g, device=device).half()
+        need = self._workspace(torch, device, x, ctx)
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        return x, ctx, ws
+
+    def _desc(self, sdvk_b200, torch_ops, x, ctx):
+        d = sdvk_b200.BlockDesc()
+        d.x, d.ctx, d.ctx_dtype = x.data_ptr(), ctx.data_ptr(), sdvk_b200.F16
+        d.batch, d.T, d.C, d.heads, d.Tctx, d.Cctx, d.ff_inner = self.B, self.T, self.C, self.H, self.Tc, self.Cc, self.F
+        for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "ln3_w", "ln3_b"):
+            setattr(d, n, self.weights[n].data_ptr())
+        for n in ("q", "k", "v", "o", "q2", "k2", "v2", "o2", "ff1", "ff2"):
+            setattr(d, n, torch_ops.q8_linear(*self.weights[n]))
+        d.eps = 1e-5
+        return d
+
+    def _workspace(self, torch, device, x, ctx):
+        import sdvk_b200
+        from sdvk_b200 import torch_ops
+
+        return sdvk_b200.Context.block_workspace(self._desc(sdvk_b200, torch_ops, x, ctx))
+
+    def step(self, torch_ops, st):
+        import sdvk_b200
+
+        x, ctx, ws = st
+        torch_ops.context(x.device).transformer_block(self._desc(sdvk_b200, torch_ops, x, ctx), ws.data_ptr(),
+                                                      ws.numel())
+
+    def e2e(self, sdvk_b200, ctx_, torch, st):
+        """Per step: pinned x and context -> device, the block, device x -> pinned host."""
+        from sdvk_b200 import torch_ops
+
+        x, cx, ws = st
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x.cpu())
+        ch = torch.empty(cx.shape, dtype=cx.dtype, pin_memory=True)
+        ch.copy_(cx.cpu())
+        d = self._desc(sdvk_b200, torch_ops, x, cx)
+
+        def run():
+            ctx_.upload_async(x.data_ptr(), xh.data_ptr(), xh.numel() * 4)
+            ctx_.upload_async(cx.data_ptr(), ch.data_ptr(), ch.numel() * 2)
+            ctx_.transformer_block(d, ws.data_ptr(), ws.numel())
+            ctx_.download_async(xh.data_ptr(), x.data_ptr(), xh.numel() * 4)
+
+        return run, xh.numel() * 4 + ch.numel() * 2, xh.numel() * 4, \
+            "2x sdvk_upload_async + sdvk_transformer_block + sdvk_download_async"
+
+    def host_inputs(self):
+        W = {k: (tuple(a.cpu().numpy() if a is not None else None for a in v) if isinstance(v, tuple)
+                 else v.cpu().numpy()) for k, v in self.weights.items()}
+        rng = np.random.default_rng(4)
+        x = rng.standard_normal((1, self.T, self.C), dtype=np.float32)
+        ctx = rng.standard_normal((1, self.Tc, self.Cc), dtype=np.float32).astype(np.float16).astype(np.float32)
+        return x, ctx, W
+
+    def cpu_run(self, inputs, rows):
+        from oracle import pyoracle
+
+        x, ctx, W = inputs
+        pyoracle.block_shader(x, ctx, self.H, W, np.arange(rows))
+        T, C, Tc, Cc, F = self.T, self.C, self.Tc, self.Cc, self.F
+        return (2.0 * rows * (C * C + C * C + C * C + C * C + 2 * F * C + C * F) + 2.0 * T * 2 * C * C
+                + 2.0 * Tc * 2 * C * Cc + 4.0 * self.H * rows * (T + Tc) * 64)
+
+
 WORKLOADS = {
     "gemm": GemmWorkload,
+    "block": BlockWorkload,
     "attn-self-4096": lambda: AttnWorkload("attn-self-4096", 2, 4096, 4096, 10),
     "attn-self-1024": lambda: AttnWorkload("attn-self-1024", 2, 1024, 1024, 20),
     "attn-cross-77": lambda: AttnWorkload("attn-cross-77", 2, 1024, 77, 20),
@@ -456,12 +586,13 @@ def main(argv=None):
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
             "config": {"workload": wl.describe, "parallelism": f"replicas x{world}",
-                       "l2": f"{wl.rotate} rotating input/output sets ({wl.rotate * wl.bytes / 1e6:.0f} MB > 126 MB L2)",
+                       "l2": getattr(wl, "l2_note", None) or
+                       f"{wl.rotate} rotating input/output sets ({wl.rotate * wl.bytes / 1e6:.0f} MB > 126 MB L2)",
                        "timing": f"CUDA events over CUDA-graph replays of {GRAPH_LEN} launches"},
             "roofline": roof,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "path": path + ", pinned host buffers"},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * getattr(wl, "launches_per_step", 1),
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
