@@ -215,6 +215,31 @@ typedef struct sdvk_block_desc {
 SDVK_API uint64_t sdvk_transformer_block_workspace(const sdvk_block_desc* desc);
 SDVK_API int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, void* workspace, uint64_t workspace_bytes);
 
+/* ---- multi-GPU: the CFG pair ----------------------------------------------------------------- */
+/* Classifier-free guidance combine on the device (evalGuided, sdvkgen.cpp:3825-3845):
+ *   out = uncond + cfg * (cond - uncond); with rescale > 0 the result's spread is pulled toward the
+ *   unconditional output's: er = (out - mean) * std(uncond) / (std(out) + 1e-6) + mean,
+ *   out = rescale * er + (1 - rescale) * out (statistics in double).  fp32 [n] each. */
+SDVK_API int sdvk_cfg_combine(sdvk_ctx* ctx, const float* cond, const float* uncond, float* out, uint64_t n, float cfg,
+                     float rescale);
+
+/* An NCCL communicator for the context's device.  The reference runs both CFG passes on one device
+ * (runPass twice, sdvkgen.cpp:3812-3813); with a GPU pair each rank runs one pass and the halves
+ * meet by all-gather.  The unique id (SDVK_COMM_ID_BYTES) is made on one rank and passed to the
+ * others out of band.  Creation and every wait poll the communicator against timeout_ms: a peer
+ * that never joins or stops answering aborts the communicator and returns SDVK_E_TIMEOUT.
+ * NCCL itself is loaded on first use (libnccl.so.2); without it these calls return SDVK_E_CUDA. */
+#define SDVK_COMM_ID_BYTES 128
+typedef struct sdvk_comm sdvk_comm;
+SDVK_API int sdvk_comm_unique_id(void* id);
+SDVK_API int sdvk_comm_create(sdvk_ctx* ctx, int nranks, int rank, const void* id, uint32_t timeout_ms, sdvk_comm** out);
+SDVK_API int sdvk_comm_destroy(sdvk_comm* comm);
+SDVK_API int sdvk_comm_abort(sdvk_comm* comm);
+/* recv[r * count + i] = rank r's send[i], queued on the context's stream. */
+SDVK_API int sdvk_allgather(sdvk_ctx* ctx, sdvk_comm* comm, const void* send, void* recv, uint64_t count, int dtype);
+/* Wait for the context's stream (the queued collectives) with the communicator's health polled. */
+SDVK_API int sdvk_comm_wait(sdvk_ctx* ctx, sdvk_comm* comm, uint32_t timeout_ms);
+
 /* NaN/Inf check of n fp32 or f16 values (the reference aborts on a non-finite UNet output,
  * sdvkgen.cpp:3819-3823): returns SDVK_E_NOT_FINITE if any value is not finite. */
 SDVK_API int sdvk_check_finite(sdvk_ctx* ctx, const void* x, int dtype, uint64_t n);

@@ -655,4 +655,27 @@ void orc_gelu_erf_shader(const float* x, float* y, uint64_t n) {
     }
 }
 
+// evalGuided's guidance combine (src/Modules/Diffusion/sdvkgen.cpp:3825-3845), in its order:
+// res = u + cfg * (c - u) in fp32; with rescale > 0, the mean and spreads in double, then
+// er = (res - m) * (su / sg) + m and res = rescale * er + (1 - rescale) * res.
+void orc_cfg_combine(const float* cond, const float* uncond, float* out, uint64_t n, float cfg, float rescale) {
+    for (uint64_t k = 0; k < n; ++k) out[k] = uncond[k] + cfg * (cond[k] - uncond[k]);
+    if (rescale > 0.0f) {
+        double m = 0, s2 = 0, u2 = 0;
+        for (uint64_t k = 0; k < n; ++k) m += out[k];
+        m /= (double)n;
+        for (uint64_t k = 0; k < n; ++k) {
+            const double d = out[k] - m;
+            s2 += d * d;
+        }
+        for (uint64_t k = 0; k < n; ++k) u2 += (double)uncond[k] * uncond[k];
+        const double su = std::sqrt(u2 / (double)n);
+        const double sg = std::sqrt(s2 / (double)n) + 1e-6;
+        for (uint64_t k = 0; k < n; ++k) {
+            const float er = (float)((out[k] - m) * (su / sg) + m);
+            out[k] = (float)(rescale * er + (1.0 - rescale) * out[k]);
+        }
+    }
+}
+
 }  // extern "C"

@@ -80,6 +80,7 @@ void orc_layernorm_shader(const float* x, const float* gamma, const float* beta,
 void orc_layernorm_f64(const double* x, const float* gamma, const float* beta, double* y,
                        uint32_t rows, uint32_t d, double eps);
 void orc_gelu_erf_shader(const float* x, float* y, uint64_t n);
+void orc_cfg_combine(const float* cond, const float* uncond, float* out, uint64_t n, float cfg, float rescale);
 
 /* ---- misc ------------------------------------------------------------------------------------ */
 int orc_num_threads(void);

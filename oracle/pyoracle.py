@@ -43,6 +43,7 @@ _SIG = {
     "orc_layernorm_shader": (None, [_P, _P, _P, _P, _U32, _U32, _F, _U32]),
     "orc_layernorm_f64": (None, [_P, _P, _P, _P, _U32, _U32, ctypes.c_double]),
     "orc_gelu_erf_shader": (None, [_P, _P, _U64]),
+    "orc_cfg_combine": (None, [_P, _P, _P, _U64, _F, _F]),
     "orc_num_threads": (_I, []),
     "orc_set_num_threads": (None, [_I]),
 }
@@ -334,6 +335,13 @@ def block_shader(x, ctx, heads, W, rows=None, eps=1e-5):
         g = lin(n, W["ff1"])
         F = g.shape[1] // 2
         out[b] = x2 + lin(np.ascontiguousarray(g[:, :F]) * gelu_erf_shader(np.ascontiguousarray(g[:, F:])), W["ff2"])
+    return out
+
+
+def cfg_combine(cond, uncond, cfg, rescale=0.0):
+    c, u = _c(cond, np.float32), _c(uncond, np.float32)
+    out = np.empty_like(c)
+    lib().orc_cfg_combine(_p(c), _p(u), _p(out), c.size, cfg, rescale)
     return out
 
 

@@ -108,6 +108,13 @@ SIGNATURES = {
                              _U64, _U64, _U64, _I]),
     "sdvk_attention": (_I, [_P, ctypes.POINTER(AttnDesc)]),
     "sdvk_check_finite": (_I, [_P, _P, _I, _U64]),
+    "sdvk_cfg_combine": (_I, [_P, _P, _P, _P, _U64, ctypes.c_float, ctypes.c_float]),
+    "sdvk_comm_unique_id": (_I, [_P]),
+    "sdvk_comm_create": (_I, [_P, _I, _I, _P, _U32, ctypes.POINTER(_P)]),
+    "sdvk_comm_destroy": (_I, [_P]),
+    "sdvk_comm_abort": (_I, [_P]),
+    "sdvk_allgather": (_I, [_P, _P, _P, _P, _U64, _I]),
+    "sdvk_comm_wait": (_I, [_P, _P, _U32]),
     "sdvk_layernorm": (_I, [_P, _P, _P, _P, _P, _I, _U32, _U32, _U64, _U64, ctypes.c_float]),
     "sdvk_geglu": (_I, [_P, _P, _P, _U32, _U32, _U64, _U64]),
     "sdvk_transformer_block_workspace": (_U64, [ctypes.POINTER(BlockDesc)]),
@@ -271,6 +278,9 @@ class Context:
     def transformer_block(self, desc: "BlockDesc", workspace: int, nbytes: int) -> None:
         self._check(lib().sdvk_transformer_block(self._h, ctypes.byref(desc), workspace, nbytes), "transformer_block")
 
+    def cfg_combine(self, cond: int, uncond: int, out: int, n: int, cfg: float, rescale: float = 0.0) -> None:
+        self._check(lib().sdvk_cfg_combine(self._h, cond, uncond, out, n, cfg, rescale), "cfg_combine")
+
     def check_finite(self, ptr: int, dtype: int, n: int) -> bool:
         st = lib().sdvk_check_finite(self._h, ptr, dtype, n)
         if st == E_NOT_FINITE:
@@ -292,3 +302,41 @@ def pack_ln(rows, d, eps=1e-5, affine=1) -> bytes:
 def pack_fa(Tq, Tk, C, heads, hd, causal, scale) -> bytes:
     """FaPush of the fused attention kernels (fused_attn.cpp:15-26)."""
     return struct.pack("<8If", Tq, Tk, C, heads, hd, int(causal), 0, 0, scale)
+
+
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL unique id (made on one rank, passed to the others out of band)."""
+    buf = ctypes.create_string_buffer(COMM_ID_BYTES)
+    st = lib().sdvk_comm_unique_id(buf)
+    if st != OK:
+        raise SdvkError(st, "sdvk_comm_unique_id failed (is libnccl.so.2 available?)")
+    return buf.raw
+
+
+class Comm:
+    """An NCCL communicator over a context's device (sdvk_comm)."""
+
+    def __init__(self, ctx: Context, nranks: int, rank: int, uid: bytes, timeout_ms: int = 30000):
+        self._ctx = ctx
+        self._h = ctypes.c_void_p()
+        idb = ctypes.create_string_buffer(uid, COMM_ID_BYTES)
+        ctx._check(lib().sdvk_comm_create(ctx.handle, nranks, rank, idb, timeout_ms, ctypes.byref(self._h)),
+                   "comm_create")
+
+    def allgather(self, send: int, recv: int, count: int, dtype: int) -> None:
+        self._ctx._check(lib().sdvk_allgather(self._ctx.handle, self._h, send, recv, count, dtype), "allgather")
+
+    def wait(self, timeout_ms: int = 30000) -> None:
+        self._ctx._check(lib().sdvk_comm_wait(self._ctx.handle, self._h, timeout_ms), "comm_wait")
+
+    def abort(self) -> None:
+        if self._h:
+            lib().sdvk_comm_abort(self._h)
+
+    def close(self) -> None:
+        if self._h:
+            lib().sdvk_comm_destroy(self._h)
+            self._h = ctypes.c_void_p()

@@ -22,7 +22,7 @@ OBJDIR = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libsdvk_b200.so")
 HOST = os.path.join(PKG, "host")
 ENGINE_LIB = os.path.join(PKG, "libsdvk_engine.so")  # C++ ofc::gpu::Engine mirror over the C ABI
-SOURCES = ["sdvk_abi.cu", "gemm_q8.cu", "attention.cu", "block.cu"]
+SOURCES = ["sdvk_abi.cu", "gemm_q8.cu", "attention.cu", "block.cu", "collective.cu"]
 HEADERS = ["ptx.cuh", "gemm_q8.cuh", "gemm_q8_2sm.cuh", "attention.cuh", "attention_tc.cuh", "backend.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -62,8 +62,8 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), SOURCES))
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < _newest(objs):
         # Static cudart keeps the library independent of which libcudart the host process loaded.
-        subprocess.run([nvcc(), *ARCH, "-shared", "-Xlinker", "-soname=libsdvk_b200.so", "-o", LIB, *objs, "-lcuda"],
-                       check=True)
+        subprocess.run([nvcc(), *ARCH, "-shared", "-Xlinker", "-soname=libsdvk_b200.so", "-o", LIB, *objs, "-lcuda",
+                        "-ldl"], check=True)
     build_engine(force)
     return LIB
 

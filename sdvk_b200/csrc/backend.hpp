@@ -51,6 +51,15 @@ int layernorm(const float* x, const float* gamma, const float* beta, void* y, in
 int geglu(const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint64_t ldy, const LaunchEnv& env);
 uint64_t block_workspace_bytes(const sdvk_block_desc& d);
 int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, const LaunchEnv& env);
+int cfg_combine(const float* cond, const float* uncond, float* out, uint64_t n, float cfg, float rescale,
+                const LaunchEnv& env);
+int comm_unique_id(void* id);
+int comm_create(int nranks, int rank, const void* id, uint32_t timeout_ms, sdvk_comm** out, const LaunchEnv& env);
+int comm_destroy(sdvk_comm* c);
+int comm_abort(sdvk_comm* c);
+int allgather(sdvk_comm* c, const void* send, void* recv, uint64_t count, int dtype, uint32_t timeout_ms,
+              const LaunchEnv& env);
+int comm_wait(sdvk_comm* c, uint32_t timeout_ms, const LaunchEnv& env);
 int check_finite(const void* x, int dtype, uint64_t n, uint32_t* flag_dev, const LaunchEnv& env);
 
 inline int dtype_size(int dt) { return dt == SDVK_F32 ? 4 : (dt == SDVK_F16 || dt == SDVK_BF16) ? 2 : 0; }

@@ -433,6 +433,39 @@ int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, void* wor
     return sdvk::transformer_block(*desc, workspace, workspace_bytes, env_of(ctx));
 }
 
+// ------------------------------------------------------------------ multi-GPU (CFG pair)
+int sdvk_cfg_combine(sdvk_ctx* ctx, const float* cond, const float* uncond, float* out, uint64_t n, float cfg,
+                     float rescale) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::cfg_combine(cond, uncond, out, n, cfg, rescale, env_of(ctx));
+}
+
+int sdvk_comm_unique_id(void* id) { return sdvk::comm_unique_id(id); }
+
+int sdvk_comm_create(sdvk_ctx* ctx, int nranks, int rank, const void* id, uint32_t timeout_ms, sdvk_comm** out) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::comm_create(nranks, rank, id, timeout_ms ? timeout_ms : 30000, out, env_of(ctx));
+}
+
+int sdvk_comm_destroy(sdvk_comm* comm) { return sdvk::comm_destroy(comm); }
+
+int sdvk_comm_abort(sdvk_comm* comm) { return sdvk::comm_abort(comm); }
+
+int sdvk_allgather(sdvk_ctx* ctx, sdvk_comm* comm, const void* send, void* recv, uint64_t count, int dtype) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::allgather(comm, send, recv, count, dtype, (uint32_t)(ctx->timeout_ns / 1000000ull), env_of(ctx));
+}
+
+int sdvk_comm_wait(sdvk_ctx* ctx, sdvk_comm* comm, uint32_t timeout_ms) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    if (int rc = sdvk::comm_wait(comm, timeout_ms ? timeout_ms : 30000, env_of(ctx))) return rc;
+    return collect_device_error(ctx);
+}
+
 // ------------------------------------------------------------------ name dispatch
 int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint32_t nbufs, const void* push,
                   uint32_t push_bytes, uint32_t gx, uint32_t gy, uint32_t gz) {

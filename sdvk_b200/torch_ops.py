@@ -153,3 +153,14 @@ def transformer_block(x: torch.Tensor, ctx: torch.Tensor, heads: int, weights: d
         workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
     context(x.device).transformer_block(d, workspace.data_ptr(), workspace.numel() * workspace.element_size())
     return x
+
+
+def cfg_combine(cond: torch.Tensor, uncond: torch.Tensor, cfg: float, rescale: float = 0.0,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """uncond + cfg * (cond - uncond), with the optional spread rescale (sdvk_cfg_combine), fp32."""
+    assert cond.dtype == torch.float32 and uncond.dtype == torch.float32 and cond.shape == uncond.shape
+    c, u = cond.contiguous(), uncond.contiguous()
+    if out is None:
+        out = torch.empty_like(c)
+    context(c.device).cfg_combine(c.data_ptr(), u.data_ptr(), out.data_ptr(), c.numel(), cfg, rescale)
+    return out
