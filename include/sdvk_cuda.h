@@ -215,6 +215,17 @@ typedef struct sdvk_block_desc {
 SDVK_API uint64_t sdvk_transformer_block_workspace(const sdvk_block_desc* desc);
 SDVK_API int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, void* workspace, uint64_t workspace_bytes);
 
+/* The same block with no workspace argument and no allocation of any kind: the intermediates live
+ * in a fixed device scratch array compiled into the library, SDVK_STATIC_SCRATCH_BYTES per device.
+ * A shape whose sdvk_transformer_block_workspace() exceeds it returns SDVK_E_SHAPE (one 1024-token
+ * image at C = 1280 fits; the batch-2 config does not).  The array is shared by every call on a
+ * device: calls that can overlap in time on one device (other streams, threads or contexts) race on
+ * it, and the caller must serialise them.  The array's address is looked up on the first call on
+ * each device; make that first call before any stream capture begins.
+ * No counterpart in the reference (it dispatches the block kernel by kernel into its step arena). */
+#define SDVK_STATIC_SCRATCH_BYTES (64ull << 20)
+SDVK_API int sdvk_transformer_block_static(sdvk_ctx* ctx, const sdvk_block_desc* desc);
+
 /* ---- multi-GPU: the CFG pair ----------------------------------------------------------------- */
 /* Classifier-free guidance combine on the device (evalGuided, sdvkgen.cpp:3825-3845):
  *   out = uncond + cfg * (cond - uncond); with rescale > 0 the result's spread is pulled toward the

@@ -119,6 +119,7 @@ SIGNATURES = {
     "sdvk_geglu": (_I, [_P, _P, _P, _U32, _U32, _U64, _U64]),
     "sdvk_transformer_block_workspace": (_U64, [ctypes.POINTER(BlockDesc)]),
     "sdvk_transformer_block": (_I, [_P, ctypes.POINTER(BlockDesc), _P, _U64]),
+    "sdvk_transformer_block_static": (_I, [_P, ctypes.POINTER(BlockDesc)]),
 }
 
 
@@ -278,6 +279,10 @@ class Context:
     def transformer_block(self, desc: "BlockDesc", workspace: int, nbytes: int) -> None:
         self._check(lib().sdvk_transformer_block(self._h, ctypes.byref(desc), workspace, nbytes), "transformer_block")
 
+    def transformer_block_static(self, desc: "BlockDesc") -> None:
+        """The block on the library's fixed device scratch array (no workspace, no allocation)."""
+        self._check(lib().sdvk_transformer_block_static(self._h, ctypes.byref(desc)), "transformer_block_static")
+
     def cfg_combine(self, cond: int, uncond: int, out: int, n: int, cfg: float, rescale: float = 0.0) -> None:
         self._check(lib().sdvk_cfg_combine(self._h, cond, uncond, out, n, cfg, rescale), "cfg_combine")
 
@@ -305,6 +310,7 @@ def pack_fa(Tq, Tk, C, heads, hd, causal, scale) -> bytes:
 
 
 COMM_ID_BYTES = 128
+STATIC_SCRATCH_BYTES = 64 << 20
 
 
 def comm_unique_id() -> bytes:

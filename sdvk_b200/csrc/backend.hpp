@@ -51,6 +51,7 @@ int layernorm(const float* x, const float* gamma, const float* beta, void* y, in
 int geglu(const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint64_t ldy, const LaunchEnv& env);
 uint64_t block_workspace_bytes(const sdvk_block_desc& d);
 int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, const LaunchEnv& env);
+int static_scratch(int device, void** ptr, const LaunchEnv& env);
 int cfg_combine(const float* cond, const float* uncond, float* out, uint64_t n, float cfg, float rescale,
                 const LaunchEnv& env);
 int comm_unique_id(void* id);

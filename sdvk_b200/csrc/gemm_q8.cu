@@ -223,7 +223,7 @@ int pick_pair_bn(const GemmQ8Desc& d, int num_sms) {
     const uint64_t xt = (d.xrows + 255) / 256;
     int best = 256;
     uint64_t best_cost = ~0ull;
-    for (int bn : {256, 160, 128}) {
+    for (int bn : {256, 224, 160, 128}) {
         const uint64_t tiles = xt * ((d.wrows + bn - 1) / bn) * d.batch;
         const uint64_t waves = (tiles + clusters - 1) / clusters;
         const uint64_t cost = waves * (uint64_t)(bn + 256);  // measured: the fixed per-tile share ~ N=256
@@ -251,6 +251,7 @@ int launch_bn(const GemmQ8Desc& d, const LaunchEnv& env) {
     if (pair) {
         const char* e = getenv("SDVK_GEMM_PAIR_BN");
         const int bn = e ? atoi(e) : pick_pair_bn(d, env.num_sms);
+        if (bn == 224) return launch_pair<TA, 224, NN, TC>(d, env);
         if (bn == 160) return launch_pair<TA, 160, NN, TC>(d, env);
         if (bn == 128) return launch_pair<TA, 128, NN, TC>(d, env);
         return launch_pair<TA, 256, NN, TC>(d, env);

@@ -433,6 +433,20 @@ int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, void* wor
     return sdvk::transformer_block(*desc, workspace, workspace_bytes, env_of(ctx));
 }
 
+int sdvk_transformer_block_static(sdvk_ctx* ctx, const sdvk_block_desc* desc) {
+    if (!ctx || !desc) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    const uint64_t need = sdvk::block_workspace_bytes(*desc);
+    if (need > SDVK_STATIC_SCRATCH_BYTES)
+        return set_err(ctx, SDVK_E_SHAPE, "the block needs " + std::to_string(need) +
+                                              " bytes of scratch, more than the static array's " +
+                                              std::to_string(SDVK_STATIC_SCRATCH_BYTES));
+    void* scratch = nullptr;
+    const sdvk::LaunchEnv env = env_of(ctx);
+    if (int rc = sdvk::static_scratch(ctx->device, &scratch, env)) return rc;
+    return sdvk::transformer_block(*desc, scratch, SDVK_STATIC_SCRATCH_BYTES, env);
+}
+
 // ------------------------------------------------------------------ multi-GPU (CFG pair)
 int sdvk_cfg_combine(sdvk_ctx* ctx, const float* cond, const float* uncond, float* out, uint64_t n, float cfg,
                      float rescale) {

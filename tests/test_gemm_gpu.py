@@ -56,11 +56,11 @@ def test_gemm_nt(orc, cuda_ok, M, N, K, dt, with_bias, out):
     check_gemm(orc, f"nt {M}x{N}x{K} {dt}->{out}", got[rows], ref, "f32" if dt == "f32" else dt)
 
 
-@pytest.mark.parametrize("variant", ["1sm", "2sm-256", "2sm-160", "2sm-128"])
+@pytest.mark.parametrize("variant", ["1sm", "2sm-256", "2sm-224", "2sm-160", "2sm-128"])
 @pytest.mark.parametrize("nn", [False, True])
 @pytest.mark.parametrize("dt", ["f16", "f32"])
 def test_gemm_variants(orc, cuda_ok, monkeypatch, variant, nn, dt):
-    """Every kernel variant (single CTA; CTA pair with 256/160/128-wide tiles) on ragged shapes,
+    """Every kernel variant (single CTA; CTA pair with 256/224/160/128-wide tiles) on ragged shapes,
     NT and NN, f16 and tf32."""
     monkeypatch.setenv("SDVK_GEMM_VARIANT", variant[:3])
     if variant.startswith("2sm"):
