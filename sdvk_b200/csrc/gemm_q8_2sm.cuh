@@ -257,8 +257,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             cur.advance();
             const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
             const uint32_t sw = it % Cfg::kSW, pw = (it / Cfg::kSW) & 1;
-            const bool got = mbar_wait(&w_full[sw], pw, p.timeout_ns) && mbar_wait(&empty[s], ph ^ 1, p.timeout_ns);
-            if (!__all_sync(0xffffffffu, got)) {  // the warp leaves the loop together
+            if (!__all_sync(0xffffffffu, mbar_wait(&w_full[sw], pw, p.timeout_ns))) {  // leave together
                 fail();
                 break;
             }
@@ -271,6 +270,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 raw[t] = (r < Cfg::kBNC) ? *reinterpret_cast<const uint4*>(wsrc + r * Cfg::kBK + chunk * 16)
                                          : make_uint4(0, 0, 0, 0);
             }
+            // The raw slot is free as soon as its bytes are in registers: hand it back to the weight
+            // TMA before waiting for the operand stage (the arrive orders the warp's reads before
+            // the next load into the slot), so the weight ring keeps moving while the stage ring is
+            // full and its depth covers the TMA latency alone.
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&w_empty[sw]);
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, p.timeout_ns))) {
+                fail();
+                break;
+            }
 #pragma unroll
             for (int t = 0; t < T; ++t) {
                 const int r = row0 + t * Cfg::kRowStep;
@@ -278,10 +287,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             }
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&w_empty[sw]);
-                mbar_arrive_cluster(mapa_shared(&full[s], 0));
-            }
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(&full[s], 0));
 #pragma unroll
             for (int t = 0; t < T; ++t) {
                 sc0[t] = sc1[t];
