@@ -71,6 +71,13 @@ SDVK_API int sdvk_ctx_reset_stream(sdvk_ctx* ctx);
 SDVK_API void* sdvk_ctx_stream(sdvk_ctx* ctx);
 /* Deadline for every bounded wait inside the kernels (default 2000 ms). */
 SDVK_API int sdvk_ctx_set_timeout_ms(sdvk_ctx* ctx, uint32_t ms);
+/* Arithmetic for fp32 inputs.  SDVK_PRECISION_REFERENCE (the default): attention on fp32 Q/K/V is
+ * computed in fp32, within the reference's own 2e-5 bar (tests/fused_attn_test.cpp:123-124).
+ * SDVK_PRECISION_FAST: fp32 Q/K/V are rounded to f16 for the tensor cores (about 3e-4).  The Q8
+ * GEMMs run fp32 activations in tf32 in both modes; 16-bit inputs are unaffected. */
+#define SDVK_PRECISION_REFERENCE 0
+#define SDVK_PRECISION_FAST 1
+SDVK_API int sdvk_ctx_set_precision(sdvk_ctx* ctx, int precision);
 /* Human-readable device report (Engine::deviceReport, vk_engine.hpp:169). */
 SDVK_API int sdvk_device_report(sdvk_ctx* ctx, char* buf, size_t len);
 /* Text of the last error on this context (empty when none). */
@@ -120,8 +127,8 @@ SDVK_API int sdvk_synchronize(sdvk_ctx* ctx);
  * The grid (gx, gy, gz) the caller computed for the Vulkan tiling is accepted and ignored: each
  * kernel covers the whole shape in the push constants with its own B200 tiling.
  * Deviations: Q8 kernels require K % 32 == 0 (whole Q8_0 blocks); attention requires hd <= 64.
- * Numerics: the GEMM runs the tensor cores in tf32 on fp32 activations, attention computes in
- * f16 operands with fp32 accumulation. */
+ * Numerics: the GEMM runs the tensor cores in tf32 on fp32 activations; attention on the fp32
+ * buffers follows sdvk_ctx_set_precision (fp32 arithmetic by default). */
 SDVK_API int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint32_t nbufs, const void* push,
                   uint32_t push_bytes, uint32_t gx, uint32_t gy, uint32_t gz);
 

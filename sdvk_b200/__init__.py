@@ -23,6 +23,7 @@ LIB_PATH = os.path.join(_HERE, "libsdvk_b200.so")
 
 OK, E_OOM, E_SHAPE, E_CUDA, E_TIMEOUT, E_ARG, E_KERNEL, E_STATE, E_NOT_FINITE = range(9)
 F32, F16, BF16 = 0, 1, 2
+PRECISION_REFERENCE, PRECISION_FAST = 0, 1
 
 _lib: Optional[ctypes.CDLL] = None
 
@@ -83,6 +84,7 @@ SIGNATURES = {
     "sdvk_ctx_reset_stream": (_I, [_P]),
     "sdvk_ctx_stream": (_P, [_P]),
     "sdvk_ctx_set_timeout_ms": (_I, [_P, _U32]),
+    "sdvk_ctx_set_precision": (_I, [_P, _I]),
     "sdvk_device_report": (_I, [_P, ctypes.c_char_p, ctypes.c_size_t]),
     "sdvk_last_error": (ctypes.c_char_p, [_P]),
     "sdvk_status_string": (ctypes.c_char_p, [_I]),
@@ -181,6 +183,10 @@ class Context:
     def reset_stream(self) -> None:
         """Return to the context's private non-blocking stream."""
         self._check(lib().sdvk_ctx_reset_stream(self._h), "reset_stream")
+
+    def set_precision(self, precision: int) -> None:
+        """PRECISION_REFERENCE (default): fp32 attention inputs computed in fp32; PRECISION_FAST: f16."""
+        self._check(lib().sdvk_ctx_set_precision(self._h, precision), "set_precision")
 
     def set_timeout_ms(self, ms: int) -> None:
         self._check(lib().sdvk_ctx_set_timeout_ms(self._h, ms), "set_timeout_ms")

@@ -4,6 +4,7 @@
 #include <string>
 
 #include "attention.cuh"
+#include "attention_fp32.cuh"
 #include "attention_tc.cuh"
 #include "backend.hpp"
 
@@ -147,6 +148,13 @@ int attention(const sdvk_attn_desc& d, const LaunchEnv& env) {
     p.ho = d.ho;
     p.scale_log2 = d.scale * 1.4426950408889634f;
     p.causal = d.causal ? 1u : 0u;
+    const char* force = getenv("SDVK_ATTN_KERNEL");
+    if (d.dtype == SDVK_F32 && env.precision == SDVK_PRECISION_REFERENCE && !(force && force[0] == 'm')) {
+        const dim3 grid((d.Tq + kF32Rows - 1) / kF32Rows, d.heads, d.batch);
+        if (d.o_dtype == SDVK_F32) attn_fp32_kernel<float><<<grid, kF32Rows, 0, env.stream>>>(p);
+        else attn_fp32_kernel<__half><<<grid, kF32Rows, 0, env.stream>>>(p);
+        return cuda_check(env, cudaGetLastError(), "attn_fp32_kernel launch");
+    }
     if (tc_eligible(d)) {
         if (d.dtype == SDVK_F16) return launch_tc_out<__half>(d, env);
         return launch_tc_out<__nv_bfloat16>(d, env);

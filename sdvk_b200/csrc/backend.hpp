@@ -19,6 +19,7 @@ struct LaunchEnv {
     int device;
     int num_sms;
     std::string* msg;     // error text for sdvk_last_error
+    int precision;        // SDVK_PRECISION_REFERENCE or SDVK_PRECISION_FAST
 };
 
 // One Q8_0 GEMM in kernel terms: x = activation operand, w = quantised weight operand.

@@ -20,6 +20,7 @@ struct sdvk_ctx {
     uint32_t* err_dev = nullptr;   // kernels OR device error codes in here
     uint32_t* flag_dev = nullptr;  // sdvk_check_finite
     uint64_t timeout_ns = 2000000000ull;
+    int precision = SDVK_PRECISION_REFERENCE;
     cudaEvent_t step_done = nullptr;
     bool in_step = false;
     bool step_recorded = false;
@@ -65,7 +66,8 @@ int use_device(sdvk_ctx* ctx) {
 }
 
 sdvk::LaunchEnv env_of(sdvk_ctx* ctx) {
-    return sdvk::LaunchEnv{ctx->stream, ctx->err_dev, ctx->timeout_ns, ctx->device, ctx->num_sms, &ctx->last_error};
+    return sdvk::LaunchEnv{ctx->stream, ctx->err_dev, ctx->timeout_ns, ctx->device, ctx->num_sms, &ctx->last_error,
+                           ctx->precision};
 }
 
 // After a synchronisation point: surface (and clear) any device-side error code.
@@ -160,6 +162,12 @@ void* sdvk_ctx_stream(sdvk_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stre
 int sdvk_ctx_set_timeout_ms(sdvk_ctx* ctx, uint32_t ms) {
     if (!ctx || ms == 0) return SDVK_E_ARG;
     ctx->timeout_ns = (uint64_t)ms * 1000000ull;
+    return SDVK_OK;
+}
+
+int sdvk_ctx_set_precision(sdvk_ctx* ctx, int precision) {
+    if (!ctx || (precision != SDVK_PRECISION_REFERENCE && precision != SDVK_PRECISION_FAST)) return SDVK_E_ARG;
+    ctx->precision = precision;
     return SDVK_OK;
 }
 

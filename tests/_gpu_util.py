@@ -5,7 +5,8 @@ saw (fp16/bf16 inputs are converted exactly to fp64).  They follow from the oper
   f16 operands   (10-bit mantissa)  rel_rms <= 1e-3,  max|err| / RMS(ref) <= 1e-2
   bf16 operands  (7-bit mantissa)   rel_rms <= 8e-3,  max|err| / RMS(ref) <= 8e-2
   tf32 (fp32 in, 10-bit mantissa)   rel_rms <= 2e-3,  max|err| / RMS(ref) <= 2e-2
-Attention (f16/bf16 P.V, fp32 accumulation): max|err| / max|ref| <= 5e-3 (f16), 3e-2 (bf16).
+Attention (f16/bf16 P.V, fp32 accumulation): max|err| / max|ref| <= 5e-3 (f16), 3e-2 (bf16);
+fp32 inputs at the default (reference) precision are computed in fp32 and meet the reference's 2e-5.
 The reference's own fp32 shader math meets 2e-5; its error is printed next to ours.
 """
 import json
@@ -15,7 +16,8 @@ import numpy as np
 import torch
 
 GEMM_TOL = {"f16": (1e-3, 1e-2), "bf16": (8e-3, 8e-2), "f32": (2e-3, 2e-2)}
-ATTN_TOL = {"f16": 5e-3, "bf16": 3e-2, "f32": 5e-3}
+# "f32_ref": fp32 inputs under SDVK_PRECISION_REFERENCE (the default) meet the reference's own bar
+ATTN_TOL = {"f16": 5e-3, "bf16": 3e-2, "f32": 5e-3, "f32_ref": 2e-5}
 REPORT = os.environ.get("SDVK_PARITY_REPORT")
 
 

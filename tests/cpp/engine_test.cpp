@@ -11,8 +11,8 @@
 // GEMM known-answer case is 100x100x96 from std::mt19937(7), A = int8/127, scale 0.01
 // (gemm_q8_bench.cpp:58-81).  The attention truth is the reference's fp64 output committed under
 // tests/golden (attn_ref_<i>.f32); the GEMM truth is computed here in double.
-// Bars: this back end computes attention with f16 operands and the fp32 GEMM in tf32 on the tensor
-// cores, so the bars are 5e-3 (max abs / max |ref|), not the fp32 shaders' 2e-5.
+// Bars: fp32 attention runs in fp32 at the default precision and meets the reference's own 2e-5;
+// the fp32 GEMM runs in tf32 on the tensor cores, so its bar is 5e-3 (max abs / max |ref|).
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -105,7 +105,7 @@ void attention_cases(ofc::gpu::Engine& eng, const std::string& golden) {
         eng.downloadNow(a.out, got.data(), (uint64_t)got.size() * 4);
         double maxAbs;
         const double rel = rel_err(got, ref, &maxAbs);
-        report(rel <= 5e-3, std::string("fusedAttention ") + s.name, maxAbs, rel);
+        report(rel <= 2e-5, std::string("fusedAttention ") + s.name, maxAbs, rel);
         arena.destroy();
     }
 }

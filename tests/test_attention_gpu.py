@@ -28,18 +28,24 @@ def _golden_cases(orc):
         yield e, q, k, v, ref
 
 
-def test_reference_test_shapes_fused_attention(orc, cuda_ok):
+@pytest.mark.parametrize("precision", ["reference", "fast"])
+def test_reference_test_shapes_fused_attention(orc, cuda_ok, precision):
     """tests/fused_attn_test.cpp's four shapes (fp32 buffers) through fusedAttention's replacement,
-    against the reference's own fp64 outputs (golden).  Ours computes in f16 operands, so the bar is
-    5e-3 instead of the fp32 kernels' 2e-5."""
+    against the reference's own fp64 outputs (golden).  At the default precision fp32 inputs are
+    computed in fp32 and meet the reference's own 2e-5; in fast mode they run as f16 operands on the
+    tensor cores (bar 5e-3)."""
     ctx = torch_ops.context()
-    for e, q, k, v, ref in _golden_cases(orc):
-        qd, kd, vd = dev(q), dev(k), dev(v)
-        o = torch.full_like(qd, float("nan"))
-        ctx.fused_attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(), e["Tq"], e["Tk"], e["C"],
-                            e["heads"], e["causal"])
-        check_attn(orc, f"fusedAttention golden Tq={e['Tq']} Tk={e['Tk']} C={e['C']} h={e['heads']}", host(o), ref,
-                   "f32")
+    ctx.set_precision(sdvk_b200.PRECISION_FAST if precision == "fast" else sdvk_b200.PRECISION_REFERENCE)
+    try:
+        for e, q, k, v, ref in _golden_cases(orc):
+            qd, kd, vd = dev(q), dev(k), dev(v)
+            o = torch.full_like(qd, float("nan"))
+            ctx.fused_attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(), e["Tq"], e["Tk"], e["C"],
+                                e["heads"], e["causal"])
+            check_attn(orc, f"fusedAttention[{precision}] golden Tq={e['Tq']} Tk={e['Tk']} C={e['C']} h={e['heads']}",
+                       host(o), ref, "f32_ref" if precision == "reference" else "f32")
+    finally:
+        ctx.set_precision(sdvk_b200.PRECISION_REFERENCE)
 
 
 def test_reference_test_shapes_dispatch(orc, cuda_ok):
@@ -54,7 +60,7 @@ def test_reference_test_shapes_dispatch(orc, cuda_ok):
         push = sdvk_b200.pack_fa(e["Tq"], e["Tk"], e["C"], e["heads"], hd, e["causal"],
                                  float(np.float32(1) / np.sqrt(np.float32(hd))))
         ctx.dispatch(name, bufs, push, (e["Tq"] + 63) // 64, e["heads"], 1)
-        check_attn(orc, f"dispatch {name} golden Tq={e['Tq']}", host(o), ref, "f32")
+        check_attn(orc, f"dispatch {name} golden Tq={e['Tq']}", host(o), ref, "f32_ref")
 
 
 CONFIG1 = [

@@ -2,9 +2,9 @@
 unchanged against the C++ engine mirror (oracle/Makefile target ref-b200 builds them where the
 reference sources are present; the binaries travel with the tree), run on the B200.
 
-They print their own error figures.  The figures are judged against this back end's bars (5e-3 of
-max |ref|: f16 attention operands and tf32 GEMM tensor cores), not the fp32 shaders' 2e-5, which
-fused_attn_test.cpp itself applies and reports as FAIL."""
+fused_attn_test applies the reference's own bar (2e-5 of max |ref|) and must pass: fp32 attention
+runs in fp32 at the default precision.  gemm_q8_bench prints its error without a bar; it is judged
+against this back end's tf32 bar for fp32 activations (5e-3 of max |ref|)."""
 import os
 import re
 import subprocess
@@ -28,7 +28,8 @@ def test_reference_fused_attn_harness_on_b200(cuda_ok):
     r = _run("fused_attn_test_b200")
     rels = [float(x) for x in re.findall(r"^(?:PASS|FAIL) .* rel=(\S+)$", r.stdout, re.M)]
     assert len(rels) == 4, r.stdout + r.stderr
-    assert max(rels) <= 5e-3, rels
+    assert max(rels) <= 2e-5, rels
+    assert r.returncode == 0 and "ALL PASS" in r.stdout, r.stdout
     assert "latency" in r.stdout and "cross 9216x77" in r.stdout
 
 
