@@ -121,6 +121,32 @@ __global__ void geglu_kernel(const __half* __restrict__ h, __half* __restrict__ 
 
 bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// y[r][c] = f16(sum_z part[z][r][c] (+ bias[c])): the split-K partial planes summed in a fixed order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, const float* __restrict__ bias,
+                                     __half* __restrict__ y, uint32_t rows, uint32_t cols, uint32_t splits,
+                                     uint64_t ldy) {
+    const uint64_t plane = (uint64_t)rows * cols, n4 = plane / 4;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
+        float4 a = reinterpret_cast<const float4*>(part)[i];
+        for (uint32_t z = 1; z < splits; ++z) {
+            const float4 b = reinterpret_cast<const float4*>(part + z * plane)[i];
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        const uint64_t e = i * 4;
+        const uint32_t r = (uint32_t)(e / cols), c = (uint32_t)(e % cols);
+        if (bias) {
+            a.x += bias[c];
+            a.y += bias[c + 1];
+            a.z += bias[c + 2];
+            a.w += bias[c + 3];
+        }
+        store4<__half>(y + (uint64_t)r * ldy + c, a.x, a.y, a.z, a.w);
+    }
+}
+
 template <class TO>
 int launch_ln(const float* x, const float* g, const float* b, TO* y, uint32_t rows, uint32_t d, uint64_t ldx,
               uint64_t ldy, float eps, const LaunchEnv& env) {
@@ -162,8 +188,13 @@ int geglu(const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint6
 namespace {
 
 struct BlockLayout {
-    uint64_t n, qkv, a, g, h, total;  // byte offsets into the workspace
+    uint64_t n, qkv, a, g, h, part, total;  // byte offsets into the workspace
 };
+
+// The context's K|V projection has few rows (batch x 77) against a long K: split K so that the GEMM
+// has enough tiles to fill the GPU.
+constexpr uint32_t kKvSplits = 4;
+bool kv_split(uint32_t crow, uint32_t Cc) { return crow <= 512 && Cc % (kKvSplits * 64) == 0; }
 
 uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
 
@@ -178,7 +209,9 @@ BlockLayout block_layout(const sdvk_block_desc& d) {
     L.a = align256(L.qkv + qkv_bytes);
     L.g = align256(L.a + rows * C * 2);
     L.h = align256(L.g + rows * 2 * F * 2);
-    L.total = align256(L.h + rows * F * 2);
+    L.part = align256(L.h + rows * F * 2);
+    const uint64_t part_bytes = kv_split((uint32_t)crow, d.Cctx) ? (uint64_t)kKvSplits * crow * 2 * C * 4 : 0;
+    L.total = align256(L.part + part_bytes);
     return L;
 }
 
@@ -223,6 +256,26 @@ int fused_linears(const void* x, int x_dtype, uint64_t ldx, const sdvk_q8_linear
                              env))
             return rc;
     return SDVK_OK;
+}
+
+// [k | v] = ctx [Wk; Wv]^T for back-to-back weights, K split into kKvSplits GEMM batches: batch z
+// reads the z-th K slice of every row of ctx and of the weight (batch strides smaller than the row
+// strides) and writes its own fp32 plane; splitk_reduce_kernel sums the planes into the f16 output.
+int kv_linear_split(const void* ctx, int ctx_dtype, uint64_t ldctx, const sdvk_q8_linear* w, uint32_t N, uint32_t K,
+                    __half* y, uint64_t ldy, uint32_t rows, float* part, const LaunchEnv& env) {
+    const uint32_t Ks = K / kKvSplits;
+    GemmQ8Desc g = linear_desc(ctx, ctx_dtype, ldctx, sdvk_q8_linear{w[0].q, w[0].s, nullptr}, 2 * N, Ks, part, SDVK_F32,
+                               2ull * N, rows, false);
+    g.ldw = K;
+    g.batch = kKvSplits;
+    g.sx = Ks;
+    g.sw = Ks;
+    g.sc = (uint64_t)rows * 2 * N;
+    if (int rc = gemm_q8(g, env)) return rc;
+    const uint64_t n4 = (uint64_t)rows * 2 * N / 4;
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)env.num_sms * 4);
+    splitk_reduce_kernel<<<blocks, 256, 0, env.stream>>>(part, w[0].bias, y, rows, 2 * N, kKvSplits, ldy);
+    return cuda_check(env, cudaGetLastError(), "splitk_reduce_kernel launch");
 }
 
 sdvk_attn_desc attn_desc(const __half* q, uint64_t ldq, uint64_t sq, const __half* k, const __half* v, uint64_t ldkv,
@@ -288,8 +341,13 @@ int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, con
     if ((rc = layernorm(d.x, d.ln2_w, d.ln2_b, n, SDVK_F16, rows, C, C, C, eps, env))) return rc;
     if ((rc = gemm_q8(linear_desc(n, SDVK_F16, C, d.q2, C, C, q2, SDVK_F16, C, rows, false), env))) return rc;
     const sdvk_q8_linear kv_w[2] = {d.k2, d.v2};
-    if (crow && (rc = fused_linears(d.ctx, d.ctx_dtype, d.Cctx, kv_w, 2, C, d.Cctx, kv2, 2ull * C, crow, env)))
+    if (crow && kv_split(crow, d.Cctx) && contiguous(kv_w, 2, C, d.Cctx) && C % 2 == 0) {
+        if ((rc = kv_linear_split(d.ctx, d.ctx_dtype, d.Cctx, kv_w, C, d.Cctx, kv2, 2ull * C, crow,
+                                  reinterpret_cast<float*>(base + L.part), env)))
+            return rc;
+    } else if (crow && (rc = fused_linears(d.ctx, d.ctx_dtype, d.Cctx, kv_w, 2, C, d.Cctx, kv2, 2ull * C, crow, env))) {
         return rc;
+    }
     at = attn_desc(q2, C, (uint64_t)d.T * C, kv2, kv2 + C, 2ull * C, (uint64_t)d.Tctx * 2 * C, a, C, (uint64_t)d.T * C,
                    d.batch, H, d.T, d.Tctx, hd);
     if ((rc = attention(at, env))) return rc;
