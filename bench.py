@@ -281,7 +281,8 @@ class BlockWorkload:
                 "x ~N(0,1), fp16 context ~N(0,1), LN gamma 1 beta 0")
     bound = "tensor"
     dtype = "f16"
-    # LN, QKV GEMM, attention, out GEMM; LN, Q GEMM, K|V GEMM, attention, out GEMM; LN, FF1, GEGLU, FF2
+    # LN, QKV GEMM, attention, out GEMM; LN, Q GEMM, K|V GEMM (split-K + reduce), attention, out GEMM;
+    # LN, FF1 with GEGLU in its epilogue, FF2
     launches_per_step = 13
 
     def __init__(self):
@@ -322,6 +323,10 @@ class BlockWorkload:
         for i in (1, 2, 3):
             W[f"ln{i}_w"] = torch.ones(C, device=device)
             W[f"ln{i}_b"] = torch.zeros(C, device=device)
+        # the load-time repack that folds GEGLU into the ff.net.0 GEMM (the original stays for the CPU arm)
+        from sdvk_b200 import torch_ops
+
+        W["ff1_il"] = torch_ops.geglu_interleave(*W["ff1"])
         return W
 
     def make_set(self, torch, device, seed):
@@ -341,8 +346,10 @@ class BlockWorkload:
         d.batch, d.T, d.C, d.heads, d.Tctx, d.Cctx, d.ff_inner = self.B, self.T, self.C, self.H, self.Tc, self.Cc, self.F
         for n in ("ln1_w", "ln1_b", "ln2_w", "ln2_b", "ln3_w", "ln3_b"):
             setattr(d, n, self.weights[n].data_ptr())
-        for n in ("q", "k", "v", "o", "q2", "k2", "v2", "o2", "ff1", "ff2"):
+        for n in ("q", "k", "v", "o", "q2", "k2", "v2", "o2", "ff2"):
             setattr(d, n, torch_ops.q8_linear(*self.weights[n]))
+        d.ff1 = torch_ops.q8_linear(*self.weights["ff1_il"])
+        d.ff1_geglu_interleaved = 1
         d.eps = 1e-5
         return d
 

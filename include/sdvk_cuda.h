@@ -192,6 +192,19 @@ SDVK_API int sdvk_layernorm(sdvk_ctx* ctx, const float* x, const float* gamma, c
  * Requirements: F, ldh, ldy multiples of 8, 16-byte aligned bases. */
 SDVK_API int sdvk_geglu(sdvk_ctx* ctx, const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint64_t ldy);
 
+/* GEGLU folded into the ff.net.0 GEMM.  sdvk_geglu_interleave repacks an ff.net.0.proj weight
+ * [2F][K] (+ scales, + optional bias; rows 0..F-1 = a, F..2F-1 = gate) into row order
+ * [a 0..15, gate 0..15, a 16..31, gate 16..31, ...] -- a one-time load-time repack into the caller's
+ * buffers of the same sizes.  sdvk_gemm_q8_nt_geglu then computes
+ * C[m][j] = a[m][j] * gelu_erf(gate[m][j]) (f16 [M][ldc]) for (a | gate) = A . W^T (+ bias) with the
+ * GEGLU applied to the fp32 accumulators, in place of gemm_nt_q8 + geglu (sdvkgen.cpp:1710-1720).
+ * Requirements: F % 16 == 0, K % 32 == 0, 16-byte aligned rows. */
+SDVK_API int sdvk_geglu_interleave(sdvk_ctx* ctx, const int8_t* q, const float* s, const float* bias, uint32_t F,
+                          uint32_t K, int8_t* q_out, float* s_out, float* bias_out);
+SDVK_API int sdvk_gemm_q8_nt_geglu(sdvk_ctx* ctx, const void* A, int a_dtype, const int8_t* q_interleaved,
+                          const float* s_interleaved, const float* bias_interleaved, void* C, uint32_t M, uint32_t F,
+                          uint32_t K, uint32_t lda, uint32_t ldc);
+
 /* One Q8_0 linear layer: int8 weight [N][K] (row stride K), fp32 scale per 32 weights, optional
  * fp32 bias [N] (the loader's split layout, Gguf.cpp:559-583). */
 typedef struct sdvk_q8_linear {
@@ -218,6 +231,7 @@ typedef struct sdvk_block_desc {
     const float *ln1_w, *ln1_b, *ln2_w, *ln2_b, *ln3_w, *ln3_b;
     sdvk_q8_linear q, k, v, o, q2, k2, v2, o2, ff1, ff2;
     float eps;
+    uint32_t ff1_geglu_interleaved;  /* ff1 was repacked by sdvk_geglu_interleave: GEGLU in its epilogue */
 } sdvk_block_desc;
 SDVK_API uint64_t sdvk_transformer_block_workspace(const sdvk_block_desc* desc);
 SDVK_API int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, void* workspace, uint64_t workspace_bytes);

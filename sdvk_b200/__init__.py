@@ -72,6 +72,7 @@ class BlockDesc(ctypes.Structure):
         ("q2", Q8Linear), ("k2", Q8Linear), ("v2", Q8Linear), ("o2", Q8Linear),
         ("ff1", Q8Linear), ("ff2", Q8Linear),
         ("eps", ctypes.c_float),
+        ("ff1_geglu_interleaved", ctypes.c_uint32),
     ]
 
 
@@ -117,6 +118,8 @@ SIGNATURES = {
     "sdvk_comm_abort": (_I, [_P]),
     "sdvk_allgather": (_I, [_P, _P, _P, _P, _U64, _I]),
     "sdvk_comm_wait": (_I, [_P, _P, _U32]),
+    "sdvk_geglu_interleave": (_I, [_P, _P, _P, _P, _U32, _U32, _P, _P, _P]),
+    "sdvk_gemm_q8_nt_geglu": (_I, [_P, _P, _I, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32]),
     "sdvk_layernorm": (_I, [_P, _P, _P, _P, _P, _I, _U32, _U32, _U64, _U64, ctypes.c_float]),
     "sdvk_geglu": (_I, [_P, _P, _P, _U32, _U32, _U64, _U64]),
     "sdvk_transformer_block_workspace": (_U64, [ctypes.POINTER(BlockDesc)]),
@@ -274,6 +277,16 @@ class Context:
                   ldx: int = 0, ldy: int = 0, eps: float = 1e-5) -> None:
         self._check(lib().sdvk_layernorm(self._h, x, gamma or None, beta or None, y, y_dtype, rows, d, ldx or d,
                                          ldy or d, eps), "layernorm")
+
+    def geglu_interleave(self, q: int, s: int, bias: Optional[int], F: int, K: int, q_out: int, s_out: int,
+                         bias_out: Optional[int]) -> None:
+        self._check(lib().sdvk_geglu_interleave(self._h, q, s, bias or None, F, K, q_out, s_out, bias_out or None),
+                    "geglu_interleave")
+
+    def gemm_q8_nt_geglu(self, A: int, a_dtype: int, q: int, s: int, bias: Optional[int], C: int, M: int, F: int,
+                         K: int, lda: int = 0, ldc: int = 0) -> None:
+        self._check(lib().sdvk_gemm_q8_nt_geglu(self._h, A, a_dtype, q, s, bias or None, C, M, F, K, lda, ldc),
+                    "gemm_q8_nt_geglu")
 
     def geglu(self, h: int, y: int, rows: int, F: int, ldh: int = 0, ldy: int = 0) -> None:
         self._check(lib().sdvk_geglu(self._h, h, y, rows, F, ldh or 2 * F, ldy or F), "geglu")

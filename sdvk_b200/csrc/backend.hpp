@@ -39,9 +39,12 @@ struct GemmQ8Desc {
     uint32_t xrows, wrows, K, batch;
     bool nn;
     bool accumulate;
+    bool geglu;  // NT, f16 output: GEGLU-interleaved weight rows, output [rows][wrows / 2]
 };
 
 int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env);
+int geglu_interleave(const int8_t* q, const float* s, const float* bias, uint32_t F, uint32_t K, int8_t* q_out,
+                     float* s_out, float* bias_out, const LaunchEnv& env);
 // cuTensorMapEncodeTiled from the driver (null if unavailable), and the per-device dynamic
 // shared-memory opt-in for a kernel (done once per kernel and device).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();

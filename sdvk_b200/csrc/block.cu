@@ -11,6 +11,7 @@
 //   n = LN1(x); [q|k|v] = n Wqkv^T; a = attn(q, k, v); x += a Wo^T + bo
 //   n = LN2(x); q = n Wq2^T; [k|v] = ctx Wkv2^T; a = attn(q, k, v); x += a Wo2^T + bo2
 //   n = LN3(x); g = n Wff1^T + b1; h = geglu(g); x += h Wff2^T + b2
+//   (with a GEGLU-interleaved ff1 weight the middle two are one GEMM whose epilogue writes h)
 // x is the fp32 residual stream [batch][T][C], updated in place by the accumulating GEMMs; every
 // intermediate is fp16 in the caller's workspace.  Q/K/V (and the cross K/V) run as one GEMM when
 // their weights lie back to back in memory (a [3C][C] weight), else as separate GEMMs writing the
@@ -18,6 +19,7 @@
 #include <cmath>
 
 #include "backend.hpp"
+#include "gemm_q8.cuh"  // gelu_erf_as
 #include "ptx.cuh"
 
 namespace sdvk {
@@ -87,15 +89,6 @@ __global__ void __launch_bounds__(kLnWarps * 32) layernorm_kernel(const float* _
     }
 }
 
-// erf-GELU by Abramowitz & Stegun 7.1.26 (|error of erf| <= 1.5e-7), the reference's formula.
-__device__ __forceinline__ float gelu_erf(float v) {
-    const float xs = v * 0.70710678118654752440f;
-    const float ax = fabsf(xs);
-    const float t = 1.0f / (1.0f + 0.3275911f * ax);
-    const float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
-    const float e = 1.0f - poly * expf(-ax * ax);
-    return 0.5f * v * (1.0f + (xs >= 0.0f ? e : -e));
-}
 
 // y[r][j] = h[r][j] * gelu(h[r][F + j]), 8 halves per thread per step.
 __global__ void geglu_kernel(const __half* __restrict__ h, __half* __restrict__ y, uint32_t rows, uint32_t F,
@@ -113,7 +106,7 @@ __global__ void geglu_kernel(const __half* __restrict__ h, __half* __restrict__ 
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const float2 av = __half22float2(a2[k]), gv = __half22float2(g2[k]);
-            o2[k] = __floats2half2_rn(av.x * gelu_erf(gv.x), av.y * gelu_erf(gv.y));
+            o2[k] = __floats2half2_rn(av.x * gelu_erf_as(gv.x), av.y * gelu_erf_as(gv.y));
         }
         *reinterpret_cast<uint4*>(y + (uint64_t)r * ldy + c) = o;
     }
@@ -354,8 +347,15 @@ int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, con
     if ((rc = gemm_q8(linear_desc(a, SDVK_F16, C, d.o2, C, C, d.x, SDVK_F32, C, rows, true), env))) return rc;
     // ---- GEGLU feed-forward
     if ((rc = layernorm(d.x, d.ln3_w, d.ln3_b, n, SDVK_F16, rows, C, C, C, eps, env))) return rc;
-    if ((rc = gemm_q8(linear_desc(n, SDVK_F16, C, d.ff1, 2 * F, C, g, SDVK_F16, 2ull * F, rows, false), env))) return rc;
-    if ((rc = geglu(g, h, rows, F, 2ull * F, F, env))) return rc;
+    if (d.ff1_geglu_interleaved) {  // GEGLU in the GEMM epilogue: h straight from the accumulators
+        GemmQ8Desc gd = linear_desc(n, SDVK_F16, C, d.ff1, 2 * F, C, h, SDVK_F16, F, rows, false);
+        gd.geglu = true;
+        if ((rc = gemm_q8(gd, env))) return rc;
+    } else {
+        if ((rc = gemm_q8(linear_desc(n, SDVK_F16, C, d.ff1, 2 * F, C, g, SDVK_F16, 2ull * F, rows, false), env)))
+            return rc;
+        if ((rc = geglu(g, h, rows, F, 2ull * F, F, env))) return rc;
+    }
     return gemm_q8(linear_desc(h, SDVK_F16, F, d.ff2, C, F, d.x, SDVK_F32, C, rows, true), env);
 }
 

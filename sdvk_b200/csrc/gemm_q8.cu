@@ -169,7 +169,10 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, d.wq, d.K, d.wrows, d.sw ? d.batch : 1, d.ldw, d.sw,
                   Cfg::kBK, Cfg::kBNC, CU_TENSOR_MAP_SWIZZLE_NONE, env, "weight");
     if (rc) return rc;
-    if (!NN) {
+    if (!NN && d.geglu) {  // 16 output columns per 32 accumulator columns, 32-byte rows
+        rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.wrows / 2, d.xrows, d.batch, d.ldc * ces, d.sc * ces, 16, 32,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, env, "output");
+    } else if (!NN) {
         rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.wrows, d.xrows, d.batch, d.ldc * ces, d.sc * ces, 32, 32,
                       ces == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, env, "output");
     } else {
@@ -187,6 +190,7 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     p.batch = d.batch;
     p.ldw = d.ldw;
     p.sW = d.sw;
+    p.geglu = d.geglu ? 1u : 0u;
     p.tiles_x = (d.xrows + 2 * Cfg::kBM - 1) / (2 * Cfg::kBM);
     p.tiles_w = (d.wrows + Cfg::kBNP - 1) / Cfg::kBNP;
     p.num_tiles = p.tiles_x * p.tiles_w * d.batch;
@@ -247,7 +251,8 @@ template <class TA, bool NN, class TC>
 int launch_bn(const GemmQ8Desc& d, const LaunchEnv& env) {
     const uint64_t pair_tiles = (uint64_t)((d.xrows + 255) / 256) * ((d.wrows + 255) / 256) * d.batch;
     const int forced = variant_override();
-    const bool pair = forced == 2 || (forced == 0 && d.wrows > 128 && pair_tiles * 4 >= (uint64_t)env.num_sms);
+    // the GEGLU epilogue exists in the CTA-pair kernel only
+    const bool pair = d.geglu || forced == 2 || (forced == 0 && d.wrows > 128 && pair_tiles * 4 >= (uint64_t)env.num_sms);
     if (pair) {
         const char* e = getenv("SDVK_GEMM_PAIR_BN");
         const int bn = e ? atoi(e) : pick_pair_bn(d, env.num_sms);
@@ -279,6 +284,30 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+// GEGLU interleave of an ff.net.0.proj weight [2F][K] (rows 0..F-1 = a, F..2F-1 = gate): output row
+// r = 32j + t holds a row 16j + t for t < 16 and gate row 16j + t - 16 otherwise, with its scales and
+// bias, so that each 32-column accumulator chunk of the GEMM holds 16 (a, gate) column pairs.
+__global__ void geglu_interleave_kernel(const int8_t* __restrict__ q, const float* __restrict__ s,
+                                        const float* __restrict__ bias, uint32_t F, uint32_t K, int8_t* q_out,
+                                        float* s_out, float* bias_out) {
+    const uint32_t r = blockIdx.x, t = r & 31, j = r >> 5;
+    const uint32_t src = t < 16 ? 16 * j + t : F + 16 * j + (t - 16);
+    const uint4* qs = reinterpret_cast<const uint4*>(q + (uint64_t)src * K);
+    uint4* qd = reinterpret_cast<uint4*>(q_out + (uint64_t)r * K);
+    for (uint32_t i = threadIdx.x; i < K / 16; i += blockDim.x) qd[i] = qs[i];
+    for (uint32_t i = threadIdx.x; i < K / 32; i += blockDim.x) s_out[(uint64_t)r * (K / 32) + i] = s[(uint64_t)src * (K / 32) + i];
+    if (bias && bias_out && threadIdx.x == 0) bias_out[r] = bias[src];
+}
+
+int geglu_interleave(const int8_t* q, const float* s, const float* bias, uint32_t F, uint32_t K, int8_t* q_out,
+                     float* s_out, float* bias_out, const LaunchEnv& env) {
+    if (!q || !s || !q_out || !s_out || (bias && !bias_out)) return fail(env, SDVK_E_ARG, "null pointer");
+    if (F == 0 || F % 16 || K % 32 || !aligned16(q) || !aligned16(q_out))
+        return fail(env, SDVK_E_SHAPE, "GEGLU interleave needs F % 16 == 0, K % 32 == 0, 16-byte aligned rows");
+    geglu_interleave_kernel<<<2 * F, 128, 0, env.stream>>>(q, s, bias, F, K, q_out, s_out, bias_out);
+    return cuda_check(env, cudaGetLastError(), "geglu_interleave_kernel launch");
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
 bool kernel_smem_attr(const void* kern, int bytes, int device) { return set_smem_attr(kern, bytes, device); }
 
@@ -292,12 +321,14 @@ int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env) {
     if (d.K % 32) return fail(env, SDVK_E_SHAPE, "K must be a multiple of 32 (whole Q8_0 blocks)");
     if (d.ldw % 32 || d.sw % 32 || d.ldw < d.K) return fail(env, SDVK_E_SHAPE, "weight strides must be multiples of 32");
     const int es = dtype_size(d.x_dtype), ces = dtype_size(d.c_dtype);
-    const uint64_t xmin = d.nn ? d.xrows : d.K, cmin = d.nn ? d.xrows : d.wrows;
+    const uint64_t xmin = d.nn ? d.xrows : d.K, cmin = d.nn ? d.xrows : d.geglu ? d.wrows / 2 : d.wrows;
     if (d.ldx < xmin || d.ldc < cmin) return fail(env, SDVK_E_SHAPE, "row stride smaller than the row");
     if (!aligned16(d.x) || !aligned16(d.c) || !aligned16(d.wq))
         return fail(env, SDVK_E_SHAPE, "operands must be 16-byte aligned");
     if ((d.ldx * es) % 16 || (d.ldc * ces) % 16 || (d.batch > 1 && ((d.sx * es) % 16 || (d.sc * ces) % 16)))
         return fail(env, SDVK_E_SHAPE, "row/batch strides must be multiples of 16 bytes");
+    if (d.geglu && (d.nn || d.c_dtype != SDVK_F16 || d.accumulate || d.wrows % 32 || d.ldc < d.wrows / 2 || d.K == 0))
+        return fail(env, SDVK_E_SHAPE, "the GEGLU epilogue needs NT, an F16 output, 32 | rows and K > 0");
     if (d.K == 0) {
         if (d.accumulate && !d.bias) return SDVK_OK;
         if (d.c_dtype != SDVK_F32) return fail(env, SDVK_E_SHAPE, "K == 0 needs an F32 output");

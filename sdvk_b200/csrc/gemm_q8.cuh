@@ -41,7 +41,37 @@ struct GemmQ8Params {
     uint64_t timeout_ns;
     void* c;                // output (direct-store epilogue): NT C[z][x][w], NN C[z][w][x]
     uint64_t ldc, sc;       // output row and batch strides (elements)
+    uint32_t geglu;         // NT only: the weight rows are GEGLU-interleaved (see gemm_q8_geglu), and
+                            // each 32-column chunk [a(16) | gate(16)] is stored as 16 a * gelu(gate)
 };
+
+// erf-GELU with the Abramowitz & Stegun 7.1.26 erf (|error| <= 1.5e-7), the reference's formula
+// (unary_fwd.comp:29-35).
+__device__ __forceinline__ float gelu_erf_as(float v) {
+    const float xs = v * 0.70710678118654752440f;
+    const float ax = fabsf(xs);
+    const float t = 1.0f / (1.0f + 0.3275911f * ax);
+    const float poly =
+        ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    const float e = 1.0f - poly * expf(-ax * ax);
+    return 0.5f * v * (1.0f + (xs >= 0.0f ? e : -e));
+}
+
+// The same formula with the reciprocal and the exponential as single approximate hardware ops
+// (rcp.approx, ex2.approx: a few ulp of fp32), for the GEMM epilogue, whose instruction count shares
+// issue slots with the mainloop's warps; the result is stored in f16.
+__device__ __forceinline__ float gelu_erf_as_fast(float v) {
+    const float xs = v * 0.70710678118654752440f;
+    const float ax = fabsf(xs);
+    float t;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.0f)));
+    const float poly =
+        ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    float ex;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ex) : "f"(-ax * ax * 1.4426950408889634f));
+    const float e = 1.0f - poly * ex;
+    return 0.5f * v * (1.0f + copysignf(e, xs));
+}
 
 template <class TA>
 struct OperandTraits;

@@ -333,6 +333,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 uint8_t* buf = ebuf + (nstore & 1) * 4096;
                 if (lane == 0) bulk_wait_read<1>();  // the store that last used `buf` has read it
                 __syncwarp();
+                if constexpr (!NN && sizeof(TC) == 2) {
+                    if (p.geglu) {  // chunk = [a(16) | gate(16)] -> 16 outputs, a 32-byte row per lane
+                        uint32_t h[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            __half2 t2 = __floats2half2_rn(v[2 * j] * gelu_erf_as_fast(v[16 + 2 * j]),
+                                                           v[2 * j + 1] * gelu_erf_as_fast(v[17 + 2 * j]));
+                            h[j] = *reinterpret_cast<uint32_t*>(&t2);
+                        }
+                        *reinterpret_cast<uint4*>(buf + lane * 32) = make_uint4(h[0], h[1], h[2], h[3]);
+                        *reinterpret_cast<uint4*>(buf + lane * 32 + 16) = make_uint4(h[4], h[5], h[6], h[7]);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_3d(&tmC, buf, w0 / 2, x0, (int)z);
+                            bulk_commit();
+                        }
+                        continue;
+                    }
+                }
                 if constexpr (!NN) store_epi_row<TC>(buf, lane, v);
                 else store_epi_col<TC>(buf, lane, v);
                 fence_proxy_async_smem();

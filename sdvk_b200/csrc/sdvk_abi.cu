@@ -417,6 +417,36 @@ int sdvk_check_finite(sdvk_ctx* ctx, const void* x, int dtype, uint64_t n) {
     return flag ? set_err(ctx, SDVK_E_NOT_FINITE, "non-finite value found") : SDVK_OK;
 }
 
+int sdvk_geglu_interleave(sdvk_ctx* ctx, const int8_t* q, const float* s, const float* bias, uint32_t F, uint32_t K,
+                          int8_t* q_out, float* s_out, float* bias_out) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::geglu_interleave(q, s, bias, F, K, q_out, s_out, bias_out, env_of(ctx));
+}
+
+int sdvk_gemm_q8_nt_geglu(sdvk_ctx* ctx, const void* A, int a_dtype, const int8_t* q, const float* s,
+                          const float* bias, void* C, uint32_t M, uint32_t F, uint32_t K, uint32_t lda, uint32_t ldc) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    sdvk::GemmQ8Desc d{};
+    d.x = A;
+    d.x_dtype = a_dtype;
+    d.ldx = lda ? lda : K;
+    d.wq = q;
+    d.ws = s;
+    d.ldw = K;
+    d.bias = bias;
+    d.c = C;
+    d.c_dtype = SDVK_F16;
+    d.ldc = ldc ? ldc : F;
+    d.xrows = M;
+    d.wrows = 2 * F;
+    d.K = K;
+    d.batch = 1;
+    d.geglu = true;
+    return sdvk::gemm_q8(d, env_of(ctx));
+}
+
 // ------------------------------------------------------------------ transformer block
 int sdvk_layernorm(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, void* y, int y_dtype,
                    uint32_t rows, uint32_t d, uint64_t ldx, uint64_t ldy, float eps) {

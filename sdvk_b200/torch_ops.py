@@ -148,6 +148,7 @@ def transformer_block(x: torch.Tensor, ctx: torch.Tensor, heads: int, weights: d
     for name in ("q", "k", "v", "o", "q2", "k2", "v2", "o2", "ff1", "ff2"):
         setattr(d, name, q8_linear(*weights[name]))
     d.eps = eps
+    d.ff1_geglu_interleaved = int(bool(weights.get("ff1_geglu_interleaved", False)))
     need = Context.block_workspace(d)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
@@ -163,4 +164,28 @@ def cfg_combine(cond: torch.Tensor, uncond: torch.Tensor, cfg: float, rescale: f
     if out is None:
         out = torch.empty_like(c)
     context(c.device).cfg_combine(c.data_ptr(), u.data_ptr(), out.data_ptr(), c.numel(), cfg, rescale)
+    return out
+
+
+def geglu_interleave(q: torch.Tensor, s: torch.Tensor, bias: Optional[torch.Tensor] = None):
+    """Repack an ff.net.0.proj Q8_0 weight [2F, K] for the GEGLU epilogue (sdvk_geglu_interleave)."""
+    two_f, K = q.shape
+    F = two_f // 2
+    qo, so = torch.empty_like(q), torch.empty_like(s)
+    bo = torch.empty_like(bias) if bias is not None else None
+    context(q.device).geglu_interleave(q.data_ptr(), s.data_ptr(), bias.data_ptr() if bias is not None else None,
+                                       F, K, qo.data_ptr(), so.data_ptr(), bo.data_ptr() if bo is not None else None)
+    return qo, so, bo
+
+
+def gemm_q8_nt_geglu(a: torch.Tensor, q_il: torch.Tensor, s_il: torch.Tensor, bias_il: Optional[torch.Tensor] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """a . W^T (+ bias) with GEGLU in the epilogue, for a weight repacked by geglu_interleave: [M, F] f16."""
+    M, K = a.shape
+    F = q_il.shape[0] // 2
+    if out is None:
+        out = torch.empty((M, F), dtype=torch.float16, device=a.device)
+    context(a.device).gemm_q8_nt_geglu(a.data_ptr(), _dt(a), q_il.data_ptr(), s_il.data_ptr(),
+                                       bias_il.data_ptr() if bias_il is not None else None, out.data_ptr(), M, F, K,
+                                       a.stride(0), out.stride(0))
     return out

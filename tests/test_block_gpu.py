@@ -49,6 +49,24 @@ def test_geglu(orc, cuda_ok, rows, F):
     assert st["rel_max"] <= 2e-3, st
 
 
+@pytest.mark.parametrize("rows,F,K", [(2048, 5120, 1280), (300, 256, 640)])
+def test_gemm_geglu_epilogue(orc, cuda_ok, rows, F, K):
+    """ff.net.0 with GEGLU in the GEMM epilogue (weight repacked by sdvk_geglu_interleave) against
+    fp64: a * gelu(gate) for (a | gate) = x W^T + b."""
+    x = orc.normal_f16(14, 0, (rows, K))
+    q, _, sc = orc.q8_weights(14, 1, 2 * F, K)
+    b = orc.normal_f32(14, 2, (2 * F,)) * 0.05
+    qi, si, bi = torch_ops.geglu_interleave(dev(q), dev(sc), dev(b))
+    y = torch_ops.gemm_q8_nt_geglu(torch.from_numpy(x).cuda(), qi, si, bi)
+    g = orc.gemm_nt_q8_f64(x.astype(np.float32), q, sc, b)
+    ref = g[:, :F] * orc._gelu64(g[:, F:])
+    st = orc.err_stats(host(y), ref)
+    record(f"gemm+geglu epilogue {rows}x{2 * F}x{K}", st)
+    # the output is heavy-tailed and stored as f16: its largest values round by 2^-11 of max|ref|,
+    # so the max error is bounded against max|ref| (as for the standalone GEGLU kernel)
+    assert st["finite"] and st["rel_rms"] <= 1e-3 and st["rel_max"] <= 2e-3, st
+
+
 def _weights(orc, seed, C, Cc, F, fused=True, ln_random=False, qkv_bias=False):
     """Random Q8_0 weights of BASELINE config 0's distribution for every linear of the block."""
     W, Wd = {}, {}
@@ -95,17 +113,21 @@ def _weights(orc, seed, C, Cc, F, fused=True, ln_random=False, qkv_bias=False):
 
 
 BLOCK_CASES = [
-    # (B, T, C, heads, Tctx, Cctx, F, fused weights, random LN / q-k-v biases)   config 2 first
-    (2, 1024, 1280, 20, 77, 2048, 5120, True, False),
-    (1, 300, 640, 10, 77, 1024, 1280, False, True),
+    # (B, T, C, heads, Tctx, Cctx, F, fused weights, random LN / q-k-v biases, GEGLU epilogue)
+    (2, 1024, 1280, 20, 77, 2048, 5120, True, False, True),  # config 2
+    (2, 1024, 1280, 20, 77, 2048, 5120, True, False, False),
+    (1, 300, 640, 10, 77, 1024, 1280, False, True, False),
 ]
 
 
-@pytest.mark.parametrize("B,T,C,heads,Tc,Cc,F,fused,rnd", BLOCK_CASES)
-def test_transformer_block(orc, cuda_ok, B, T, C, heads, Tc, Cc, F, fused, rnd):
+@pytest.mark.parametrize("B,T,C,heads,Tc,Cc,F,fused,rnd,il", BLOCK_CASES)
+def test_transformer_block(orc, cuda_ok, B, T, C, heads, Tc, Cc, F, fused, rnd, il):
     """x += attn1(LN1 x); x += attn2(LN2 x, ctx); x += ff2(geglu(ff1(LN3 x))), checked on a sample of
     query rows per image (keys and values cover every token)."""
     W, Wd = _weights(orc, 21, C, Cc, F, fused=fused, ln_random=rnd, qkv_bias=rnd)
+    if il:  # GEGLU folded into the ff1 GEMM's epilogue (the oracle keeps the original weight)
+        Wd["ff1"] = torch_ops.geglu_interleave(*Wd["ff1"])
+        Wd["ff1_geglu_interleaved"] = True
     x = orc.normal_f32(22, 0, (B, T, C))
     ctx = orc.normal_f16(22, 1, (B, Tc, Cc))
     xd = dev(x)
@@ -121,7 +143,7 @@ def test_transformer_block(orc, cuda_ok, B, T, C, heads, Tc, Cc, F, fused, rnd):
     st = orc.err_stats(got - x[:, rows], delta_ref)
     shader = orc.block_shader(x, ctx32, heads, W, rows)
     st_ref = orc.err_stats(shader - x[:, rows], delta_ref)
-    record(f"block B{B} T{T} C{C} h{heads} ctx{Tc}x{Cc} F{F} fused={fused}", st, st_ref)
+    record(f"block B{B} T{T} C{C} h{heads} ctx{Tc}x{Cc} F{F} fused={fused} geglu_epilogue={il}", st, st_ref)
     assert st["finite"], st
     assert st["rel_rms"] <= 5e-3 and st["rel_max_rms"] <= 5e-2, (st, st_ref)
 
