@@ -20,6 +20,8 @@ struct LaunchEnv {
     int num_sms;
     std::string* msg;     // error text for sdvk_last_error
     int precision;        // SDVK_PRECISION_REFERENCE or SDVK_PRECISION_FAST
+    cudaStream_t side;    // the context's second stream, for work that overlaps the main stream
+    cudaEvent_t fork, join;
 };
 
 // One Q8_0 GEMM in kernel terms: x = activation operand, w = quantised weight operand.

@@ -13,7 +13,8 @@
 //   n = LN3(x); g = n Wff1^T + b1; h = geglu(g); x += h Wff2^T + b2
 //   (with a GEGLU-interleaved ff1 weight the middle two are one GEMM whose epilogue writes h)
 // x is the fp32 residual stream [batch][T][C], updated in place by the accumulating GEMMs; every
-// intermediate is fp16 in the caller's workspace.  Q/K/V (and the cross K/V) run as one GEMM when
+// intermediate is fp16 in the caller's workspace.  The context's K|V projection depends on ctx
+// alone and runs on the context's side stream (fork/join events), overlapping the self-attention half.  Q/K/V (and the cross K/V) run as one GEMM when
 // their weights lie back to back in memory (a [3C][C] weight), else as separate GEMMs writing the
 // column blocks of the same [rows][3C] buffer.
 #include <cmath>
@@ -181,7 +182,7 @@ int geglu(const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint6
 namespace {
 
 struct BlockLayout {
-    uint64_t n, qkv, a, g, h, part, total;  // byte offsets into the workspace
+    uint64_t n, qkv, a, g, h, part, kv, total;  // byte offsets into the workspace
 };
 
 // The context's K|V projection has few rows (batch x 77) against a long K: split K so that the GEMM
@@ -197,14 +198,15 @@ BlockLayout block_layout(const sdvk_block_desc& d) {
     BlockLayout L{};
     L.n = 0;
     L.qkv = align256(L.n + rows * C * 2);
-    // [rows][3C] for self-attention, later [rows][C] (cross Q) + [crow][2C] (cross K|V)
-    const uint64_t qkv_bytes = std::max(rows * 3 * C * 2, align256(rows * C * 2) + crow * 2 * C * 2);
-    L.a = align256(L.qkv + qkv_bytes);
+    // [rows][3C] for self-attention, later [rows][C] (cross Q); the cross K|V has its own region, since
+    // it is written on the side stream while the main stream uses this one
+    L.a = align256(L.qkv + rows * 3 * C * 2);
     L.g = align256(L.a + rows * C * 2);
     L.h = align256(L.g + rows * 2 * F * 2);
     L.part = align256(L.h + rows * F * 2);
     const uint64_t part_bytes = kv_split((uint32_t)crow, d.Cctx) ? (uint64_t)kKvSplits * crow * 2 * C * 4 : 0;
-    L.total = align256(L.part + part_bytes);
+    L.kv = align256(L.part + part_bytes);
+    L.total = align256(L.kv + crow * 2 * C * 2);
     return L;
 }
 
@@ -316,12 +318,32 @@ int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, con
     __half* n = reinterpret_cast<__half*>(base + L.n);
     __half* qkv = reinterpret_cast<__half*>(base + L.qkv);
     __half* q2 = qkv;
-    __half* kv2 = reinterpret_cast<__half*>(base + L.qkv + align256((uint64_t)rows * C * 2));
+    __half* kv2 = reinterpret_cast<__half*>(base + L.kv);
     __half* a = reinterpret_cast<__half*>(base + L.a);
     __half* g = reinterpret_cast<__half*>(base + L.g);
     __half* h = reinterpret_cast<__half*>(base + L.h);
     const float eps = d.eps > 0.0f ? d.eps : 1e-5f;
     int rc;
+    // ---- the context's K|V projection depends on ctx alone: it runs on the side stream, forked here
+    //      and joined before the cross-attention, overlapping the self-attention half
+    const sdvk_q8_linear kv_w[2] = {d.k2, d.v2};
+    LaunchEnv side = env;
+    side.stream = env.side;
+    const bool fork = crow && env.side && env.fork && env.join;
+    if (fork) {
+        if ((rc = cuda_check(env, cudaEventRecord(env.fork, env.stream), "fork"))) return rc;
+        if ((rc = cuda_check(env, cudaStreamWaitEvent(env.side, env.fork, 0), "fork"))) return rc;
+    }
+    const LaunchEnv& kv_env = fork ? side : env;
+    if (crow && kv_split(crow, d.Cctx) && contiguous(kv_w, 2, C, d.Cctx) && C % 2 == 0) {
+        if ((rc = kv_linear_split(d.ctx, d.ctx_dtype, d.Cctx, kv_w, C, d.Cctx, kv2, 2ull * C, crow,
+                                  reinterpret_cast<float*>(base + L.part), kv_env)))
+            return rc;
+    } else if (crow && (rc = fused_linears(d.ctx, d.ctx_dtype, d.Cctx, kv_w, 2, C, d.Cctx, kv2, 2ull * C, crow,
+                                           kv_env))) {
+        return rc;
+    }
+    if (fork && (rc = cuda_check(env, cudaEventRecord(env.join, env.side), "join"))) return rc;
     // ---- self-attention
     if ((rc = layernorm(d.x, d.ln1_w, d.ln1_b, n, SDVK_F16, rows, C, C, C, eps, env))) return rc;
     const sdvk_q8_linear qkv_w[3] = {d.q, d.k, d.v};
@@ -333,14 +355,7 @@ int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, con
     // ---- cross-attention against the context
     if ((rc = layernorm(d.x, d.ln2_w, d.ln2_b, n, SDVK_F16, rows, C, C, C, eps, env))) return rc;
     if ((rc = gemm_q8(linear_desc(n, SDVK_F16, C, d.q2, C, C, q2, SDVK_F16, C, rows, false), env))) return rc;
-    const sdvk_q8_linear kv_w[2] = {d.k2, d.v2};
-    if (crow && kv_split(crow, d.Cctx) && contiguous(kv_w, 2, C, d.Cctx) && C % 2 == 0) {
-        if ((rc = kv_linear_split(d.ctx, d.ctx_dtype, d.Cctx, kv_w, C, d.Cctx, kv2, 2ull * C, crow,
-                                  reinterpret_cast<float*>(base + L.part), env)))
-            return rc;
-    } else if (crow && (rc = fused_linears(d.ctx, d.ctx_dtype, d.Cctx, kv_w, 2, C, d.Cctx, kv2, 2ull * C, crow, env))) {
-        return rc;
-    }
+    if (fork && (rc = cuda_check(env, cudaStreamWaitEvent(env.stream, env.join, 0), "join"))) return rc;
     at = attn_desc(q2, C, (uint64_t)d.T * C, kv2, kv2 + C, 2ull * C, (uint64_t)d.Tctx * 2 * C, a, C, (uint64_t)d.T * C,
                    d.batch, H, d.T, d.Tctx, hd);
     if ((rc = attention(at, env))) return rc;

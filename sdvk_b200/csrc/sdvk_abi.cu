@@ -22,6 +22,8 @@ struct sdvk_ctx {
     uint64_t timeout_ns = 2000000000ull;
     int precision = SDVK_PRECISION_REFERENCE;
     cudaEvent_t step_done = nullptr;
+    cudaStream_t side = nullptr;  // second stream for overlapping work (forked from and joined to `stream`)
+    cudaEvent_t fork = nullptr, join = nullptr;
     bool in_step = false;
     bool step_recorded = false;
     std::string last_error;
@@ -66,8 +68,8 @@ int use_device(sdvk_ctx* ctx) {
 }
 
 sdvk::LaunchEnv env_of(sdvk_ctx* ctx) {
-    return sdvk::LaunchEnv{ctx->stream, ctx->err_dev, ctx->timeout_ns, ctx->device, ctx->num_sms, &ctx->last_error,
-                           ctx->precision};
+    return sdvk::LaunchEnv{ctx->stream, ctx->err_dev,  ctx->timeout_ns, ctx->device, ctx->num_sms,
+                           &ctx->last_error, ctx->precision, ctx->side,   ctx->fork,   ctx->join};
 }
 
 // After a synchronisation point: surface (and clear) any device-side error code.
@@ -122,6 +124,9 @@ int sdvk_ctx_create(int device, sdvk_ctx** out) {
     if (!rc) rc = cuda_err(ctx, cudaMalloc(&ctx->err_dev, 256), "cudaMalloc(error word)");
     if (!rc) rc = cuda_err(ctx, cudaMemset(ctx->err_dev, 0, 256), "cudaMemset");
     if (!rc) rc = cuda_err(ctx, cudaEventCreateWithFlags(&ctx->step_done, cudaEventDisableTiming), "event");
+    if (!rc) rc = cuda_err(ctx, cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking), "side stream");
+    if (!rc) rc = cuda_err(ctx, cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming), "event");
+    if (!rc) rc = cuda_err(ctx, cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming), "event");
     if (rc) {
         sdvk_ctx_destroy(ctx);
         return rc;
@@ -139,6 +144,10 @@ int sdvk_ctx_destroy(sdvk_ctx* ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->step_done) cudaEventDestroy(ctx->step_done);
+    if (ctx->side) cudaStreamSynchronize(ctx->side);
+    if (ctx->fork) cudaEventDestroy(ctx->fork);
+    if (ctx->join) cudaEventDestroy(ctx->join);
+    if (ctx->side) cudaStreamDestroy(ctx->side);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
