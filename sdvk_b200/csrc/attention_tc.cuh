@@ -13,7 +13,8 @@
 //                O_g += P_g . V_t           (M 128, N 64, K 128; A = P from tensor memory)
 //   warps 0-3  softmax group A (even tiles), warps 4-7 group B (odd tiles): thread = one query row
 //              = one TMEM lane.  It reads its row of S from TMEM, applies the mask and the online
-//              softmax (exp2 domain), writes P as 16-bit values back over S in TMEM, and rescales
+//              softmax (exp2 domain; a quarter of the exponentials by polynomial on the FMA pipe),
+//              writes P as 16-bit values back over S in TMEM, and rescales
 //              its O row in TMEM only when the running maximum grew by more than 2^8.
 // S is triple-buffered (tile t in buffer t % 3), so the MMA computes S for the next tile of a group
 // while that group is still turning its current S into P: a group waits for the tensor core only
@@ -318,9 +319,12 @@ __global__ void __launch_bounds__(384, 1)
                 uint32_t pk[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    float x0, x1;
+                    float x0, x1, p0, p1;
                     f2_unpack(ffma2(f2_pack(s[64 * h + 2 * j], s[64 * h + 2 * j + 1]), sl2, nmb2), x0, x1);
-                    const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+                    // one pair in four on the FMA pipe, the rest on the MUFU: the MUFU is the
+                    // softmax's busiest pipe and the FMA pipe has room
+                    if ((j & 3) == 3) exp2_poly_pair(x0, x1, p0, p1);
+                    else p0 = ex2_approx(x0), p1 = ex2_approx(x1);
                     pk[j] = Half16Pack<T>::pack(p0, p1);
                     sum2[j & 3] = fadd2(sum2[j & 3], f2_pack(p0, p1));
                 }
