@@ -150,34 +150,34 @@ bool pdl_enabled() {
     return !(e && e[0] == '0');
 }
 
-// CTA-pair variant: 256 x BNP tiles on two SMs (cta_group::2).
-template <class TA, int BNP, bool NN, class TC>
+// CTA-pair variant: 256 (weight rows) x BNX (activation rows) tiles on two SMs (cta_group::2).
+template <class TA, int BNX, bool NN, class TC>
 int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
-    using Cfg = Gemm2Config<TA, BNP>;
+    using Cfg = Gemm2Config<TA, BNX>;
     const int es = sizeof(TA), ces = sizeof(TC);
-    CUtensorMap tmA, tmW, tmC;
+    CUtensorMap tmX, tmW, tmC;
     int rc;
     if (!NN) {
-        rc = make_map(&tmA, tma_type(d.x_dtype), d.x, d.K, d.xrows, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
-                      Cfg::kBM, CU_TENSOR_MAP_SWIZZLE_128B, env, "activation");
+        rc = make_map(&tmX, tma_type(d.x_dtype), d.x, d.K, d.xrows, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
+                      Cfg::kBXC, CU_TENSOR_MAP_SWIZZLE_128B, env, "activation");
     } else {
-        rc = make_map(&tmA, tma_type(d.x_dtype), d.x, d.xrows, d.K, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
+        rc = make_map(&tmX, tma_type(d.x_dtype), d.x, d.xrows, d.K, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
                       Cfg::kBK, es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B, env,
                       "activation");
     }
     if (rc) return rc;
     rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, d.wq, d.K, d.wrows, d.sw ? d.batch : 1, d.ldw, d.sw,
-                  Cfg::kBK, Cfg::kBNC, CU_TENSOR_MAP_SWIZZLE_NONE, env, "weight");
+                  Cfg::kBK, Cfg::kBW, CU_TENSOR_MAP_SWIZZLE_NONE, env, "weight");
     if (rc) return rc;
-    if (!NN && d.geglu) {  // 16 output columns per 32 accumulator columns, 32-byte rows
+    if (!NN && d.geglu) {  // 16 output columns per 32 weight rows: [32 x][16] f16 tiles
         rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.wrows / 2, d.xrows, d.batch, d.ldc * ces, d.sc * ces, 16, 32,
                       CU_TENSOR_MAP_SWIZZLE_NONE, env, "output");
-    } else if (!NN) {
+    } else if (!NN) {  // the accumulator transposed: [32 x][32 w] tiles
         rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.wrows, d.xrows, d.batch, d.ldc * ces, d.sc * ces, 32, 32,
-                      ces == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, env, "output");
-    } else {
-        rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.xrows, d.wrows, d.batch, d.ldc * ces, d.sc * ces, 32, 32,
                       CU_TENSOR_MAP_SWIZZLE_NONE, env, "output");
+    } else {  // [32 w][32 x] swizzled rows
+        rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.xrows, d.wrows, d.batch, d.ldc * ces, d.sc * ces, 32, 32,
+                      ces == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, env, "output");
     }
     if (rc) return rc;
     GemmQ8Params p{};
@@ -191,8 +191,8 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     p.ldw = d.ldw;
     p.sW = d.sw;
     p.geglu = d.geglu ? 1u : 0u;
-    p.tiles_x = (d.xrows + 2 * Cfg::kBM - 1) / (2 * Cfg::kBM);
-    p.tiles_w = (d.wrows + Cfg::kBNP - 1) / Cfg::kBNP;
+    p.tiles_x = (d.xrows + Cfg::kBNX - 1) / Cfg::kBNX;
+    p.tiles_w = (d.wrows + 2 * Cfg::kBW - 1) / (2 * Cfg::kBW);
     p.num_tiles = p.tiles_x * p.tiles_w * d.batch;
     p.k_stages = (d.K + Cfg::kBK - 1) / Cfg::kBK;
     p.accumulate = d.accumulate ? 1u : 0u;
@@ -201,7 +201,7 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     p.c = d.c;
     p.ldc = d.ldc;
     p.sc = d.sc;
-    auto kern = gemm_q8_tc2_kernel<TA, BNP, NN, TC>;
+    auto kern = gemm_q8_tc2_kernel<TA, BNX, NN, TC>;
     if (!set_smem_attr(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, env.device))
         return fail(env, SDVK_E_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
     const uint32_t clusters = std::min<uint32_t>(p.num_tiles, (uint32_t)env.num_sms / 2);
@@ -217,20 +217,23 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_check(env, cudaLaunchKernelEx(&cfg, kern, tmA, tmW, tmC, p), "gemm_q8_tc2_kernel launch");
+    return cuda_check(env, cudaLaunchKernelEx(&cfg, kern, tmX, tmW, tmC, p), "gemm_q8_tc2_kernel launch");
 }
 
-// Pair-tile width (tensor-core N): the candidate minimising waves x per-tile cost, where a tile
-// costs its N plus a fixed share (activation traffic and per-tile overheads do not shrink with N).
-int pick_pair_bn(const GemmQ8Desc& d, int num_sms) {
+// Pair-tile width (tensor-core N = activation rows): the candidate minimising waves x per-tile
+// cost, where a tile costs its N plus a fixed share (the 256 weight rows' dequantisation and the
+// per-tile overheads do not shrink with N).  NN stages activations as 64-column blocks per CTA,
+// so its widths are 128 and 256.
+int pick_pair_bn(const GemmQ8Desc& d, int num_sms, bool nn) {
     const int clusters = num_sms / 2;
-    const uint64_t xt = (d.xrows + 255) / 256;
+    const uint64_t wt = (d.wrows + 255) / 256;
     int best = 256;
     uint64_t best_cost = ~0ull;
-    for (int bn : {256, 224, 160, 128}) {
-        const uint64_t tiles = xt * ((d.wrows + bn - 1) / bn) * d.batch;
+    for (int bn : {256, 224, 192, 160, 128}) {
+        if (nn && bn % 128) continue;
+        const uint64_t tiles = wt * ((d.xrows + bn - 1) / bn) * d.batch;
         const uint64_t waves = (tiles + clusters - 1) / clusters;
-        const uint64_t cost = waves * (uint64_t)(bn + 256);  // measured: the fixed per-tile share ~ N=256
+        const uint64_t cost = waves * (uint64_t)(bn + 256);
         if (cost < best_cost) {
             best_cost = cost;
             best = bn;
@@ -241,7 +244,7 @@ int pick_pair_bn(const GemmQ8Desc& d, int num_sms) {
 
 // Kernel choice: the CTA-pair kernel when the problem fills at least about half of the SM pairs
 // with 256 x 256 tiles; otherwise single-CTA tiles (128 x 128 or 128 x 256) give more parallelism.
-// SDVK_GEMM_VARIANT=1sm|2sm forces one of them.
+// SDVK_GEMM_VARIANT=1sm|2sm forces one of them; SDVK_GEMM_PAIR_BN forces the pair tile width.
 int variant_override() {
     const char* e = getenv("SDVK_GEMM_VARIANT");
     return (e && e[0] == '1') ? 1 : (e && e[0] == '2') ? 2 : 0;
@@ -255,11 +258,16 @@ int launch_bn(const GemmQ8Desc& d, const LaunchEnv& env) {
     const bool pair = d.geglu || forced == 2 || (forced == 0 && d.wrows > 128 && pair_tiles * 4 >= (uint64_t)env.num_sms);
     if (pair) {
         const char* e = getenv("SDVK_GEMM_PAIR_BN");
-        const int bn = e ? atoi(e) : pick_pair_bn(d, env.num_sms);
-        if (bn == 224) return launch_pair<TA, 224, NN, TC>(d, env);
-        if (bn == 160) return launch_pair<TA, 160, NN, TC>(d, env);
-        if (bn == 128) return launch_pair<TA, 128, NN, TC>(d, env);
-        return launch_pair<TA, 256, NN, TC>(d, env);
+        int bn = e ? atoi(e) : pick_pair_bn(d, env.num_sms, NN);
+        if constexpr (NN) {
+            return bn == 128 ? launch_pair<TA, 128, NN, TC>(d, env) : launch_pair<TA, 256, NN, TC>(d, env);
+        } else {
+            if (bn == 224) return launch_pair<TA, 224, NN, TC>(d, env);
+            if (bn == 192) return launch_pair<TA, 192, NN, TC>(d, env);
+            if (bn == 160) return launch_pair<TA, 160, NN, TC>(d, env);
+            if (bn == 128) return launch_pair<TA, 128, NN, TC>(d, env);
+            return launch_pair<TA, 256, NN, TC>(d, env);
+        }
     }
     if (d.wrows <= 128) return launch<TA, 128, NN, TC>(d, env);
     return launch<TA, 256, NN, TC>(d, env);

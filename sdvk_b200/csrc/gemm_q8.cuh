@@ -551,26 +551,25 @@ __global__ void __launch_bounds__(512, 1)
         constexpr int T = Cfg::kTasksPerThread;
         const uint32_t my_tiles = (p.num_tiles > blockIdx.x) ? (p.num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
         const uint32_t my_iters = my_tiles * p.k_stages;
-        // Scales are loaded two stages ahead of use so their L2 latency is hidden.
+        // Scales come from L2 kRing stages ahead of use, into a ring of registers indexed by
+        // compile-time constants (the loop body is unrolled over the ring), so no instruction touches
+        // a scale before its load has had kRing stages to land.
+        constexpr int kRing = 4;
         WeightCursor<T> cur;
         cur.init(&p, blockIdx.x, gridDim.x, row0, kRowStep, Cfg::kBK, chunk * 16, BN, 0, BN);
-        float sc0[T], sc1[T], sc2[T];
+        float sc[kRing][T];
         uint4 unused[T];
-        cur.load<false>(sc0, unused);
-        cur.advance();
-        cur.load<false>(sc1, unused);
-        cur.advance();
-        for (uint32_t it = 0; ok && it < my_iters; ++it) {
-            cur.load<false>(sc2, unused);
+#pragma unroll
+        for (int j = 0; j < kRing; ++j) {
+            cur.load<false>(sc[j], unused);
             cur.advance();
+        }
+        auto stage = [&](uint32_t it, float(&scale)[T]) -> bool {
             const uint32_t slot = it % Cfg::kStages, ph = (it / Cfg::kStages) & 1;
             const uint32_t bslot = it % Cfg::kBStages, bph = (it / Cfg::kBStages) & 1;
             const bool got =
                 mbar_wait(&w_full[slot], ph, p.timeout_ns) && mbar_wait(&b_empty[bslot], bph ^ 1, p.timeout_ns);
-            if (!__all_sync(0xffffffffu, got)) {  // the warp leaves the loop together
-                fail();
-                break;
-            }
+            if (!__all_sync(0xffffffffu, got)) return false;  // the warp leaves the loop together
             const uint8_t* wsrc = sW + slot * Cfg::kWBytes;
             uint8_t* bdst = sB + bslot * Cfg::kBBytes;
             uint4 raw[T];
@@ -580,7 +579,7 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
             for (int t = 0; t < T; ++t) {
                 const int r = row0 + t * kRowStep;
-                dequant16<TA>(raw[t], sc0[t], bdst + r * 128, r, chunk * Cfg::kES);  // 16 elements = kES chunks
+                dequant16<TA>(raw[t], scale[t], bdst + r * 128, r, chunk * Cfg::kES);  // 16 elements = kES chunks
             }
             fence_proxy_async_smem();
             __syncwarp();
@@ -588,10 +587,18 @@ __global__ void __launch_bounds__(512, 1)
                 mbar_arrive(&w_empty[slot]);
                 mbar_arrive(&b_full[bslot]);
             }
+            cur.load<false>(scale, unused);  // the scales of stage it + kRing
+            cur.advance();
+            return true;
+        };
+        for (uint32_t it = 0; ok && it < my_iters; it += kRing) {
 #pragma unroll
-            for (int t = 0; t < T; ++t) {
-                sc0[t] = sc1[t];
-                sc1[t] = sc2[t];
+            for (int j = 0; j < kRing; ++j) {
+                if (it + j >= my_iters) break;
+                if (!stage(it + j, sc[j])) {
+                    fail();
+                    break;
+                }
             }
         }
     } else if (warp >= 12) {

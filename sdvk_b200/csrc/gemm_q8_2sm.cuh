@@ -1,46 +1,58 @@
 // gemm_q8_2sm.cuh -- the Q8_0 GEMM on CTA pairs (tcgen05 cta_group::2).
 //
-// A cluster of two CTAs on one TPC computes a 256 (x rows) x BNP (w rows) tile with one
-// tcgen05.mma.cta_group::2 per 16-element K step, issued by the even CTA.  Each CTA stages its own
-// 128 activation rows and dequantises only its own BNP/2 weight rows, so per SM the dequantisation
-// work and the weight traffic are half of the single-CTA kernel's for the same tensor-core work.
-// The accumulator rows each CTA owns land in its own TMEM; each CTA runs its own epilogue.
+// A cluster of two CTAs on one TPC computes a 256 (w rows) x BNX (x rows) tile with one
+// tcgen05.mma.cta_group::2 per 16-element K step, issued by the even CTA.  Operand roles:
+//   A (tensor-core M, 128 rows per CTA)  the dequantised weights: each CTA dequantises its own 128
+//                                        weight rows into its own shared memory, and only its own
+//                                        SM's tensor core reads them;
+//   B (tensor-core N, BNX/2 rows per CTA) the activations, staged by TMA; both SMs' tensor cores
+//                                        read both halves.
+// With the operand written by generic stores (the dequantised weights) on the per-CTA side, the
+// data a tensor core reads from generic stores is always its own SM's, ordered by a CTA-scope
+// proxy fence; the activations that both SMs read arrive by TMA.  The 256 weight rows of a tile
+// also divide the model's widths (1280, 10240) exactly.
+// The accumulator D[w][x] (TMEM lane = weight row, column = activation row) is stored transposed
+// for NT (C[x][w]) and directly for NN (C[w][x]).
 //
 // The tensor pipe idles whenever the issuing thread polls a barrier that is not yet complete, so
 // its per-stage control path is one CTA-scope poll of one barrier and one commit:
-//   full[s]   (even CTA)  activation TMA bytes of both CTAs (cta_group::2 TMA) + the 16
-//                         dequantiser warps of both CTAs; the even CTA's producer sets the tx count
+//   full[s]   (even CTA)  activation TMA bytes of both CTAs (cta_group::2 TMA) + one dequantiser
+//                         group's warps of both CTAs; the even CTA's producer sets the tx count
 //   empty[s]  (each CTA)  one MMA commit multicast to both CTAs frees activation and operand slot s
 //   acc_full  (each CTA)  MMA commit multicast;  acc_empty (even CTA): the 8 epilogue warps
 //   w_full, w_empty (each CTA)  the local raw int8 weight ring (TMA -> dequantisers)
 // Warp roles per CTA: 0 activation TMA, 1 TMEM + MMA (even CTA issues), 2 weight TMA,
-// 4-11 dequantisers, 12-15 epilogue (3 idle).
+// 4-11 dequantisers in groups that take stages round-robin, 12-15 epilogue (3 idle).  One warp's pass
+// over a stage is a chain of waits, shared-memory round trips, a proxy fence and a remote arrive
+// that lasts several times the stage's MMA time, so several groups keep several stages in flight.
 //
 // Every wait is bounded (GemmQ8Params::timeout_ns): a wait that runs out records kErrTimeout, the
 // CTA drains what it issued, both CTAs meet at the final cluster barrier and free TMEM.
 #pragma once
 
+#include <type_traits>
+
 #include "gemm_q8.cuh"
 
 namespace sdvk {
 
-template <class TA, int BNP>
+template <class TA, int BNX>
 struct Gemm2Config {
-    static constexpr int kBM = 128;       // activation rows per CTA (pair: 256)
-    static constexpr int kBNP = BNP;      // weight rows per pair tile (tensor-core N)
-    static constexpr int kBNC = BNP / 2;  // weight rows dequantised by each CTA
+    static constexpr int kBW = 128;       // weight rows per CTA (pair: 256, tensor-core M)
+    static constexpr int kBNX = BNX;      // activation rows per pair tile (tensor-core N)
+    static constexpr int kBXC = BNX / 2;  // activation rows staged by each CTA
     static constexpr int kES = sizeof(TA);
     static constexpr int kBK = 128 / kES;
     static constexpr int kUmmaK = 32 / kES;
-    static constexpr int kS = 5;          // stages of (activation tile, dequantised weight tile)
+    static constexpr int kS = 5;          // stages of (dequantised weight tile, activation tile)
     static constexpr int kSW = 4;         // raw int8 weight stages
     static constexpr int kAcc = 2;
-    static constexpr int kABytes = kBM * 128;
-    static constexpr int kBBytes = kBNC * 128;
-    static constexpr int kStageBytes = kABytes + ((kBBytes + 1023) / 1024) * 1024;
-    static constexpr int kWBytes = kBNC * kBK;
+    static constexpr int kABytes = kBW * 128;
+    static constexpr int kXBytes = kBXC * 128;
+    static constexpr int kStageBytes = kABytes + ((kXBytes + 1023) / 1024) * 1024;
+    static constexpr int kWBytes = kBW * kBK;
     static constexpr int kEpiBytes = 4 * 2 * 4096;  // 4 epilogue warps x 2 buffers x 32x32 fp32
-    static constexpr uint32_t kTmemCols = 512;
+    static constexpr uint32_t kTmemCols = (kAcc * BNX <= 256) ? 256 : 512;
     static constexpr int kOffStage = 0;
     static constexpr int kOffW = kOffStage + kS * kStageBytes;
     static constexpr int kOffEpi = kOffW + ((kSW * kWBytes + 1023) / 1024) * 1024;
@@ -48,22 +60,27 @@ struct Gemm2Config {
     static constexpr int kNumBars = 2 * kS + 2 * kSW + 2 * kAcc + 1;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
     static constexpr int kThreads = 512;
-    static constexpr int kConvThreads = 256;
+    // dequantiser groups (stages round-robin); bf16's dequantisation goes through fp32 and needs
+    // the registers of a two-group split
+    static constexpr int kDqGroups = std::is_same<TA, __nv_bfloat16>::value ? 2 : 4;
+    static constexpr int kDqWarps = 8 / kDqGroups;  // warps per group
+    static constexpr int kConvThreads = 32 * kDqWarps;
     static constexpr int kChunksPerRow = kBK / 16;
-    static constexpr int kTasksPerThread = (kBNC * kChunksPerRow + kConvThreads - 1) / kConvThreads;
+    static constexpr int kTasksPerThread = kBW * kChunksPerRow / kConvThreads;
     static constexpr int kRowStep = kConvThreads / kChunksPerRow;
     static_assert(kSmemBytes <= 232448, "shared memory");
-    static_assert(BNP % 32 == 0 && BNP >= 128 && BNP <= 256, "pair tile N");
+    static_assert(BNX % 32 == 0 && BNX >= 64 && BNX <= 256, "pair tile N");
+    static_assert((kBW * kChunksPerRow) % kConvThreads == 0, "dequant task split");
 };
 
-template <class TA, int BNP, bool NN, class TC>
+template <class TA, int BNX, bool NN, class TC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
-    gemm_q8_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+    gemm_q8_tc2_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmC, const GemmQ8Params p) {
-    using Cfg = Gemm2Config<TA, BNP>;
+    using Cfg = Gemm2Config<TA, BNX>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sStage = smem + Cfg::kOffStage;  // stage s: activation tile, then dequantised weights
+    uint8_t* sStage = smem + Cfg::kOffStage;  // stage s: dequantised weights, then activations
     uint8_t* sW = smem + Cfg::kOffW;
     uint8_t* sEpi = smem + Cfg::kOffEpi;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
@@ -84,12 +101,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < Cfg::kS; ++i) {
-            mbar_init(&full[i], 1 + 16);  // producer's expect_tx + 16 dequantiser warps
+            mbar_init(&full[i], 1 + 2 * Cfg::kDqWarps);  // producer's expect_tx + one group's warps of both CTAs
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < Cfg::kSW; ++i) {
             mbar_init(&w_full[i], 1);
-            mbar_init(&w_empty[i], 8);
+            mbar_init(&w_empty[i], Cfg::kDqWarps);
         }
         for (int i = 0; i < Cfg::kAcc; ++i) {
             mbar_init(&acc_full[i], 1);
@@ -99,7 +116,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmX);
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmC);
     }
@@ -121,7 +138,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         atomicOr(p.err, kErrTimeout);
         ok = false;
     };
-    // Pair tiles: tiles_x counts 256-row pair tiles.
+    // Pair tiles: tiles_w counts 256-row weight tiles (fastest, so the clusters working at one time
+    // share activation rows in L2), tiles_x counts BNX-row activation tiles.
     auto decode = [&](uint32_t tile, uint32_t& z, uint32_t& xt, uint32_t& wt) {
         wt = tile % p.tiles_w;
         const uint32_t rest = tile / p.tiles_w;
@@ -138,7 +156,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             for (uint32_t i = 0; ok && i < my_tiles; ++i) {
                 uint32_t z, xt, wt;
                 decode(cid + i * ncl, z, xt, wt);
-                const int x0 = (int)(xt * 2 * Cfg::kBM + rank * Cfg::kBM);
+                const int x0 = (int)(xt * Cfg::kBNX + rank * Cfg::kBXC);
                 for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
                     const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
                     const int k0 = (int)(ks * Cfg::kBK);
@@ -146,15 +164,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                         fail();
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kABytes);  // both CTAs' bytes
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kXBytes);  // both CTAs' bytes
                     const uint32_t full_l = mapa_shared(&full[s], 0);
-                    uint8_t* a_dst = sStage + s * Cfg::kStageBytes;
+                    uint8_t* x_dst = sStage + s * Cfg::kStageBytes + Cfg::kABytes;
                     if constexpr (!NN) {
-                        tma_load_3d_pair(a_dst, &tmA, full_l, k0, x0, (int)z);
-                    } else {
+                        tma_load_3d_pair(x_dst, &tmX, full_l, k0, x0, (int)z);
+                    } else {  // [K][x] activations: kBXC / kBK column blocks of kBK x kBK
 #pragma unroll
-                        for (int j = 0; j < Cfg::kBM / Cfg::kBK; ++j)
-                            tma_load_3d_pair(a_dst + j * Cfg::kBK * 128, &tmA, full_l, x0 + j * Cfg::kBK, k0, (int)z);
+                        for (int j = 0; j < Cfg::kBXC / Cfg::kBK; ++j)
+                            tma_load_3d_pair(x_dst + j * Cfg::kBK * 128, &tmX, full_l, x0 + j * Cfg::kBK, k0, (int)z);
                     }
                 }
             }
@@ -176,7 +194,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                     }
                     mbar_arrive_expect_tx(&w_full[sw], Cfg::kWBytes);
                     tma_load_3d(sW + sw * Cfg::kWBytes, &tmW, &w_full[sw], (int)(ks * Cfg::kBK),
-                                (int)(wt * Cfg::kBNP + rank * Cfg::kBNC), zw);
+                                (int)(wt * 2 * Cfg::kBW + rank * Cfg::kBW), zw);
                 }
             }
             for (uint32_t i = (it > Cfg::kSW ? it - Cfg::kSW : 0); i < it; ++i)  // drain
@@ -189,17 +207,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         // spends between MMAs can be tensor-pipe idle time.
         if (leader) {
             constexpr uint32_t idesc =
-                make_idesc(OperandTraits<TA>::kFmt, OperandTraits<TA>::kFmt, NN ? 1 : 0, 0, 2 * Cfg::kBM, Cfg::kBNP);
+                make_idesc(OperandTraits<TA>::kFmt, OperandTraits<TA>::kFmt, 0, NN ? 1 : 0, 2 * Cfg::kBW, Cfg::kBNX);
             // Operand descriptors of stage 0; a stage adds kStageBytes, a K step of kUmmaK elements
             // adds 32 bytes (K-major) or kUmmaK rows of 128 bytes (MN-major activations).
             const uint32_t a0 = smem_u32(sStage);
-            uint64_t adesc0;
-            if constexpr (!NN) adesc0 = smem_desc_sw128(a0, 16, 1024);
-            else if constexpr (!OperandTraits<TA>::kTf32) adesc0 = smem_desc_sw128(a0, Cfg::kBK * 128, 1024);
-            else adesc0 = smem_desc(a0, Cfg::kBK * 128, 512, kLayoutSw128Base32);
-            const uint64_t bdesc0 = smem_desc_sw128(a0 + Cfg::kABytes, 16, 1024);
+            const uint64_t adesc0 = smem_desc_sw128(a0, 16, 1024);
+            const uint32_t b0 = a0 + Cfg::kABytes;
+            uint64_t bdesc0;
+            if constexpr (!NN) bdesc0 = smem_desc_sw128(b0, 16, 1024);
+            else if constexpr (!OperandTraits<TA>::kTf32) bdesc0 = smem_desc_sw128(b0, Cfg::kBK * 128, 1024);
+            else bdesc0 = smem_desc(b0, Cfg::kBK * 128, 512, kLayoutSw128Base32);
             constexpr uint64_t kStageDesc = Cfg::kStageBytes >> 4;
-            constexpr uint64_t kAStep = NN ? (Cfg::kUmmaK * 128) >> 4 : 2;
+            constexpr uint64_t kBStep = NN ? (Cfg::kUmmaK * 128) >> 4 : 2;
             uint32_t s = 0, ph = 0;
             for (uint32_t i = 0; ok && i < my_tiles; ++i) {
                 const uint32_t acc = i & (Cfg::kAcc - 1), aph = (i / Cfg::kAcc) & 1;
@@ -208,7 +227,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * Cfg::kBNP;
+                const uint32_t d_tmem = tmem_base + acc * Cfg::kBNX;
                 for (uint32_t ks = 0; ks < p.k_stages; ++ks) {
                     if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.timeout_ns))) {
                         fail();
@@ -221,8 +240,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                         for (int kk = 0; kk < Cfg::kBK / Cfg::kUmmaK; ++kk) {
                             const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
                             if constexpr (OperandTraits<TA>::kTf32)
-                                mma_tf32_pair(d_tmem, ad + kk * kAStep, bd + 2 * kk, idesc, accum);
-                            else mma_f16_pair(d_tmem, ad + kk * kAStep, bd + 2 * kk, idesc, accum);
+                                mma_tf32_pair(d_tmem, ad + 2 * kk, bd + kk * kBStep, idesc, accum);
+                            else mma_f16_pair(d_tmem, ad + 2 * kk, bd + kk * kBStep, idesc, accum);
                         }
                         mma_commit_pair_mc(&empty[s], 0x3);
                     }
@@ -239,63 +258,76 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         }
     } else if (warp >= 4 && warp < 12) {
         // ------------------------------------------------------------ dequantisers (both CTAs)
-        const int ct = threadIdx.x - 128;
+        constexpr int G = Cfg::kDqGroups;
+        const uint32_t grp = (uint32_t)(warp - 4) / Cfg::kDqWarps;  // this group dequantises stages grp, grp+G, ...
+        const int ct = (threadIdx.x - 128) % Cfg::kConvThreads;
         const int chunk = ct % Cfg::kChunksPerRow;
         const int row0 = ct / Cfg::kChunksPerRow;
         constexpr int T = Cfg::kTasksPerThread;
-        // Scales come from L2 two stages ahead of use (latency hidden).
+        // Scales come from L2 (far-die hits take about a thousand cycles under load) kRing own
+        // stages ahead of use, into a ring of registers indexed by compile-time constants: the loop
+        // body is unrolled over the ring, so no instruction (not even a register move) touches a
+        // scale before its load has had kRing stages to land.
+        constexpr int kRing = 4;
         WeightCursor<T> cur;
-        cur.init(&p, cid, ncl, row0, Cfg::kRowStep, Cfg::kBK, chunk * 16, Cfg::kBNP, rank * Cfg::kBNC, Cfg::kBNC);
-        float sc0[T], sc1[T], sc2[T];
+        cur.init(&p, cid, ncl, row0, Cfg::kRowStep, Cfg::kBK, chunk * 16, 2 * Cfg::kBW, rank * Cfg::kBW, Cfg::kBW);
+        for (uint32_t g = 0; g < grp; ++g) cur.advance();
+        auto next_own = [&]() {
+#pragma unroll
+            for (int g = 0; g < G; ++g) cur.advance();
+        };
+        float sc[kRing][T];
         uint4 unused[T];
-        cur.load<false>(sc0, unused);
-        cur.advance();
-        cur.load<false>(sc1, unused);
-        cur.advance();
-        for (uint32_t it = 0; ok && it < my_iters; ++it) {
-            cur.load<false>(sc2, unused);
-            cur.advance();
+#pragma unroll
+        for (int j = 0; j < kRing; ++j) {
+            cur.load<false>(sc[j], unused);
+            next_own();
+        }
+        auto stage = [&](uint32_t it, float(&scale)[T]) -> bool {
             const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
             const uint32_t sw = it % Cfg::kSW, pw = (it / Cfg::kSW) & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&w_full[sw], pw, p.timeout_ns))) {  // leave together
-                fail();
-                break;
-            }
+            if (!__all_sync(0xffffffffu, mbar_wait(&w_full[sw], pw, p.timeout_ns))) return false;  // leave together
             const uint8_t* wsrc = sW + sw * Cfg::kWBytes;
-            uint8_t* bdst = sStage + s * Cfg::kStageBytes + Cfg::kABytes;
+            uint8_t* adst = sStage + s * Cfg::kStageBytes;
             uint4 raw[T];
 #pragma unroll
-            for (int t = 0; t < T; ++t) {
-                const int r = row0 + t * Cfg::kRowStep;
-                raw[t] = (r < Cfg::kBNC) ? *reinterpret_cast<const uint4*>(wsrc + r * Cfg::kBK + chunk * 16)
-                                         : make_uint4(0, 0, 0, 0);
-            }
-            // The raw slot is free as soon as its bytes are in registers: hand it back to the weight
-            // TMA before waiting for the operand stage (the arrive orders the warp's reads before
-            // the next load into the slot), so the weight ring keeps moving while the stage ring is
-            // full and its depth covers the TMA latency alone.
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&w_empty[sw]);
-            if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, p.timeout_ns))) {
-                fail();
-                break;
-            }
+            for (int t = 0; t < T; ++t)
+                raw[t] = *reinterpret_cast<const uint4*>(wsrc + (row0 + t * Cfg::kRowStep) * Cfg::kBK + chunk * 16);
+            if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, p.timeout_ns))) return false;
 #pragma unroll
             for (int t = 0; t < T; ++t) {
                 const int r = row0 + t * Cfg::kRowStep;
-                if (r < Cfg::kBNC) dequant16<TA>(raw[t], sc0[t], bdst + r * 128, r, chunk * Cfg::kES);
+                dequant16<TA>(raw[t], scale[t], adst + r * 128, r, chunk * Cfg::kES);
             }
+            // Only this SM's tensor core reads these rows (operand A of the pair MMA).  The fence
+            // also orders this thread's generic reads of the raw slot before the weight TMA's next
+            // (async-proxy) write into it: the raw slot is handed back only here.  Handing it back
+            // right after the reads, behind a warp barrier alone, let the next TMA overwrite it
+            // before every read had been performed (stale weight rows in up to a third of launches).
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa_shared(&full[s], 0));
+            if (lane == 0) {
+                mbar_arrive_cluster(mapa_shared(&full[s], 0));
+                mbar_arrive(&w_empty[sw]);
+            }
+            cur.load<false>(scale, unused);  // the scales of this group's stage it + G * kRing
+            next_own();
+            return true;
+        };
+        for (uint32_t it = grp; ok && it < my_iters; it += G * kRing) {
 #pragma unroll
-            for (int t = 0; t < T; ++t) {
-                sc0[t] = sc1[t];
-                sc1[t] = sc2[t];
+            for (int j = 0; j < kRing; ++j) {
+                if (it + G * j >= my_iters) break;
+                if (!stage(it + G * j, sc[j])) {
+                    fail();
+                    break;
+                }
             }
         }
     } else if (warp >= 12) {
         // ------------------------------------------------------------ epilogue (both CTAs)
+        // Warp q reads TMEM lanes 32q..32q+31: weight rows w = wt*256 + rank*128 + 32q + lane; each
+        // 32-column chunk is 32 activation rows.
         const int q = warp & 3;
         uint8_t* ebuf = sEpi + q * (2 * 4096);
         uint32_t nstore = 0;
@@ -308,42 +340,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 break;
             }
             tc_fence_after();
-            const int x0 = (int)(xt * 2 * Cfg::kBM + rank * Cfg::kBM) + q * 32;
+            const int w0 = (int)(wt * 2 * Cfg::kBW + rank * Cfg::kBW) + q * 32;  // this warp's first weight row
+            const uint32_t n = (uint32_t)w0 + lane;                           // this thread's weight row
+            const float b = (p.bias && n < p.wrows) ? __ldg(p.bias + n) : 0.0f;
 #pragma unroll 1
-            for (int cc = 0; cc < Cfg::kBNP / 32; ++cc, ++nstore) {
-                const int w0 = (int)(wt * Cfg::kBNP) + cc * 32;
+            for (int cc = 0; cc < Cfg::kBNX / 32; ++cc, ++nstore) {
+                const int x0 = (int)(xt * Cfg::kBNX) + cc * 32;
                 uint32_t raw[32];
-                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * Cfg::kBNP + cc * 32, raw);
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * Cfg::kBNX + cc * 32, raw);
                 tmem_wait_ld();
-                if (cc + 1 == Cfg::kBNP / 32) {  // accumulator fully read: hand it back to the MMA
+                if (cc + 1 == Cfg::kBNX / 32) {  // accumulator fully read: hand it back to the MMA
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
                 }
                 float v[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
-                if (p.bias) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const uint32_t n = (uint32_t)w0 + j;
-                        v[j] += (n < p.wrows) ? __ldg(p.bias + n) : 0.0f;
-                    }
-                }
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + b;
                 uint8_t* buf = ebuf + (nstore & 1) * 4096;
                 if (lane == 0) bulk_wait_read<1>();  // the store that last used `buf` has read it
                 __syncwarp();
                 if constexpr (!NN && sizeof(TC) == 2) {
-                    if (p.geglu) {  // chunk = [a(16) | gate(16)] -> 16 outputs, a 32-byte row per lane
-                        uint32_t h[8];
+                    if (p.geglu) {
+                        // Lanes 0-15 hold a(16 columns), lanes 16-31 the matching gate rows: 16
+                        // outputs a * gelu(gate) per activation row, a [32 x][16] f16 tile.
+                        __half* t = reinterpret_cast<__half*>(buf);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            __half2 t2 = __floats2half2_rn(v[2 * j] * gelu_erf_as_fast(v[16 + 2 * j]),
-                                                           v[2 * j + 1] * gelu_erf_as_fast(v[17 + 2 * j]));
-                            h[j] = *reinterpret_cast<uint32_t*>(&t2);
+                        for (int j = 0; j < 32; ++j) {
+                            const float g = __shfl_down_sync(0xffffffffu, v[j], 16);
+                            if (lane < 16) t[j * 16 + lane] = __float2half_rn(v[j] * gelu_erf_as_fast(g));
                         }
-                        *reinterpret_cast<uint4*>(buf + lane * 32) = make_uint4(h[0], h[1], h[2], h[3]);
-                        *reinterpret_cast<uint4*>(buf + lane * 32 + 16) = make_uint4(h[4], h[5], h[6], h[7]);
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) {
@@ -353,8 +379,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                         continue;
                     }
                 }
-                if constexpr (!NN) store_epi_row<TC>(buf, lane, v);
-                else store_epi_col<TC>(buf, lane, v);
+                if constexpr (!NN) store_epi_col<TC>(buf, lane, v);  // [32 x][32 w]
+                else store_epi_row<TC>(buf, lane, v);                // [32 w][32 x]
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
