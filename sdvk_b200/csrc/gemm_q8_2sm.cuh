@@ -362,13 +362,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 __syncwarp();
                 if constexpr (!NN && sizeof(TC) == 2) {
                     if (p.geglu) {
-                        // Lanes 0-15 hold a(16 columns), lanes 16-31 the matching gate rows: 16
-                        // outputs a * gelu(gate) per activation row, a [32 x][16] f16 tile.
+                        // Lane l < 16 holds a of output column l, lane l + 16 the matching gate: 16
+                        // outputs a * gelu(gate) per activation row, a [32 x][16] f16 tile.  Each
+                        // lane computes half of the 32 rows (lanes < 16 rows 0-15, lanes >= 16 rows
+                        // 16-31), trading the half its partner needs in one shuffle per row pair.
                         __half* t = reinterpret_cast<__half*>(buf);
+                        const bool lo = lane < 16;
+                        const int o = lane & 15;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float g = __shfl_down_sync(0xffffffffu, v[j], 16);
-                            if (lane < 16) t[j * 16 + lane] = __float2half_rn(v[j] * gelu_erf_as_fast(g));
+                        for (int j = 0; j < 16; ++j) {
+                            const float mine = lo ? v[j] : v[16 + j];  // a (lo) or gate (hi) of my row
+                            const float other = __shfl_xor_sync(0xffffffffu, lo ? v[16 + j] : v[j], 16);
+                            const float a = lo ? mine : other, g = lo ? other : mine;
+                            t[(lo ? j : 16 + j) * 16 + o] = __float2half_rn(a * gelu_erf_as_fast(g));
                         }
                         fence_proxy_async_smem();
                         __syncwarp();
