@@ -6,14 +6,26 @@
 #include "attention.cuh"
 #include "attention_fp32.cuh"
 #include "attention_tc.cuh"
+#include "attention_tc_short.cuh"
 #include "backend.hpp"
 
 namespace sdvk {
 namespace {
 
+// Keys that fit two 64-key tiles go to attn_short_kernel (whole grid resident, loads in flight
+// together) unless SDVK_ATTN_KERNEL=mma forces the general kernel.
+bool short_eligible(const AttnParams& p) {
+    const char* e = getenv("SDVK_ATTN_KERNEL");
+    return p.Tk <= 2 * kAttnBN && !(e && e[0] == 'm');
+}
+
 template <class TIn, class TOut, bool kAsync>
 int launch(const AttnParams& p, const LaunchEnv& env) {
     dim3 grid((p.Tq + kAttnBM - 1) / kAttnBM, p.heads, p.batch);
+    if (short_eligible(p)) {
+        attn_short_kernel<TIn, TOut, kAsync><<<grid, kAttnShortThreads, kAttnSmem, env.stream>>>(p);
+        return cuda_check(env, cudaGetLastError(), "attn_short_kernel launch");
+    }
     attn_fwd_kernel<TIn, TOut, kAsync><<<grid, kAttnThreads, kAttnSmem, env.stream>>>(p);
     return cuda_check(env, cudaGetLastError(), "attn_fwd_kernel launch");
 }
@@ -55,15 +67,21 @@ int make_attn_map(CUtensorMap* m, int dtype, const void* base, uint32_t T, uint3
     return SDVK_OK;
 }
 
-// The tensor-core kernel takes head dim 64, 16-bit Q/K/V, a positive scale, and TMA-legal layouts
-// (16-byte aligned bases and strides) with an output that takes 16-byte vector stores.  It is
-// chosen when the keys span more than one 128-key tile; a single tile (the 77-token
-// cross-attention) runs faster on the warp-level kernel (attention.cuh), whose CTAs are smaller.
-// SDVK_ATTN_KERNEL=mma or =tc forces one of them (tc only where eligible).
-bool tc_eligible(const sdvk_attn_desc& d) {
+// The tensor-core kernels take head dim 64, 16-bit Q/K/V, a positive scale, and TMA-legal layouts
+// (16-byte aligned bases and strides) with an output that takes 16-byte vector stores.
+// attn_tc_kernel serves keys beyond one 128-key tile; attn_tc_short_kernel serves at most 128
+// non-causal keys (the 77-token cross-attention).  SDVK_ATTN_KERNEL=mma forces the warp-level
+// kernels (attention.cuh), =tc forces attn_tc_kernel wherever the layout allows it.
+enum class AttnKernel { kWarp, kTc, kTcShort };
+bool tc_layout_ok(const sdvk_attn_desc& d);
+AttnKernel attn_kernel_choice(const sdvk_attn_desc& d) {
     const char* e = getenv("SDVK_ATTN_KERNEL");
-    if (e && e[0] == 'm') return false;
-    if (!(e && e[0] == 't') && d.Tk <= 128) return false;
+    if ((e && e[0] == 'm') || !tc_layout_ok(d)) return AttnKernel::kWarp;
+    if (e && e[0] == 't') return AttnKernel::kTc;
+    if (d.Tk > 128) return AttnKernel::kTc;
+    return d.causal ? AttnKernel::kWarp : AttnKernel::kTcShort;
+}
+bool tc_layout_ok(const sdvk_attn_desc& d) {
     const uint64_t es = 2, eo = d.o_dtype == SDVK_F32 ? 4 : 2;
     auto s16 = [](uint64_t bytes) { return bytes % 16 == 0 && bytes < (1ull << 40); };
     return (d.dtype == SDVK_F16 || d.dtype == SDVK_BF16) && d.hd == 64 && d.scale > 0.0f && d.Tk > 0 &&
@@ -100,8 +118,40 @@ int launch_tc(const sdvk_attn_desc& d, const LaunchEnv& env) {
     return cuda_check(env, cudaGetLastError(), "attn_tc_kernel launch");
 }
 
+template <class T, class TO>
+int launch_tc_short(const sdvk_attn_desc& d, const LaunchEnv& env) {
+    CUtensorMap mq, mk, mv;
+    if (int rc = make_attn_map(&mq, d.dtype, d.q, d.Tq, d.heads, d.batch, d.ldq, d.hq, d.sq, env, "Q")) return rc;
+    if (int rc = make_attn_map(&mk, d.dtype, d.k, d.Tk, d.heads, d.batch, d.ldk, d.hk, d.sk, env, "K")) return rc;
+    if (int rc = make_attn_map(&mv, d.dtype, d.v, d.Tk, d.heads, d.batch, d.ldv, d.hv, d.sv, env, "V")) return rc;
+    TcAttnParams p{};
+    p.o = d.o;
+    p.ldo = d.ldo;
+    p.so = d.so;
+    p.ho = d.ho;
+    p.Tq = d.Tq;
+    p.Tk = d.Tk;
+    p.heads = d.heads;
+    p.batch = d.batch;
+    p.scale_log2 = d.scale * 1.4426950408889634f;
+    p.causal = 0;
+    p.err = env.err_dev;
+    p.timeout_ns = env.timeout_ns;
+    auto kern = attn_tc_short_kernel<T, TO>;
+    if (!kernel_smem_attr(reinterpret_cast<const void*>(kern), TcShortCfg::kSmemBytes, env.device))
+        return fail(env, SDVK_E_CUDA, "attn_tc_short_kernel: shared memory opt-in failed");
+    const uint64_t items = (uint64_t)((d.Tq + TcShortCfg::kBM - 1) / TcShortCfg::kBM) * d.heads * d.batch;
+    const uint32_t grid = (uint32_t)std::min<uint64_t>(items, 2ull * env.num_sms);
+    kern<<<grid, TcShortCfg::kThreads, TcShortCfg::kSmemBytes, env.stream>>>(mq, mk, mv, p);
+    return cuda_check(env, cudaGetLastError(), "attn_tc_short_kernel launch");
+}
+
 template <class T>
-int launch_tc_out(const sdvk_attn_desc& d, const LaunchEnv& env) {
+int launch_tc_out(const sdvk_attn_desc& d, bool short_keys, const LaunchEnv& env) {
+    if (short_keys) {
+        if (d.o_dtype == SDVK_F32) return launch_tc_short<T, float>(d, env);
+        return launch_tc_short<T, __half>(d, env);
+    }
     if (d.o_dtype == SDVK_F32) return launch_tc<T, float>(d, env);
     return launch_tc<T, __half>(d, env);
 }
@@ -155,9 +205,11 @@ int attention(const sdvk_attn_desc& d, const LaunchEnv& env) {
         else attn_fp32_kernel<__half><<<grid, kF32Rows, 0, env.stream>>>(p);
         return cuda_check(env, cudaGetLastError(), "attn_fp32_kernel launch");
     }
-    if (tc_eligible(d)) {
-        if (d.dtype == SDVK_F16) return launch_tc_out<__half>(d, env);
-        return launch_tc_out<__nv_bfloat16>(d, env);
+    const AttnKernel choice = attn_kernel_choice(d);
+    if (choice != AttnKernel::kWarp) {
+        const bool short_keys = choice == AttnKernel::kTcShort;
+        if (d.dtype == SDVK_F16) return launch_tc_out<__half>(d, short_keys, env);
+        return launch_tc_out<__nv_bfloat16>(d, short_keys, env);
     }
     // cp.async staging needs 16-byte aligned rows and whole 8-element chunks of the head.
     const uint64_t es = 2;

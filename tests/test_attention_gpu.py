@@ -141,11 +141,20 @@ KERNEL_CASES = [
 ]
 
 
-@pytest.mark.parametrize("kernel", ["tc", "mma"])
-@pytest.mark.parametrize("B,Tq,Tk,heads,causal,dt,out", KERNEL_CASES)
+@pytest.mark.parametrize("kernel", ["tc", "mma", "auto"])
+@pytest.mark.parametrize("B,Tq,Tk,heads,causal,dt,out", KERNEL_CASES + [
+    # at most 128 non-causal keys: the short-key tcgen05 kernel under "auto"; many items per CTA
+    (4, 1100, 128, 40, False, "f16", "f16"),
+    (2, 130, 1, 3, False, "bf16", "f32"),
+    (1, 64, 16, 5, False, "f16", "f32"),
+])
 def test_attention_kernel_variants(orc, cuda_ok, monkeypatch, kernel, B, Tq, Tk, heads, causal, dt, out):
-    """Both attention kernels (SDVK_ATTN_KERNEL=tc: tcgen05/TMEM; =mma: warp-level) against fp64."""
-    monkeypatch.setenv("SDVK_ATTN_KERNEL", kernel)
+    """The attention kernels (SDVK_ATTN_KERNEL=tc: tcgen05/TMEM; =mma: warp-level; auto: the default
+    choice, which sends at most 128 non-causal keys to the short-key tcgen05 kernel) against fp64."""
+    if kernel == "auto":
+        monkeypatch.delenv("SDVK_ATTN_KERNEL", raising=False)
+    else:
+        monkeypatch.setenv("SDVK_ATTN_KERNEL", kernel)
     C = heads * 64
     tdt = {"f16": torch.float16, "bf16": torch.bfloat16}[dt]
     qt, kt, vt = (dev(orc.normal_f32(5, i, (B, T, C))).to(tdt) for i, T in enumerate((Tq, Tk, Tk)))
