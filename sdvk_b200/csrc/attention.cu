@@ -23,11 +23,11 @@ template <class TIn, class TOut, bool kAsync>
 int launch(const AttnParams& p, const LaunchEnv& env) {
     dim3 grid((p.Tq + kAttnBM - 1) / kAttnBM, p.heads, p.batch);
     if (short_eligible(p)) {
-        attn_short_kernel<TIn, TOut, kAsync><<<grid, kAttnShortThreads, kAttnSmem, env.stream>>>(p);
-        return cuda_check(env, cudaGetLastError(), "attn_short_kernel launch");
+        return launch_pdl(attn_short_kernel<TIn, TOut, kAsync>, grid, dim3(kAttnShortThreads), kAttnSmem, env,
+                          "attn_short_kernel launch", p);
     }
-    attn_fwd_kernel<TIn, TOut, kAsync><<<grid, kAttnThreads, kAttnSmem, env.stream>>>(p);
-    return cuda_check(env, cudaGetLastError(), "attn_fwd_kernel launch");
+    return launch_pdl(attn_fwd_kernel<TIn, TOut, kAsync>, grid, dim3(kAttnThreads), kAttnSmem, env,
+                      "attn_fwd_kernel launch", p);
 }
 
 template <class TIn, class TOut>
@@ -114,8 +114,8 @@ int launch_tc(const sdvk_attn_desc& d, const LaunchEnv& env) {
     if (!kernel_smem_attr(reinterpret_cast<const void*>(kern), TcAttnCfg::kSmemBytes, env.device))
         return fail(env, SDVK_E_CUDA, "attn_tc_kernel: shared memory opt-in failed");
     dim3 grid((d.Tq + TcAttnCfg::kBM - 1) / TcAttnCfg::kBM, d.heads, d.batch);
-    kern<<<grid, TcAttnCfg::kThreads, TcAttnCfg::kSmemBytes, env.stream>>>(mq, mk, mv, p);
-    return cuda_check(env, cudaGetLastError(), "attn_tc_kernel launch");
+    return launch_pdl(kern, grid, dim3(TcAttnCfg::kThreads), TcAttnCfg::kSmemBytes, env, "attn_tc_kernel launch", mq,
+                      mk, mv, p);
 }
 
 template <class T, class TO>
@@ -142,8 +142,8 @@ int launch_tc_short(const sdvk_attn_desc& d, const LaunchEnv& env) {
         return fail(env, SDVK_E_CUDA, "attn_tc_short_kernel: shared memory opt-in failed");
     const uint64_t items = (uint64_t)((d.Tq + TcShortCfg::kBM - 1) / TcShortCfg::kBM) * d.heads * d.batch;
     const uint32_t grid = (uint32_t)std::min<uint64_t>(items, 2ull * env.num_sms);
-    kern<<<grid, TcShortCfg::kThreads, TcShortCfg::kSmemBytes, env.stream>>>(mq, mk, mv, p);
-    return cuda_check(env, cudaGetLastError(), "attn_tc_short_kernel launch");
+    return launch_pdl(kern, dim3(grid), dim3(TcShortCfg::kThreads), TcShortCfg::kSmemBytes, env,
+                      "attn_tc_short_kernel launch", mq, mk, mv, p);
 }
 
 template <class T>
@@ -201,9 +201,9 @@ int attention(const sdvk_attn_desc& d, const LaunchEnv& env) {
     const char* force = getenv("SDVK_ATTN_KERNEL");
     if (d.dtype == SDVK_F32 && env.precision == SDVK_PRECISION_REFERENCE && !(force && force[0] == 'm')) {
         const dim3 grid((d.Tq + kF32Rows - 1) / kF32Rows, d.heads, d.batch);
-        if (d.o_dtype == SDVK_F32) attn_fp32_kernel<float><<<grid, kF32Rows, 0, env.stream>>>(p);
-        else attn_fp32_kernel<__half><<<grid, kF32Rows, 0, env.stream>>>(p);
-        return cuda_check(env, cudaGetLastError(), "attn_fp32_kernel launch");
+        if (d.o_dtype == SDVK_F32)
+            return launch_pdl(attn_fp32_kernel<float>, grid, dim3(kF32Rows), 0, env, "attn_fp32_kernel launch", p);
+        return launch_pdl(attn_fp32_kernel<__half>, grid, dim3(kF32Rows), 0, env, "attn_fp32_kernel launch", p);
     }
     const AttnKernel choice = attn_kernel_choice(d);
     if (choice != AttnKernel::kWarp) {

@@ -258,6 +258,8 @@ __device__ __forceinline__ void attn_store_slab(const AttnParams& p, TOut* O, ui
 
 template <class TIn, class TOut, bool kAsync>
 __global__ void __launch_bounds__(kAttnThreads, 2) attn_fwd_kernel(const AttnParams p) {
+    grid_dependency_wait();
+    grid_launch_dependents();
     using TC = typename AttnCompute<TIn>::T;
     extern __shared__ __align__(1024) uint8_t attn_smem[];
     uint8_t* sQ = attn_smem;
@@ -330,6 +332,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_fwd_kernel(const AttnPar
 // together; the per-tile math is the general kernel's.
 template <class TIn, class TOut, bool kAsync>
 __global__ void __launch_bounds__(kAttnShortThreads, 4) attn_short_kernel(const AttnParams p) {
+    grid_dependency_wait();
+    grid_launch_dependents();
     using TC = typename AttnCompute<TIn>::T;
     extern __shared__ __align__(1024) uint8_t attn_smem[];
     uint8_t* sQ = attn_smem;

@@ -19,6 +19,8 @@ constexpr int kF32Keys = 32;
 
 template <class TOut>
 __global__ void __launch_bounds__(kF32Rows) attn_fp32_kernel(const AttnParams p) {
+    grid_dependency_wait();
+    grid_launch_dependents();
     __shared__ float sK[kF32Keys][64];
     __shared__ float sV[kF32Keys][64];
     const uint32_t b = blockIdx.z, h = blockIdx.y;

@@ -139,6 +139,9 @@ __global__ void __launch_bounds__(384, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Everything above overlaps the previous kernel's tail; global memory is touched only after it.
+    grid_dependency_wait();
+    grid_launch_dependents();
     bool ok = true;
     auto fail = [&]() {
         atomicOr(p.err, kErrTimeout);

@@ -6,6 +6,7 @@
 
 #include <cstdint>
 #include <string>
+#include <utility>
 
 #include "../../include/sdvk_cuda.h"
 
@@ -79,6 +80,28 @@ inline int fail(const LaunchEnv& env, int code, const std::string& what) {
 inline int cuda_check(const LaunchEnv& env, cudaError_t e, const char* what) {
     if (e == cudaSuccess) return SDVK_OK;
     return fail(env, SDVK_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// Programmatic dependent launch (SDVK_PDL=0 turns it off): a kernel launched this way may start
+// its prologue while the previous kernel on the stream finishes; every kernel launched through
+// launch_pdl touches global memory only after griddepcontrol.wait (grid_dependency_wait), which
+// returns once the previous grid has completed and its writes are visible.
+bool pdl_enabled();
+
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, const LaunchEnv& env, const char* what,
+               Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = env.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_check(env, cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
 }
 
 }  // namespace sdvk

@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(kLnWarps * 32) layernorm_kernel(const float* _
                                                                   const float* __restrict__ beta, TO* __restrict__ y,
                                                                   uint32_t rows, uint32_t d, uint64_t ldx, uint64_t ldy,
                                                                   float eps) {
+    grid_dependency_wait();  // x is the previous kernel's output
+    grid_launch_dependents();
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t row = blockIdx.x * kLnWarps + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -94,6 +96,8 @@ __global__ void __launch_bounds__(kLnWarps * 32) layernorm_kernel(const float* _
 // y[r][j] = h[r][j] * gelu(h[r][F + j]), 8 halves per thread per step.
 __global__ void geglu_kernel(const __half* __restrict__ h, __half* __restrict__ y, uint32_t rows, uint32_t F,
                              uint64_t ldh, uint64_t ldy) {
+    grid_dependency_wait();
+    grid_launch_dependents();
     const uint32_t per_row = F / 8;
     const uint64_t n = (uint64_t)rows * per_row;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
@@ -119,6 +123,8 @@ bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, const float* __restrict__ bias,
                                      __half* __restrict__ y, uint32_t rows, uint32_t cols, uint32_t splits,
                                      uint64_t ldy) {
+    grid_dependency_wait();
+    grid_launch_dependents();
     const uint64_t plane = (uint64_t)rows * cols, n4 = plane / 4;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
         float4 a = reinterpret_cast<const float4*>(part)[i];
@@ -145,10 +151,8 @@ template <class TO>
 int launch_ln(const float* x, const float* g, const float* b, TO* y, uint32_t rows, uint32_t d, uint64_t ldx,
               uint64_t ldy, float eps, const LaunchEnv& env) {
     const dim3 grid((rows + kLnWarps - 1) / kLnWarps), block(kLnWarps * 32);
-    if (d <= 512) layernorm_kernel<TO, 4><<<grid, block, 0, env.stream>>>(x, g, b, y, rows, d, ldx, ldy, eps);
-    else if (d <= 1280) layernorm_kernel<TO, 10><<<grid, block, 0, env.stream>>>(x, g, b, y, rows, d, ldx, ldy, eps);
-    else layernorm_kernel<TO, 24><<<grid, block, 0, env.stream>>>(x, g, b, y, rows, d, ldx, ldy, eps);
-    return cuda_check(env, cudaGetLastError(), "layernorm_kernel launch");
+    auto kern = d <= 512 ? layernorm_kernel<TO, 4> : d <= 1280 ? layernorm_kernel<TO, 10> : layernorm_kernel<TO, 24>;
+    return launch_pdl(kern, grid, block, 0, env, "layernorm_kernel launch", x, g, b, y, rows, d, ldx, ldy, eps);
 }
 
 }  // namespace
@@ -173,9 +177,8 @@ int geglu(const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint6
         return fail(env, SDVK_E_SHAPE, "GEGLU needs F, ldh, ldy multiples of 8 and 16-byte aligned rows");
     const uint64_t n = (uint64_t)rows * (F / 8);
     const uint32_t blocks = (uint32_t)std::min<uint64_t>((n + 255) / 256, (uint64_t)env.num_sms * 8);
-    geglu_kernel<<<blocks, 256, 0, env.stream>>>(static_cast<const __half*>(h), static_cast<__half*>(y), rows, F, ldh,
-                                                 ldy);
-    return cuda_check(env, cudaGetLastError(), "geglu_kernel launch");
+    return launch_pdl(geglu_kernel, dim3(blocks), dim3(256), 0, env, "geglu_kernel launch",
+                      static_cast<const __half*>(h), static_cast<__half*>(y), rows, F, ldh, ldy);
 }
 
 // ------------------------------------------------------------------------------------ the block
@@ -269,8 +272,8 @@ int kv_linear_split(const void* ctx, int ctx_dtype, uint64_t ldctx, const sdvk_q
     if (int rc = gemm_q8(g, env)) return rc;
     const uint64_t n4 = (uint64_t)rows * 2 * N / 4;
     const uint32_t blocks = (uint32_t)std::min<uint64_t>((n4 + 255) / 256, (uint64_t)env.num_sms * 4);
-    splitk_reduce_kernel<<<blocks, 256, 0, env.stream>>>(part, w[0].bias, y, rows, 2 * N, kKvSplits, ldy);
-    return cuda_check(env, cudaGetLastError(), "splitk_reduce_kernel launch");
+    return launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, env, "splitk_reduce_kernel launch",
+                      (const float*)part, w[0].bias, y, rows, 2 * N, (uint32_t)kKvSplits, ldy);
 }
 
 sdvk_attn_desc attn_desc(const __half* q, uint64_t ldq, uint64_t sq, const __half* k, const __half* v, uint64_t ldkv,

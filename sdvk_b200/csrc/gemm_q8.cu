@@ -145,10 +145,6 @@ int launch(const GemmQ8Desc& d, const LaunchEnv& env) {
     return cuda_check(env, cudaGetLastError(), "gemm_q8_tc_kernel launch");
 }
 
-bool pdl_enabled() {
-    const char* e = getenv("SDVK_PDL");
-    return !(e && e[0] == '0');
-}
 
 // CTA-pair variant: 256 (weight rows) x BNX (activation rows) tiles on two SMs (cta_group::2).
 template <class TA, int BNX, bool NN, class TC>
@@ -291,6 +287,11 @@ int launch_a(const GemmQ8Desc& d, const LaunchEnv& env) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+bool pdl_enabled() {
+    const char* e = getenv("SDVK_PDL");
+    return !(e && e[0] == '0');
+}
 
 // GEGLU interleave of an ff.net.0.proj weight [2F][K] (rows 0..F-1 = a, F..2F-1 = gate): output row
 // r = 32j + t holds a row 16j + t for t < 16 and gate row 16j + t - 16 otherwise, with its scales and
