@@ -122,6 +122,7 @@ SDVK_API int sdvk_synchronize(sdvk_ctx* ctx);
  *   "gemm_nn_q8", "gemm_nn_q8_v"        bufs {Aq, B, C, S}        push Pg
  *   "fused_attn", "fused_attn_tiled"    bufs {Q, K, V, O}         push FaPush (36 B)
  *   "layernorm_fwd"                     bufs {X, gamma, beta, Y}  push {rows, d, eps, affine} (16 B)
+ *   "groupnorm"                         bufs {X, gamma, beta, Y}  push {C, P, G, eps, act} (20 B)
  * Pg = {M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, pad} (sdvkgen.cpp:901-903);
  * FaPush = {Tq, Tk, C, heads, hd, causal, pad0, pad1, scale} (fused_attn.cpp:15-26).
  * The grid (gx, gy, gz) the caller computed for the Vulkan tiling is accepted and ignored: each
@@ -254,6 +255,26 @@ SDVK_API int sdvk_transformer_block_static(sdvk_ctx* ctx, const sdvk_block_desc*
  *   out = rescale * er + (1 - rescale) * out (statistics in double).  fp32 [n] each. */
 SDVK_API int sdvk_cfg_combine(sdvk_ctx* ctx, const float* cond, const float* uncond, float* out, uint64_t n, float cfg,
                      float rescale);
+
+/* ---- model loading and the ResBlock's normalisation ---------------------------------------- */
+/* GGUF Q8_0 ingest on the device (GgufFile::readQ8Into, src/Modules/Model/Gguf.cpp:559-583, and
+ * fp16ToFp32, Gguf.cpp:11-35).  blocks: the tensor's raw data in device memory, rows x cols values
+ * as rows*cols/32 blocks of 34 bytes (little-endian binary16 d, then 32 x int8), 2-byte aligned.
+ * Writes q[row*ldq + k] and scales[row*(ldq/32) + k/32] (fp32, converted exactly): the layout the
+ * Q8 entry points take, bit-identical to the reference loader's for ldq = cols (ldq = 0 means cols).
+ * cols % 32 == 0, ldq % 32 == 0 (SDVK_E_SHAPE otherwise).  No counterpart in the reference's GPU
+ * module: it replaces the host-side split when the raw blocks are uploaded as they are. */
+SDVK_API int sdvk_q8_0_ingest(sdvk_ctx* ctx, const void* blocks, uint64_t rows, uint64_t cols, int8_t* q,
+                              uint64_t ldq, float* scales);
+/* GroupNorm over x[batch][C][P] (channel-major, P = H*W) with G groups of C/G channels
+ * (groupnorm.comp, gnInto sdvkgen.cpp:1105-1113; the reference runs batch 1): per (image, group)
+ * mean and population variance, y = (x - mean)/sqrt(var + eps)*gamma[c] + beta[c], then
+ * y/(1 + e^-y) when silu != 0.  fp32 in and out; y may alias x.  workspace: device memory of at
+ * least sdvk_groupnorm_workspace(batch, C, P, G) bytes, 16-byte aligned. */
+SDVK_API uint64_t sdvk_groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G);
+SDVK_API int sdvk_groupnorm(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, float* y,
+                            uint32_t batch, uint32_t C, uint32_t P, uint32_t G, float eps, int silu, void* workspace,
+                            uint64_t workspace_bytes);
 
 /* An NCCL communicator for the context's device.  The reference runs both CFG passes on one device
  * (runPass twice, sdvkgen.cpp:3812-3813); with a GPU pair each rank runs one pass and the halves

@@ -623,6 +623,47 @@ void orc_layernorm_shader(const float* x, const float* gamma, const float* beta,
     }
 }
 
+// groupnorm.comp:12-39, one workgroup (256 lanes) per group: lane t sums x[base + i], i = t, t+256,
+// ... in order, a tree over the 256 partials (stride 128 down to 1) gives the mean; the same for the
+// squared deviations gives the population variance; then (x - mean) * r * gamma[c] + beta[c] and,
+// with act == 1, v / (1 + exp(-v)).  Multiply-adds are fused as in the layernorm restatement above.
+void orc_groupnorm_shader(const float* x, const float* gamma, const float* beta, float* y, uint32_t C,
+                          uint32_t P, uint32_t G, float eps, uint32_t act) {
+    const uint32_t Cg = C / G;
+    const uint64_t cnt = (uint64_t)Cg * P;
+#pragma omp parallel for schedule(static)
+    for (int64_t g = 0; g < (int64_t)G; ++g) {
+        const uint64_t base = (uint64_t)g * cnt;
+        float red[256];
+        for (uint32_t t = 0; t < 256; ++t) {
+            float s = 0.0f;
+            for (uint64_t i = t; i < cnt; i += 256) s += x[base + i];
+            red[t] = s;
+        }
+        for (uint32_t st = 128; st > 0; st >>= 1)
+            for (uint32_t t = 0; t < st; ++t) red[t] += red[t + st];
+        const float mean = red[0] / (float)cnt;
+        for (uint32_t t = 0; t < 256; ++t) {
+            float ss = 0.0f;
+            for (uint64_t i = t; i < cnt; i += 256) {
+                const float dv = x[base + i] - mean;
+                ss = fmaf(dv, dv, ss);
+            }
+            red[t] = ss;
+        }
+        for (uint32_t st = 128; st > 0; st >>= 1)
+            for (uint32_t t = 0; t < st; ++t) red[t] += red[t + st];
+        const float var = red[0] / (float)cnt;
+        const float r = 1.0f / std::sqrt(var + eps);
+        for (uint64_t i = 0; i < cnt; ++i) {
+            const uint32_t ch = (uint32_t)(g * Cg + i / P);
+            float v = fmaf((x[base + i] - mean) * r, gamma[ch], beta[ch]);
+            if (act == 1u) v = v / (1.0f + std::exp(-v));
+            y[base + i] = v;
+        }
+    }
+}
+
 void orc_layernorm_f64(const double* x, const float* gamma, const float* beta, double* y,
                        uint32_t rows, uint32_t d, double eps) {
 #pragma omp parallel for schedule(static)

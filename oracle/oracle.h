@@ -77,6 +77,9 @@ void orc_attn_f64(const float* Q, const float* K, const float* V, double* O, uin
 /* ---- block glue ------------------------------------------------------------------------------ */
 void orc_layernorm_shader(const float* x, const float* gamma, const float* beta, float* y,
                           uint32_t rows, uint32_t d, float eps, uint32_t affine);
+/* groupnorm.comp:12-39 (batch 1): x[C][P], G groups; act 1 = fused SiLU. */
+void orc_groupnorm_shader(const float* x, const float* gamma, const float* beta, float* y, uint32_t C,
+                          uint32_t P, uint32_t G, float eps, uint32_t act);
 void orc_layernorm_f64(const double* x, const float* gamma, const float* beta, double* y,
                        uint32_t rows, uint32_t d, double eps);
 void orc_gelu_erf_shader(const float* x, float* y, uint64_t n);

@@ -41,6 +41,7 @@ _SIG = {
     "orc_fused_attention": (_I, [_P, _P, _P, _P] + [_U32] * 5 + [_I]),
     "orc_attn_f64": (None, [_P, _P, _P, _P] + [_U32] * 5 + [_U64] * 8 + [_U32, ctypes.c_double]),
     "orc_layernorm_shader": (None, [_P, _P, _P, _P, _U32, _U32, _F, _U32]),
+    "orc_groupnorm_shader": (None, [_P, _P, _P, _P, _U32, _U32, _U32, _F, _U32]),
     "orc_layernorm_f64": (None, [_P, _P, _P, _P, _U32, _U32, ctypes.c_double]),
     "orc_gelu_erf_shader": (None, [_P, _P, _U64]),
     "orc_cfg_combine": (None, [_P, _P, _P, _U64, _F, _F]),
@@ -269,6 +270,36 @@ def layernorm_f64(x, gamma, beta, eps=1e-5):
     rows, d = x.reshape(-1, x.shape[-1]).shape
     y = np.empty_like(x)
     lib().orc_layernorm_f64(_p(x), _p(_c(gamma, np.float32)), _p(_c(beta, np.float32)), _p(y), rows, d, eps)
+    return y
+
+
+def groupnorm_shader(x, gamma, beta, G, eps=1e-5, act=0):
+    """groupnorm.comp restated in fp32 (oracle.cpp), per image of x [B, C, P...]."""
+    x = _c(x, np.float32)
+    B, C = x.shape[0], x.shape[1]
+    P = x[0, 0].size
+    y = np.empty_like(x)
+    g, b = _c(gamma, np.float32), _c(beta, np.float32)
+    for i in range(B):
+        xi = np.ascontiguousarray(x[i])
+        yi = np.empty_like(xi)
+        lib().orc_groupnorm_shader(_p(xi), _p(g), _p(b), _p(yi), C, P, G, eps, act)
+        y[i] = yi
+    return y
+
+
+def groupnorm_f64(x, gamma, beta, G, eps=1e-5, act=0):
+    """GroupNorm (+SiLU) in float64 (the truth the kernels and the restatement are measured against)."""
+    x = np.asarray(x, np.float64)
+    B, C = x.shape[0], x.shape[1]
+    xg = x.reshape(B, G, -1)
+    mean = xg.mean(axis=2, keepdims=True)
+    var = ((xg - mean) ** 2).mean(axis=2, keepdims=True)
+    y = ((xg - mean) / np.sqrt(var + eps)).reshape(x.shape)
+    shape = (1, C) + (1,) * (x.ndim - 2)
+    y = y * np.asarray(gamma, np.float64).reshape(shape) + np.asarray(beta, np.float64).reshape(shape)
+    if act:
+        y = y / (1.0 + np.exp(-y))
     return y
 
 

@@ -112,6 +112,9 @@ SIGNATURES = {
     "sdvk_attention": (_I, [_P, ctypes.POINTER(AttnDesc)]),
     "sdvk_check_finite": (_I, [_P, _P, _I, _U64]),
     "sdvk_cfg_combine": (_I, [_P, _P, _P, _P, _U64, ctypes.c_float, ctypes.c_float]),
+    "sdvk_q8_0_ingest": (_I, [_P, _P, _U64, _U64, _P, _U64, _P]),
+    "sdvk_groupnorm_workspace": (_U64, [_U32, _U32, _U32, _U32]),
+    "sdvk_groupnorm": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, ctypes.c_float, _I, _P, _U64]),
     "sdvk_comm_unique_id": (_I, [_P]),
     "sdvk_comm_create": (_I, [_P, _I, _I, _P, _U32, ctypes.POINTER(_P)]),
     "sdvk_comm_destroy": (_I, [_P]),
@@ -305,6 +308,18 @@ class Context:
     def cfg_combine(self, cond: int, uncond: int, out: int, n: int, cfg: float, rescale: float = 0.0) -> None:
         self._check(lib().sdvk_cfg_combine(self._h, cond, uncond, out, n, cfg, rescale), "cfg_combine")
 
+    def q8_0_ingest(self, blocks: int, rows: int, cols: int, q: int, ldq: int, scales: int) -> None:
+        self._check(lib().sdvk_q8_0_ingest(self._h, blocks, rows, cols, q, ldq, scales), "q8_0_ingest")
+
+    @staticmethod
+    def groupnorm_workspace(batch: int, C: int, P: int, G: int) -> int:
+        return lib().sdvk_groupnorm_workspace(batch, C, P, G)
+
+    def groupnorm(self, x: int, gamma: int, beta: int, y: int, batch: int, C: int, P: int, G: int, eps: float,
+                  silu: bool, workspace: int, workspace_bytes: int) -> None:
+        self._check(lib().sdvk_groupnorm(self._h, x, gamma, beta, y, batch, C, P, G, eps, int(silu), workspace or None,
+                                         workspace_bytes), "groupnorm")
+
     def check_finite(self, ptr: int, dtype: int, n: int) -> bool:
         st = lib().sdvk_check_finite(self._h, ptr, dtype, n)
         if st == E_NOT_FINITE:
@@ -316,6 +331,11 @@ class Context:
 def pack_pg(M, N, K, mode=0, sA=0, sB=0, sC=0, batch=1, lda=0, ldb=0, ldc=0) -> bytes:
     """Pg push constants of the Q8 GEMM kernels (sdvkgen.cpp:901-903)."""
     return struct.pack("<12I", M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, 0)
+
+
+def pack_gn(C, P, G, eps=1e-5, act=0) -> bytes:
+    """groupnorm.comp push constants {C, P, G, eps, act} (sdvkgen.cpp:1107-1111)."""
+    return struct.pack("<IIIfI", C, P, G, eps, act)
 
 
 def pack_ln(rows, d, eps=1e-5, affine=1) -> bytes:

@@ -70,6 +70,13 @@ int allgather(sdvk_comm* c, const void* send, void* recv, uint64_t count, int dt
 int comm_wait(sdvk_comm* c, uint32_t timeout_ms, const LaunchEnv& env);
 int check_finite(const void* x, int dtype, uint64_t n, uint32_t* flag_dev, const LaunchEnv& env);
 
+// ingest.cu: GGUF Q8_0 blocks -> (int8 payload, fp32 scales); GroupNorm (+SiLU).
+int q8_0_ingest(const void* blocks, uint64_t rows, uint64_t cols, int8_t* q, uint64_t ldq, float* scales,
+                const LaunchEnv& env);
+uint64_t groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G);
+int groupnorm(const float* x, const float* gamma, const float* beta, float* y, uint32_t batch, uint32_t C, uint32_t P,
+              uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes, const LaunchEnv& env);
+
 inline int dtype_size(int dt) { return dt == SDVK_F32 ? 4 : (dt == SDVK_F16 || dt == SDVK_BF16) ? 2 : 0; }
 
 inline int fail(const LaunchEnv& env, int code, const std::string& what) {

@@ -26,6 +26,8 @@ struct sdvk_ctx {
     cudaEvent_t fork = nullptr, join = nullptr;
     bool in_step = false;
     bool step_recorded = false;
+    void* scratch = nullptr;  // workspace of name-dispatched kernels that need one (groupnorm)
+    uint64_t scratch_bytes = 0;
     std::string last_error;
     std::string device_name;
 };
@@ -40,6 +42,12 @@ struct FaPush {
     uint32_t Tq, Tk, C, heads, hd, causal, pad0, pad1;
     float scale;
 };
+struct GnPush {  // groupnorm.comp push constants (sdvkgen.cpp:1107-1111)
+    uint32_t C, P, G;
+    float eps;
+    uint32_t act;
+};
+static_assert(sizeof(GnPush) == 20, "GnPush layout");
 struct LnPush {  // layernorm_fwd.comp push constants (sdvkgen.cpp:1096-1100)
     uint32_t rows, d;
     float eps;
@@ -149,6 +157,10 @@ int sdvk_ctx_destroy(sdvk_ctx* ctx) {
     if (ctx->join) cudaEventDestroy(ctx->join);
     if (ctx->side) cudaStreamDestroy(ctx->side);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
+    if (ctx->scratch) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(ctx->scratch);
+    }
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return SDVK_OK;
@@ -502,6 +514,25 @@ int sdvk_cfg_combine(sdvk_ctx* ctx, const float* cond, const float* uncond, floa
     return sdvk::cfg_combine(cond, uncond, out, n, cfg, rescale, env_of(ctx));
 }
 
+int sdvk_q8_0_ingest(sdvk_ctx* ctx, const void* blocks, uint64_t rows, uint64_t cols, int8_t* q, uint64_t ldq,
+                     float* scales) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::q8_0_ingest(blocks, rows, cols, q, ldq ? ldq : cols, scales, env_of(ctx));
+}
+
+uint64_t sdvk_groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G) {
+    return sdvk::groupnorm_workspace(batch, C, P, G);
+}
+
+int sdvk_groupnorm(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, float* y, uint32_t batch,
+                   uint32_t C, uint32_t P, uint32_t G, float eps, int silu, void* workspace, uint64_t workspace_bytes) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::groupnorm(x, gamma, beta, y, batch, C, P, G, eps, silu ? 1u : 0u, workspace, workspace_bytes,
+                           env_of(ctx));
+}
+
 int sdvk_comm_unique_id(void* id) { return sdvk::comm_unique_id(id); }
 
 int sdvk_comm_create(sdvk_ctx* ctx, int nranks, int rank, const void* id, uint32_t timeout_ms, sdvk_comm** out) {
@@ -590,6 +621,36 @@ int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint3
                               pc.affine ? static_cast<const float*>(buf_ptr(bufs[1])) : nullptr,
                               pc.affine ? static_cast<const float*>(buf_ptr(bufs[2])) : nullptr, buf_mptr(bufs[3]),
                               SDVK_F32, pc.rows, pc.d, pc.d, pc.d, pc.eps);
+    }
+    if (is({"groupnorm"})) {
+        if (push_bytes < sizeof(GnPush) || nbufs < 4u)
+            return set_err(ctx, SDVK_E_ARG, name + ": needs 4 buffers and a 20-byte push");
+        GnPush pc;
+        std::memcpy(&pc, push, sizeof(pc));
+        const uint64_t xy_end = (uint64_t)pc.C * pc.P * 4;
+        if (!buf_holds(bufs[0], xy_end) || !buf_holds(bufs[3], xy_end) || !buf_holds(bufs[1], (uint64_t)pc.C * 4) ||
+            !buf_holds(bufs[2], (uint64_t)pc.C * 4))
+            return set_err(ctx, SDVK_E_ARG, name + ": a buffer is smaller than the shape needs");
+        const uint64_t need = sdvk::groupnorm_workspace(1, pc.C, pc.P, pc.G);
+        if (need == 0) return set_err(ctx, SDVK_E_SHAPE, name + ": C must be a multiple of G");
+        if (int rc = use_device(ctx)) return rc;
+        if (ctx->scratch_bytes < need) {  // grows once; stream-ordered so queued work keeps its copy valid
+            if (ctx->scratch) {
+                cudaStreamSynchronize(ctx->stream);
+                cudaFree(ctx->scratch);
+                ctx->scratch = nullptr;
+                ctx->scratch_bytes = 0;
+            }
+            if (cudaMalloc(&ctx->scratch, need) != cudaSuccess) {
+                cudaGetLastError();
+                return set_err(ctx, SDVK_E_OOM, name + ": workspace allocation failed");
+            }
+            ctx->scratch_bytes = need;
+        }
+        return sdvk_groupnorm(ctx, static_cast<const float*>(buf_ptr(bufs[0])),
+                              static_cast<const float*>(buf_ptr(bufs[1])), static_cast<const float*>(buf_ptr(bufs[2])),
+                              static_cast<float*>(buf_mptr(bufs[3])), 1, pc.C, pc.P, pc.G, pc.eps, pc.act == 1u,
+                              ctx->scratch, ctx->scratch_bytes);
     }
     if (is({"fused_attn", "fused_attn_tiled"})) {
         if (push_bytes < sizeof(FaPush) || nbufs < 4u)

@@ -30,11 +30,15 @@ uint64_t now_ns() {
 
 inline void* at(const BufRef& b) { return static_cast<unsigned char*>(b.buf) + b.offset; }
 
-// Push-constant sizes of the hot-path kernels: Pg (48 B, sdvkgen.cpp:901-903) for the Q8 GEMMs,
-// FaPush (36 B, fused_attn.cpp:15-26) for attention.  0 = not a kernel this back end runs.
+// Push-constant sizes of the kernels this back end runs (the reference's kernel table,
+// vk_engine.cpp:51-125): Pg (48 B, sdvkgen.cpp:901-903) for the Q8 GEMMs, FaPush (36 B,
+// fused_attn.cpp:15-26) for attention, 16 B for layernorm_fwd and 20 B for groupnorm
+// (vk_engine.cpp:117,119).  0 = not a kernel this back end runs.
 uint32_t push_size(const char* kernel) {
     if (!std::strncmp(kernel, "gemm_nt_q8", 10) || !std::strncmp(kernel, "gemm_nn_q8", 10)) return 48;
     if (!std::strncmp(kernel, "fused_attn", 10)) return 36;
+    if (!std::strcmp(kernel, "layernorm_fwd")) return 16;
+    if (!std::strcmp(kernel, "groupnorm")) return 20;
     return 0;
 }
 

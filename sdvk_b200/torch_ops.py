@@ -167,6 +167,33 @@ def cfg_combine(cond: torch.Tensor, uncond: torch.Tensor, cfg: float, rescale: f
     return out
 
 
+def q8_0_ingest(blocks: torch.Tensor, rows: int, cols: int, ldq: int = 0):
+    """Split raw GGUF Q8_0 blocks (uint8 on the device, rows*cols/32 blocks of 34 bytes) into the int8
+    payload [rows, ldq or cols] and fp32 scales [rows * (ldq or cols) / 32] (sdvk_q8_0_ingest)."""
+    assert blocks.dtype == torch.uint8 and blocks.is_contiguous() and blocks.numel() == rows * cols // 32 * 34
+    ld = ldq or cols
+    q = torch.zeros((rows, ld), dtype=torch.int8, device=blocks.device)
+    s = torch.zeros((rows * ld // 32,), dtype=torch.float32, device=blocks.device)
+    context(blocks.device).q8_0_ingest(blocks.data_ptr(), rows, cols, q.data_ptr(), ld, s.data_ptr())
+    return q, s
+
+
+def groupnorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, groups: int = 32, eps: float = 1e-5,
+              silu: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """GroupNorm (+SiLU) of fp32 x [B, C, *spatial] (groupnorm.comp), via sdvk_groupnorm."""
+    assert x.dtype == torch.float32 and x.is_contiguous() and x.dim() >= 2
+    B, C = x.shape[0], x.shape[1]
+    P = x.numel() // (B * C)
+    if out is None:
+        out = torch.empty_like(x)
+    ctx = context(x.device)
+    nbytes = ctx.groupnorm_workspace(B, C, P, groups)
+    ws = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=x.device)
+    ctx.groupnorm(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), out.data_ptr(), B, C, P, groups, eps, silu,
+                  ws.data_ptr(), ws.numel())
+    return out
+
+
 def geglu_interleave(q: torch.Tensor, s: torch.Tensor, bias: Optional[torch.Tensor] = None):
     """Repack an ff.net.0.proj Q8_0 weight [2F, K] for the GEGLU epilogue (sdvk_geglu_interleave)."""
     two_f, K = q.shape

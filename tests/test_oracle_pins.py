@@ -235,3 +235,14 @@ def test_block_restatement_vs_f64(orc):
     got = orc.block_shader(x, ctx, heads, W)
     st = orc.err_stats(got - x, ref - x)
     assert st["rel_rms"] < 1e-5 and st["rel_max_rms"] < 1e-4, st
+
+
+@pytest.mark.parametrize("B,C,P,G,act", [(1, 64, 300, 8, 0), (2, 12, 7, 3, 1), (1, 320, 1024, 32, 1)])
+def test_groupnorm_restatement_against_f64(orc, B, C, P, G, act):
+    """The fp32 restatement of groupnorm.comp (lane-strided partial sums, a tree over 256 lanes, two
+    passes) stays within fp32 rounding of the float64 GroupNorm (+SiLU)."""
+    x = orc.normal_f32(43, 0, (B, C, P)) * 2.0 + 0.5
+    g = orc.normal_f32(43, 1, (C,)) * 0.2 + 1.0
+    b = orc.normal_f32(43, 2, (C,)) * 0.1
+    st = orc.err_stats(orc.groupnorm_shader(x, g, b, G, 1e-5, act), orc.groupnorm_f64(x, g, b, G, 1e-5, act))
+    assert st["rel_max"] <= 2e-6, st
