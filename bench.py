@@ -404,8 +404,94 @@ class BlockWorkload:
                 + 2.0 * Tc * 2 * C * Cc + 4.0 * self.H * rows * (T + Tc) * 64)
 
 
+class GroupNormWorkload:
+    """The ResBlock's GroupNorm + SiLU (groupnorm.comp via gnInto, sdvkgen.cpp:1105-1113) at the first
+    UNet level of a 1024^2 latent: 2 images, 320 channels, 128 x 128, 32 groups.  HBM-bound."""
+
+    dtype = "f32"
+    unit = "GB/s"
+    launches_per_step = 2  # statistics, apply
+
+    def __init__(self, B=2, C=320, H=128, W=128, G=32):
+        self.name = "groupnorm"
+        self.B, self.C, self.P, self.G = B, C, H * W, G
+        self.bytes = 2.0 * 4 * B * C * self.P  # x read once, y written once
+        self.work = self.bytes
+        self.flop = 8.0 * B * C * self.P
+        self.bound = "hbm"
+        self.metric = f"GroupNorm+SiLU GB/s @B{B} C{C} {H}x{W} G{G}"
+        self.describe = (f"GroupNorm + SiLU (groupnorm.comp, ResBlock): {B} images, {C} channels, {H}x{W}, {G} groups, "
+                         f"fp32 x ~N(0,1) channel-major, gamma ~1, beta ~0, eps 1e-5")
+        self.rotate = max(2, -(-2 * L2_BYTES // int(self.bytes)))
+        self.cpu_units = G
+        self.cpu_what = "groups of image 0 (fp32 restatement of groupnorm.comp)"
+
+    def make_set(self, torch, device, seed):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        x = torch.randn((self.B, self.C, self.P), generator=g, device=device, dtype=torch.float32)
+        gamma = 1.0 + 0.1 * torch.randn((self.C,), generator=g, device=device, dtype=torch.float32)
+        beta = 0.1 * torch.randn((self.C,), generator=g, device=device, dtype=torch.float32)
+        y = torch.empty_like(x)
+        import sdvk_b200
+
+        nbytes = sdvk_b200.Context.groupnorm_workspace(self.B, self.C, self.P, self.G)
+        ws = torch.empty((nbytes,), dtype=torch.uint8, device=device)
+        return x, gamma, beta, y, ws
+
+    def step(self, torch_ops, st):
+        x, gamma, beta, y, ws = st
+        torch_ops.context(x.device).groupnorm(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), y.data_ptr(), self.B,
+                                              self.C, self.P, self.G, 1e-5, True, ws.data_ptr(), ws.numel())
+
+    def e2e(self, sdvk_b200, ctx, torch, st):
+        """Per step: pinned x -> device, GroupNorm + SiLU, device y -> pinned host."""
+        x, gamma, beta, y, ws = st
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x.cpu())
+        yh = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+
+        def run():
+            ctx.upload_async(x.data_ptr(), xh.data_ptr(), xh.numel() * 4)
+            ctx.groupnorm(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), y.data_ptr(), self.B, self.C, self.P,
+                          self.G, 1e-5, True, ws.data_ptr(), ws.numel())
+            ctx.download_async(yh.data_ptr(), y.data_ptr(), yh.numel() * 4)
+
+        return run, xh.numel() * 4, yh.numel() * 4, "sdvk_upload_async + sdvk_groupnorm + sdvk_download_async"
+
+    def host_inputs(self):
+        rng = np.random.default_rng(1)
+        x = rng.standard_normal((1, self.C, self.P), dtype=np.float32)
+        gamma = (1.0 + 0.1 * rng.standard_normal(self.C)).astype(np.float32)
+        beta = (0.1 * rng.standard_normal(self.C)).astype(np.float32)
+        return x, gamma, beta
+
+    def cpu_run(self, inputs, groups):
+        from oracle import pyoracle
+
+        x, gamma, beta = inputs
+        cg = self.C // self.G
+        ch = groups * cg
+        pyoracle.groupnorm_shader(np.ascontiguousarray(x[:, :ch]), gamma[:ch], beta[:ch], groups, 1e-5, 1)
+        return 2.0 * 4 * ch * self.P
+
+
+def wl_unit(wl):
+    return getattr(wl, "unit", "TFLOP/s")
+
+
+def wl_work(wl):
+    """The workload's unit of work per step: FLOP, or bytes for the GB/s workloads."""
+    return getattr(wl, "work", wl.flop)
+
+
+def wl_scale(wl):
+    return 1e12 if wl_unit(wl) == "TFLOP/s" else 1e9
+
+
 WORKLOADS = {
     "gemm": GemmWorkload,
+    "groupnorm": GroupNormWorkload,
     "block": BlockWorkload,
     "attn-self-4096": lambda: AttnWorkload("attn-self-4096", 2, 4096, 4096, 10),
     "attn-self-1024": lambda: AttnWorkload("attn-self-1024", 2, 1024, 1024, 20),
@@ -445,15 +531,15 @@ def run_reference(args, rank, world, wl):
         return 0
     budget = 60.0
     fps, units, _, dt, threads = cpu_sample(wl, budget, steps=args.steps)
-    value = fps / 1e12
+    value = fps / wl_scale(wl)
     sample = f"{units} of {wl.cpu_units} {wl.cpu_what} per step"
     line = {
-        "impl": "reference", "metric": wl.metric, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "impl": "reference", "metric": wl.metric, "value": value, "unit": wl_unit(wl), "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": wl.describe, "sample_units": units},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": value, "unit": wl_unit(wl), "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": wl_unit(wl), "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference Vulkan path unavailable on this box (no graphics stack); its shader arithmetic is timed "
                 "as the oracle's C++ restatement on the host cores",
     }
@@ -547,7 +633,7 @@ def main(argv=None):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ms_per_step = ms_max / args.steps
-    value = world * wl.flop * args.steps / (ms_max * 1e-3) / 1e12
+    value = world * wl_work(wl) * args.steps / (ms_max * 1e-3) / wl_scale(wl)
 
     # ---- end to end through the C ABI with pinned host buffers
     e2e_steps = min(args.steps, 100)
@@ -567,13 +653,13 @@ def main(argv=None):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item()) / e2e_steps
-    e2e_value = world * wl.flop / (e2e_ms * 1e-3) / 1e12
+    e2e_value = world * wl_work(wl) / (e2e_ms * 1e-3) / wl_scale(wl)
 
     # ---- CPU baseline (rank 0, N = 1 only): a bounded sample of the same workload
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         fps, units, runs, secs, threads = cpu_sample(wl, budget_s=15.0)
-        cpu = {"value": fps / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+        cpu = {"value": fps / wl_scale(wl), "unit": wl_unit(wl), "cores": threads, "kind": "port",
                "sample": f"{runs} x {units} of {wl.cpu_units} {wl.cpu_what}, {secs:.1f} s"}
 
     pk, pk_kind = peaks()
@@ -589,7 +675,7 @@ def main(argv=None):
                  "algorithmic_bytes_per_launch": wl.bytes})
     if rank == 0:
         line = {
-            "metric": wl.metric, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "metric": wl.metric, "value": value, "unit": wl_unit(wl), "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
             "config": {"workload": wl.describe, "parallelism": f"replicas x{world}",
@@ -597,7 +683,7 @@ def main(argv=None):
                        f"{wl.rotate} rotating input/output sets ({wl.rotate * wl.bytes / 1e6:.0f} MB > 126 MB L2)",
                        "timing": f"CUDA events over CUDA-graph replays of {GRAPH_LEN} launches"},
             "roofline": roof,
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "e2e": {"value": e2e_value, "unit": wl_unit(wl), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "path": path + ", pinned host buffers"},
             "gpu_launches": args.steps * getattr(wl, "launches_per_step", 1),
             "clocks": clocks,

@@ -11,10 +11,10 @@
 // P = H*W), G groups of C/G channels; per (batch, group) mean and variance over C/G*P values,
 // y = (x - mean) / sqrt(var + eps) * gamma[c] + beta[c], optionally SiLU v / (1 + e^-v).  A group of a
 // 128x128 latent holds up to 655 k values, so the statistics are split over CTAs: each CTA reduces a
-// chunk to (count, mean, M2) with a two-pass sum over its chunk (the reference's two-pass form), a
-// one-warp kernel merges a group's chunks with Chan's pairwise update, and the apply kernel
-// normalises.  All three are HBM-bound: x is read twice (the second stats pass hits L2) and y
-// written once.
+// chunk to (count, mean, M2) with a two-pass sum over its chunk (the reference's two-pass form), and
+// each apply CTA (one channel row) merges its group's chunks with Chan's pairwise update before
+// normalising.  Both are HBM-bound: x is read twice (the second stats pass hits L2) and y written
+// once.
 #include <algorithm>
 #include <cmath>
 
@@ -99,9 +99,10 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // grid (chunks, G, B): (count, mean, M2) of chunk c of group g of image b, two passes over the chunk
-// (the second from L2).
+// (the second from L2).  vec: 16-byte loads (x 16-byte aligned and P % 4 == 0, so every group,
+// chunk and channel row starts on a 16-byte boundary).
 __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const float* __restrict__ x, uint32_t C, uint32_t P,
-                                                              uint32_t G, GnStat* __restrict__ stats) {
+                                                              uint32_t G, bool vec, GnStat* __restrict__ stats) {
     grid_dependency_wait();
     grid_launch_dependents();
     __shared__ float red[kGnThreads / 32];
@@ -110,56 +111,95 @@ __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const float* __res
     const float* xg = x + (uint64_t)b * C * P + (uint64_t)g * cnt;
     const uint64_t lo = (uint64_t)blockIdx.x * kGnChunk, hi = min(cnt, lo + kGnChunk);
     float s = 0.0f;
-    for (uint64_t i = lo + threadIdx.x; i < hi; i += kGnThreads) s += xg[i];
+    if (vec) {
+#pragma unroll 4
+        for (uint64_t i = lo + 4 * threadIdx.x; i < hi; i += 4 * kGnThreads) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(xg + i));
+            s += (v.x + v.y) + (v.z + v.w);
+        }
+    } else {
+        for (uint64_t i = lo + threadIdx.x; i < hi; i += kGnThreads) s += xg[i];
+    }
     const float n = (float)(hi - lo);
     const float mean = block_sum(s, red) / n;
     float ss = 0.0f;
-    for (uint64_t i = lo + threadIdx.x; i < hi; i += kGnThreads) {
-        const float d = xg[i] - mean;
-        ss = fmaf(d, d, ss);
+    if (vec) {
+#pragma unroll 4
+        for (uint64_t i = lo + 4 * threadIdx.x; i < hi; i += 4 * kGnThreads) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(xg + i));
+            const float d0 = v.x - mean, d1 = v.y - mean, d2 = v.z - mean, d3 = v.w - mean;
+            ss = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, fmaf(d3, d3, ss))));
+        }
+    } else {
+        for (uint64_t i = lo + threadIdx.x; i < hi; i += kGnThreads) {
+            const float d = xg[i] - mean;
+            ss = fmaf(d, d, ss);
+        }
     }
     const float m2 = block_sum(ss, red);
     if (threadIdx.x == 0) stats[((uint64_t)b * G + g) * chunks + blockIdx.x] = GnStat{n, mean, m2};
 }
 
-// grid (G, B), one warp: merge the group's chunk statistics in a fixed order (Chan et al.'s
-// pairwise update of count, mean and M2) into (mean, 1 / sqrt(var + eps)).
-__global__ void gn_finalize_kernel(const GnStat* __restrict__ stats, uint32_t chunks, float eps,
-                                   float2* __restrict__ norm) {
-    grid_dependency_wait();
-    grid_launch_dependents();
-    if (threadIdx.x != 0) return;
-    const uint64_t gi = (uint64_t)blockIdx.y * gridDim.x + blockIdx.x;
-    const GnStat* st = stats + gi * chunks;
-    float n = st[0].n, m = st[0].mean, m2 = st[0].m2;
-    for (uint32_t c = 1; c < chunks; ++c) {
-        const GnStat o = st[c];
-        const float nn = n + o.n, d = o.mean - m;
-        m += d * (o.n / nn);
-        m2 += o.m2 + d * d * (n * o.n / nn);
-        n = nn;
-    }
-    norm[gi] = make_float2(m, 1.0f / sqrtf(m2 / n + eps));
-}
-
-// grid (blocks over C*P, B): y = (x - mean) * rstd * gamma + beta (+ SiLU v / (1 + e^-v)).
+// grid (C, B): one channel row of one image per CTA.  Warp 0 merges the channel's group statistics
+// (Chan et al.'s pairwise update of count, mean and M2, in a fixed order) into (mean,
+// 1/sqrt(var + eps)), then the CTA writes y = (x - mean) * rstd * gamma[c] + beta[c] (+ SiLU
+// v / (1 + e^-v)).
 __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                               const float* __restrict__ beta, float* __restrict__ y,
-                                                              uint32_t C, uint32_t P, uint32_t G, uint32_t act,
-                                                              const float2* __restrict__ norm) {
+                                                              uint32_t C, uint32_t P, uint32_t G, float eps,
+                                                              uint32_t act, const GnStat* __restrict__ stats,
+                                                              uint32_t chunks, bool vec) {
     grid_dependency_wait();
     grid_launch_dependents();
-    const uint32_t b = blockIdx.y;
-    const uint64_t per = (uint64_t)C * P, cnt = (uint64_t)(C / G) * P;
-    const float* xb = x + (uint64_t)b * per;
-    float* yb = y + (uint64_t)b * per;
-    const float2* nb = norm + (uint64_t)b * G;
-    for (uint64_t i = (uint64_t)blockIdx.x * kGnThreads + threadIdx.x; i < per; i += (uint64_t)gridDim.x * kGnThreads) {
-        const float2 mr = nb[i / cnt];
-        const uint32_t ch = (uint32_t)(i / P);
-        float v = (xb[i] - mr.x) * mr.y * gamma[ch] + beta[ch];
-        if (act) v = v / (1.0f + expf(-v));
-        yb[i] = v;
+    __shared__ float2 norm;
+    const uint32_t c = blockIdx.x, b = blockIdx.y, g = c / (C / G);
+    if (threadIdx.x < 32) {
+        // Warp 0: lane l merges chunks l, l+32, ... in order, then a fixed butterfly over the lanes
+        // (every CTA of the group computes the same result in the same order).
+        const GnStat* st = stats + ((uint64_t)b * G + g) * chunks;
+        float n = 0.0f, m = 0.0f, m2 = 0.0f;
+        auto merge = [](float& n, float& m, float& m2, float on, float om, float om2) {
+            if (on == 0.0f) return;
+            const float nn = n + on, d = om - m;
+            m += d * (on / nn);
+            m2 += om2 + d * d * (n * on / nn);
+            n = nn;
+        };
+        for (uint32_t k = threadIdx.x; k < chunks; k += 32) merge(n, m, m2, st[k].n, st[k].mean, st[k].m2);
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float on = __shfl_xor_sync(0xffffffffu, n, o), om = __shfl_xor_sync(0xffffffffu, m, o),
+                        om2 = __shfl_xor_sync(0xffffffffu, m2, o);
+            // both partners merge the pair in the same order (lower lane first), so they agree
+            if ((threadIdx.x & o) == 0) {
+                merge(n, m, m2, on, om, om2);
+            } else {
+                float pn = on, pm = om, pm2 = om2;
+                merge(pn, pm, pm2, n, m, m2);
+                n = pn, m = pm, m2 = pm2;
+            }
+        }
+        if (threadIdx.x == 0) norm = make_float2(m, 1.0f / sqrtf(m2 / n + eps));
+    }
+    __syncthreads();
+    const float mean = norm.x, sc = norm.y * gamma[c], sh = beta[c];
+    const uint64_t off = ((uint64_t)b * C + c) * P;
+    const float* xr = x + off;
+    float* yr = y + off;
+    // SiLU with the fast exponential and a correctly rounded reciprocal (a few ulp, against a full
+    // division and expf that made the apply pass issue-bound rather than HBM-bound)
+    auto f = [&](float v) {
+        v = (v - mean) * sc + sh;
+        return act ? v * __frcp_rn(1.0f + __expf(-v)) : v;
+    };
+    if (vec) {
+#pragma unroll 4
+        for (uint32_t i = 4 * threadIdx.x; i < P; i += 4 * kGnThreads) {
+            const float4 v = __ldcs(reinterpret_cast<const float4*>(xr + i));  // last use of x
+            *reinterpret_cast<float4*>(yr + i) = make_float4(f(v.x), f(v.y), f(v.z), f(v.w));
+        }
+    } else {
+        for (uint32_t i = threadIdx.x; i < P; i += kGnThreads) yr[i] = f(xr[i]);
     }
 }
 
@@ -186,8 +226,7 @@ uint64_t groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G)
     if (G == 0 || C % G) return 0;
     const uint64_t cnt = (uint64_t)(C / G) * P;
     const uint64_t chunks = (cnt + kGnChunk - 1) / kGnChunk;
-    const uint64_t stats = (uint64_t)batch * G * chunks * sizeof(GnStat);
-    return ((stats + 15) / 16) * 16 + (uint64_t)batch * G * sizeof(float2);
+    return (uint64_t)batch * G * chunks * sizeof(GnStat);
 }
 
 int groupnorm(const float* x, const float* gamma, const float* beta, float* y, uint32_t batch, uint32_t C, uint32_t P,
@@ -203,18 +242,12 @@ int groupnorm(const float* x, const float* gamma, const float* beta, float* y, u
     const uint32_t chunks = (uint32_t)((cnt + kGnChunk - 1) / kGnChunk);
     if (chunks > 0x7FFFFFFFu) return fail(env, SDVK_E_SHAPE, "GroupNorm group too large");
     GnStat* st = static_cast<GnStat*>(workspace);
-    const uint64_t stat_bytes = (uint64_t)batch * G * chunks * sizeof(GnStat);
-    float2* norm = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + ((stat_bytes + 15) / 16) * 16);
+    const bool vec = P % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
     if (int rc = launch_pdl(gn_stats_kernel, dim3(chunks, G, batch), dim3(kGnThreads), 0, env, "gn_stats_kernel launch",
-                            x, C, P, G, st))
+                            x, C, P, G, vec, st))
         return rc;
-    if (int rc = launch_pdl(gn_finalize_kernel, dim3(G, batch), dim3(32), 0, env, "gn_finalize_kernel launch",
-                            (const GnStat*)st, chunks, eps, norm))
-        return rc;
-    const uint64_t per = (uint64_t)C * P;
-    const uint32_t blocks = (uint32_t)std::min<uint64_t>((per + kGnThreads - 1) / kGnThreads, 8ull * env.num_sms);
-    return launch_pdl(gn_apply_kernel, dim3(blocks, batch), dim3(kGnThreads), 0, env, "gn_apply_kernel launch", x, gamma,
-                      beta, y, C, P, G, act, (const float2*)norm);
+    return launch_pdl(gn_apply_kernel, dim3(C, batch), dim3(kGnThreads), 0, env, "gn_apply_kernel launch", x, gamma,
+                      beta, y, C, P, G, eps, act, (const GnStat*)st, chunks, vec);
 }
 
 }  // namespace sdvk
