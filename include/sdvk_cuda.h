@@ -271,6 +271,18 @@ SDVK_API int sdvk_q8_0_ingest(sdvk_ctx* ctx, const void* blocks, uint64_t rows, 
  * mean and population variance, y = (x - mean)/sqrt(var + eps)*gamma[c] + beta[c], then
  * y/(1 + e^-y) when silu != 0.  fp32 in and out; y may alias x.  workspace: device memory of at
  * least sdvk_groupnorm_workspace(batch, C, P, G) bytes, 16-byte aligned. */
+/* 3x3 convolution with a Q8_0 weight (conv3RawInto / conv3s2, sdvkgen.cpp:1133-1175: im2col.comp or
+ * im2col_s2.comp, then gemmNnQ8 with ldc = P, then biasAddCh).  x: x_dtype (F16, BF16 or F32)
+ * [batch][cin][H][W]; q: int8 [cout][cin*9] (k = c*9 + ky*3 + kx; cin*9 % 32 == 0) with fp32 scales
+ * per 32; bias fp32 [cout] or NULL; y: y_dtype (F32 or F16) [batch][cout][OH][OW].  stride 1 pads
+ * 1 on every side (OH = H); stride 2 gives OH = H/2, OW = W/2 with pad_off -1 (symmetric ring, the
+ * UNet downsamplers) or 0 (right/bottom only, the VAE encoder).  F32 input runs the GEMM in tf32.
+ * workspace: device memory for the column matrix, 16-byte aligned; sdvk_conv3x3_workspace gives the
+ * size of one whole image's (any smaller size that holds one band of output rows works, in bands). */
+SDVK_API uint64_t sdvk_conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, int stride, int x_dtype);
+SDVK_API int sdvk_conv3x3_q8(sdvk_ctx* ctx, const void* x, int x_dtype, const int8_t* q, const float* s,
+                             const float* bias, void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout,
+                             uint32_t H, uint32_t W, int stride, int pad_off, void* workspace, uint64_t workspace_bytes);
 SDVK_API uint64_t sdvk_groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G);
 SDVK_API int sdvk_groupnorm(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, float* y,
                             uint32_t batch, uint32_t C, uint32_t P, uint32_t G, float eps, int silu, void* workspace,

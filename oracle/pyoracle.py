@@ -214,6 +214,57 @@ def gemm_nn_q8_f64(q, s, B, batch=1):
     return C
 
 
+# ------------------------------------------------------------------------------ 3x3 convolution
+def im2col3x3(x, stride=1, off=-1):
+    """im2col.comp (stride 1, pad 1) / im2col_s2.comp (stride 2, pad offset off) for one image x [C, H, W]:
+    col[k, p], k = c*9 + ky*3 + kx, p = oh*OW + ow (pure data movement, exact)."""
+    x = np.asarray(x)
+    C, H, W = x.shape
+    if stride == 1:
+        off = -1
+    OH, OW = (H, W) if stride == 1 else (H // 2, W // 2)
+    pad = np.zeros((C, H + 3, W + 3), x.dtype)  # room for offsets -1..+2 on both axes
+    pad[:, 1:H + 1, 1:W + 1] = x
+    col = np.empty((C, 3, 3, OH, OW), x.dtype)
+    for ky in range(3):
+        for kx in range(3):
+            ih = np.arange(OH) * stride + ky + off + 1
+            iw = np.arange(OW) * stride + kx + off + 1
+            col[:, ky, kx] = pad[:, ih][:, :, iw]
+    return col.reshape(C * 9, OH * OW)
+
+
+def conv3x3_shader(x, q, s, bias, stride=1, off=-1):
+    """conv3RawInto / conv3s2 (sdvkgen.cpp:1133-1175) in fp32: im2col, gemm_nn_q8_v.comp, biasAddCh."""
+    x = np.asarray(x, np.float32)
+    out = []
+    for xi in x:
+        col = im2col3x3(xi, stride, off)
+        y = gemm_nn_q8_shader(q, s, col)
+        if bias is not None:
+            y = y + np.asarray(bias, np.float32)[:, None]
+        out.append(y)
+    H, W = x.shape[2], x.shape[3]
+    OH, OW = (H, W) if stride == 1 else (H // 2, W // 2)
+    return np.stack(out).reshape(x.shape[0], -1, OH, OW)
+
+
+def conv3x3_f64(x, q, s, bias, stride=1, off=-1):
+    """The same convolution in float64 with the dequantised weight (the truth)."""
+    x = np.asarray(x, np.float64)
+    qf = np.asarray(q, np.float64)
+    w = (qf.reshape(qf.shape[0], -1, 32) * np.asarray(s, np.float64).reshape(qf.shape[0], -1, 1)).reshape(qf.shape)
+    out = []
+    for xi in x:
+        y = w @ im2col3x3(xi, stride, off)
+        if bias is not None:
+            y = y + np.asarray(bias, np.float64)[:, None]
+        out.append(y)
+    H, W = x.shape[2], x.shape[3]
+    OH, OW = (H, W) if stride == 1 else (H // 2, W // 2)
+    return np.stack(out).reshape(x.shape[0], -1, OH, OW)
+
+
 # ------------------------------------------------------------------------------ attention
 def fused_attention(Q, K, V, Tq, Tk, C, heads, causal=False, force_simple=False):
     Q, K, V = (_c(x, np.float32) for x in (Q, K, V))

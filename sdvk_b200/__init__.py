@@ -113,6 +113,8 @@ SIGNATURES = {
     "sdvk_check_finite": (_I, [_P, _P, _I, _U64]),
     "sdvk_cfg_combine": (_I, [_P, _P, _P, _P, _U64, ctypes.c_float, ctypes.c_float]),
     "sdvk_q8_0_ingest": (_I, [_P, _P, _U64, _U64, _P, _U64, _P]),
+    "sdvk_conv3x3_workspace": (_U64, [_U32, _U32, _U32, _I, _I]),
+    "sdvk_conv3x3_q8": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _U32, _U32, _U32, _U32, _U32, _I, _I, _P, _U64]),
     "sdvk_groupnorm_workspace": (_U64, [_U32, _U32, _U32, _U32]),
     "sdvk_groupnorm": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, ctypes.c_float, _I, _P, _U64]),
     "sdvk_comm_unique_id": (_I, [_P]),
@@ -310,6 +312,16 @@ class Context:
 
     def q8_0_ingest(self, blocks: int, rows: int, cols: int, q: int, ldq: int, scales: int) -> None:
         self._check(lib().sdvk_q8_0_ingest(self._h, blocks, rows, cols, q, ldq, scales), "q8_0_ingest")
+
+    @staticmethod
+    def conv3x3_workspace(cin: int, H: int, W: int, stride: int, x_dtype: int) -> int:
+        return lib().sdvk_conv3x3_workspace(cin, H, W, stride, x_dtype)
+
+    def conv3x3_q8(self, x: int, x_dtype: int, q: int, s: int, bias: Optional[int], y: int, y_dtype: int, batch: int,
+                   cin: int, cout: int, H: int, W: int, stride: int, pad_off: int, workspace: int,
+                   workspace_bytes: int) -> None:
+        self._check(lib().sdvk_conv3x3_q8(self._h, x, x_dtype, q, s, bias or None, y, y_dtype, batch, cin, cout, H, W,
+                                          stride, pad_off, workspace or None, workspace_bytes), "conv3x3_q8")
 
     @staticmethod
     def groupnorm_workspace(batch: int, C: int, P: int, G: int) -> int:

@@ -74,6 +74,11 @@ int check_finite(const void* x, int dtype, uint64_t n, uint32_t* flag_dev, const
 int q8_0_ingest(const void* blocks, uint64_t rows, uint64_t cols, int8_t* q, uint64_t ldq, float* scales,
                 const LaunchEnv& env);
 uint64_t groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G);
+// conv.cu: 3x3 convolution with Q8_0 weights (im2col + NN GEMM).
+uint64_t conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, uint32_t stride, int dtype);
+int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, void* y, int y_dtype,
+               uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W, uint32_t stride, int off,
+               void* workspace, uint64_t ws_bytes, const LaunchEnv& env);
 int groupnorm(const float* x, const float* gamma, const float* beta, float* y, uint32_t batch, uint32_t C, uint32_t P,
               uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes, const LaunchEnv& env);
 

@@ -1,0 +1,118 @@
+// conv.cu -- the UNet's 3x3 convolutions with Q8_0 weights: im2col + the Q8_0 NN GEMM, the
+// reference's structure (conv3RawInto and conv3s2, sdvkgen.cpp:1133-1175; im2col.comp and
+// im2col_s2.comp; gemmNnQ8 with ldc = P; biasAddCh).
+//
+// x [batch][cin][H][W] (channel-major), weight [cout][cin*9] with k = c*9 + ky*3 + kx, output
+// [batch][cout][OH][OW].  Stride 1 pads 1 on every side; stride 2 gives OH = H/2, OW = W/2 with either
+// the symmetric pad-1 ring (off = -1, the UNet downsamplers) or padding on the right/bottom only
+// (off = 0, the VAE encoder's Downsample2D).  The column matrix col[k][p] (p over a band of output rows)
+// goes to a caller-provided workspace in the GEMM's activation type, in bands of output rows that fit
+// it; the GEMM writes the band's output columns with the row stride OH*OW and adds the bias in its
+// epilogue.  An implicit-GEMM form that never materialises col (TMA im2col loads) is the next step.
+#include <algorithm>
+
+#include "backend.hpp"
+#include "ptx.cuh"
+
+namespace sdvk {
+namespace {
+
+constexpr int kColThreads = 256;
+
+// grid (ceil(np / 256), K): col[k][p] = x[c][oh*stride + ky + off][ow*stride + kx + off] (0 outside),
+// rows of col ld elements apart.
+template <class T>
+__global__ void __launch_bounds__(kColThreads) im2col3x3_kernel(const T* __restrict__ x, T* __restrict__ col,
+                                                                uint32_t H, uint32_t W, uint32_t OW, uint32_t row0,
+                                                                uint32_t np, uint64_t ld, uint32_t stride, int off) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const uint32_t k = blockIdx.y;
+    const uint32_t p = blockIdx.x * kColThreads + threadIdx.x;
+    if (p >= np) return;
+    const uint32_t c = k / 9, r = k - c * 9, ky = r / 3, kx = r - ky * 3;
+    const uint32_t oh = row0 + p / OW, ow = p % OW;
+    const int ih = (int)(oh * stride + ky) + off, iw = (int)(ow * stride + kx) + off;
+    T v = T(0.0f);
+    if (ih >= 0 && ih < (int)H && iw >= 0 && iw < (int)W) v = x[((uint64_t)c * H + ih) * W + iw];
+    col[(uint64_t)k * ld + p] = v;
+}
+
+}  // namespace
+
+uint64_t conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, uint32_t stride, int dtype) {
+    if (stride != 1 && stride != 2) return 0;
+    const uint32_t OH = stride == 1 ? H : H / 2, OW = stride == 1 ? W : W / 2;
+    return (uint64_t)cin * 9 * OH * OW * dtype_size(dtype);
+}
+
+int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, void* y, int y_dtype,
+               uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W, uint32_t stride, int off,
+               void* workspace, uint64_t ws_bytes, const LaunchEnv& env) {
+    if (!x || !q || !s || !y) return fail(env, SDVK_E_ARG, "null pointer");
+    if (x_dtype != SDVK_F16 && x_dtype != SDVK_BF16 && x_dtype != SDVK_F32)
+        return fail(env, SDVK_E_ARG, "conv input must be F16, BF16 or F32");
+    if (y_dtype != SDVK_F16 && y_dtype != SDVK_F32) return fail(env, SDVK_E_ARG, "conv output must be F16 or F32");
+    if (stride != 1 && stride != 2) return fail(env, SDVK_E_SHAPE, "conv stride must be 1 or 2");
+    if (stride == 1) off = -1;
+    if (off != -1 && off != 0) return fail(env, SDVK_E_SHAPE, "conv padding offset must be -1 or 0");
+    if (batch == 0 || cout == 0 || H == 0 || W == 0) return SDVK_OK;
+    const uint32_t K = cin * 9;
+    if (cin == 0 || K % 32) return fail(env, SDVK_E_SHAPE, "conv needs cin*9 % 32 == 0 (whole Q8_0 blocks)");
+    const uint32_t OH = stride == 1 ? H : H / 2, OW = stride == 1 ? W : W / 2;
+    if (OH == 0 || OW == 0) return SDVK_OK;
+    const uint64_t P = (uint64_t)OH * OW, es = dtype_size(x_dtype);
+    // Bands of output rows: a band's column matrix (pitch rows*OW elements, a multiple of 8 so that
+    // the GEMM's TMA rows and every band's output columns start 16-byte aligned) must fit the
+    // workspace.  The last band may be shorter; it keeps the pitch.
+    const uint64_t row_bytes = (uint64_t)K * OW * es;
+    uint32_t rows = (uint32_t)std::min<uint64_t>(OH, workspace ? ws_bytes / row_bytes : 0);
+    while (rows > 0 && ((uint64_t)rows * OW) % 8 && rows < OH) --rows;
+    if (rows < OH && ((uint64_t)rows * OW) % 8) rows = 0;
+    if (rows == 0 || (reinterpret_cast<uintptr_t>(workspace) & 15u))
+        return fail(env, SDVK_E_ARG, "conv workspace too small for one aligned band of output rows, or misaligned");
+    const uint64_t pitch = (uint64_t)rows * OW;
+    const uint64_t xs = (uint64_t)cin * H * W * es, ys = (uint64_t)cout * P * dtype_size(y_dtype);
+    for (uint32_t bi = 0; bi < batch; ++bi) {
+        const uint8_t* xb = static_cast<const uint8_t*>(x) + bi * xs;
+        uint8_t* yb = static_cast<uint8_t*>(y) + bi * ys;
+        for (uint32_t r0 = 0; r0 < OH; r0 += rows) {
+            const uint32_t rr = std::min(rows, OH - r0), np = rr * OW;
+            const dim3 grid((np + kColThreads - 1) / kColThreads, K);
+            int rc;
+            if (x_dtype == SDVK_F32)
+                rc = launch_pdl(im2col3x3_kernel<float>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
+                                reinterpret_cast<const float*>(xb), static_cast<float*>(workspace), H, W, OW, r0, np,
+                                pitch, stride, off);
+            else if (x_dtype == SDVK_F16)
+                rc = launch_pdl(im2col3x3_kernel<__half>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
+                                reinterpret_cast<const __half*>(xb), static_cast<__half*>(workspace), H, W, OW, r0, np,
+                                pitch, stride, off);
+            else
+                rc = launch_pdl(im2col3x3_kernel<__nv_bfloat16>, grid, dim3(kColThreads), 0, env,
+                                "im2col3x3_kernel launch", reinterpret_cast<const __nv_bfloat16*>(xb),
+                                static_cast<__nv_bfloat16*>(workspace), H, W, OW, r0, np, pitch, stride, off);
+            if (rc) return rc;
+            GemmQ8Desc d{};
+            d.x = workspace;
+            d.x_dtype = x_dtype;
+            d.ldx = pitch;
+            d.wq = q;
+            d.ws = s;
+            d.ldw = K;
+            d.bias = bias;
+            d.c = yb + (uint64_t)r0 * OW * dtype_size(y_dtype);
+            d.c_dtype = y_dtype;
+            d.ldc = P;
+            d.xrows = np;
+            d.wrows = cout;
+            d.K = K;
+            d.batch = 1;
+            d.nn = true;
+            if ((rc = gemm_q8(d, env))) return rc;
+        }
+    }
+    return SDVK_OK;
+}
+
+}  // namespace sdvk

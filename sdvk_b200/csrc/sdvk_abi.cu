@@ -521,6 +521,19 @@ int sdvk_q8_0_ingest(sdvk_ctx* ctx, const void* blocks, uint64_t rows, uint64_t 
     return sdvk::q8_0_ingest(blocks, rows, cols, q, ldq ? ldq : cols, scales, env_of(ctx));
 }
 
+uint64_t sdvk_conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, int stride, int x_dtype) {
+    return sdvk::conv3x3_workspace(cin, H, W, stride > 0 ? (uint32_t)stride : 0u, x_dtype);
+}
+
+int sdvk_conv3x3_q8(sdvk_ctx* ctx, const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias,
+                    void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W,
+                    int stride, int pad_off, void* workspace, uint64_t workspace_bytes) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::conv3x3_q8(x, x_dtype, q, s, bias, y, y_dtype, batch, cin, cout, H, W,
+                            stride > 0 ? (uint32_t)stride : 0u, pad_off, workspace, workspace_bytes, env_of(ctx));
+}
+
 uint64_t sdvk_groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G) {
     return sdvk::groupnorm_workspace(batch, C, P, G);
 }

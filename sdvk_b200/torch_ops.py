@@ -178,6 +178,24 @@ def q8_0_ingest(blocks: torch.Tensor, rows: int, cols: int, ldq: int = 0):
     return q, s
 
 
+def conv3x3_q8(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, bias: Optional[torch.Tensor] = None,
+               stride: int = 1, pad_off: int = -1, out_dtype: torch.dtype = torch.float32,
+               workspace_bytes: Optional[int] = None) -> torch.Tensor:
+    """3x3 convolution of x [B, cin, H, W] with a Q8_0 weight q [cout, cin*9] (+ fp32 scales, bias)
+    (sdvk_conv3x3_q8; conv3RawInto / conv3s2)."""
+    assert x.is_contiguous() and x.dim() == 4 and q.dtype == torch.int8
+    B, cin, H, W = x.shape
+    cout = q.shape[0]
+    OH, OW = (H, W) if stride == 1 else (H // 2, W // 2)
+    y = torch.empty((B, cout, OH, OW), dtype=out_dtype, device=x.device)
+    ctx = context(x.device)
+    nbytes = workspace_bytes or ctx.conv3x3_workspace(cin, H, W, stride, _dt(x))
+    ws = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=x.device)
+    ctx.conv3x3_q8(x.data_ptr(), _dt(x), q.data_ptr(), s.data_ptr(), bias.data_ptr() if bias is not None else None,
+                   y.data_ptr(), _dt(y), B, cin, cout, H, W, stride, pad_off, ws.data_ptr(), nbytes)
+    return y
+
+
 def groupnorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, groups: int = 32, eps: float = 1e-5,
               silu: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """GroupNorm (+SiLU) of fp32 x [B, C, *spatial] (groupnorm.comp), via sdvk_groupnorm."""

@@ -246,3 +246,29 @@ def test_groupnorm_restatement_against_f64(orc, B, C, P, G, act):
     b = orc.normal_f32(43, 2, (C,)) * 0.1
     st = orc.err_stats(orc.groupnorm_shader(x, g, b, G, 1e-5, act), orc.groupnorm_f64(x, g, b, G, 1e-5, act))
     assert st["rel_max"] <= 2e-6, st
+
+
+def test_im2col_restatement_matches_shader_loops(orc):
+    """The oracle's im2col equals a line-by-line transcription of im2col.comp / im2col_s2.comp."""
+    def loop(x, stride, off):
+        C, H, W = x.shape
+        OH, OW = (H, W) if stride == 1 else (H // 2, W // 2)
+        if stride == 1:
+            off = -1
+        P = OH * OW
+        col = np.zeros((C * 9, P), x.dtype)
+        for i in range(C * 9 * P):
+            k = i // P
+            p = i - k * P
+            c = k // 9
+            r = k - c * 9
+            ky, kx = r // 3, r - (r // 3) * 3
+            oh, ow = p // OW, p % OW
+            ih, iw = oh * stride + ky + off, ow * stride + kx + off
+            if 0 <= ih < H and 0 <= iw < W:
+                col[k, p] = x[c, ih, iw]
+        return col
+
+    x = orc.normal_f32(44, 0, (3, 7, 9))
+    for stride, off in ((1, -1), (2, -1), (2, 0)):
+        assert np.array_equal(loop(x, stride, off), orc.im2col3x3(x, stride, off))
