@@ -476,6 +476,84 @@ class GroupNormWorkload:
         return 2.0 * 4 * ch * self.P
 
 
+class ConvWorkload:
+    """A ResBlock 3x3 convolution with a Q8_0 weight (conv3RawInto, sdvkgen.cpp:1133-1158) at the first
+    UNet level of a 1024^2 latent: 2 images, 320 -> 320 channels, 128 x 128."""
+
+    dtype = "f16"
+
+    def __init__(self, B=2, cin=320, cout=320, H=128, W=128):
+        self.name = "conv"
+        self.B, self.cin, self.cout, self.H, self.W = B, cin, cout, H, W
+        P, K = H * W, cin * 9
+        self.flop = 2.0 * B * cout * P * K
+        self.bytes = B * (2.0 * cin * P + 4.0 * cout * P) + cout * K * (1 + 4 / 32)
+        self.bound = "tensor"
+        self.metric = f"Q8_0 conv3x3 TFLOP/s @B{B} {cin}->{cout} {H}x{W}"
+        self.describe = (f"3x3 convolution, Q8_0 weight [{cout}, {cin}*9] (config-0 distribution), {B} images of "
+                         f"{cin}x{H}x{W} fp16 ~N(0,1), fp32 out + bias, im2col + NN GEMM")
+        self.rotate = max(2, -(-2 * L2_BYTES // int(self.bytes)))
+        self.cpu_units = cout
+        self.cpu_what = "output channels of image 0 (fp32 restatement of im2col.comp + gemm_nn_q8_v.comp)"
+        self.launches_per_step = 2 * B
+
+    def make_set(self, torch, device, seed):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        x = torch.randn((self.B, self.cin, self.H, self.W), generator=g, device=device, dtype=torch.float32).half()
+        K = self.cin * 9
+        q = torch.randint(-127, 128, (self.cout, K), generator=g, device=device, dtype=torch.int8)
+        s = torch.rand((self.cout * K // 32,), generator=g, device=device) * (0.02 / 127)
+        bias = 0.02 * torch.randn((self.cout,), generator=g, device=device)
+        y = torch.empty((self.B, self.cout, self.H, self.W), device=device, dtype=torch.float32)
+        import sdvk_b200
+
+        nbytes = sdvk_b200.Context.conv3x3_workspace(self.cin, self.H, self.W, 1, sdvk_b200.F16)
+        ws = torch.empty((nbytes,), dtype=torch.uint8, device=device)
+        return x, q, s, bias, y, ws
+
+    def _call(self, ctx, st):
+        import sdvk_b200
+
+        x, q, s, bias, y, ws = st
+        ctx.conv3x3_q8(x.data_ptr(), sdvk_b200.F16, q.data_ptr(), s.data_ptr(), bias.data_ptr(), y.data_ptr(),
+                       sdvk_b200.F32, self.B, self.cin, self.cout, self.H, self.W, 1, -1, ws.data_ptr(), ws.numel())
+
+    def step(self, torch_ops, st):
+        self._call(torch_ops.context(st[0].device), st)
+
+    def e2e(self, sdvk_b200, ctx, torch, st):
+        """Per step: pinned x -> device, convolution, device y -> pinned host."""
+        x, y = st[0], st[4]
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x.cpu())
+        yh = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+
+        def run():
+            ctx.upload_async(x.data_ptr(), xh.data_ptr(), xh.numel() * 2)
+            self._call(ctx, st)
+            ctx.download_async(yh.data_ptr(), y.data_ptr(), yh.numel() * 4)
+
+        return run, xh.numel() * 2, yh.numel() * 4, "sdvk_upload_async + sdvk_conv3x3_q8 + sdvk_download_async"
+
+    def host_inputs(self):
+        from oracle import pyoracle
+
+        rng = np.random.default_rng(1)
+        x = rng.standard_normal((1, self.cin, self.H, self.W), dtype=np.float32).astype(np.float16).astype(np.float32)
+        q, _, s = pyoracle.q8_weights(3, 0, self.cout, self.cin * 9)
+        return x, q, s
+
+    def cpu_run(self, inputs, channels):
+        from oracle import pyoracle
+
+        x, q, s = inputs
+        K = self.cin * 9
+        col = pyoracle.im2col3x3(x[0], 1, -1)
+        pyoracle.gemm_nn_q8_shader(q[:channels], s[:channels * K // 32], col)
+        return 2.0 * channels * self.H * self.W * K
+
+
 def wl_unit(wl):
     return getattr(wl, "unit", "TFLOP/s")
 
@@ -492,6 +570,7 @@ def wl_scale(wl):
 WORKLOADS = {
     "gemm": GemmWorkload,
     "groupnorm": GroupNormWorkload,
+    "conv": ConvWorkload,
     "block": BlockWorkload,
     "attn-self-4096": lambda: AttnWorkload("attn-self-4096", 2, 4096, 4096, 10),
     "attn-self-1024": lambda: AttnWorkload("attn-self-1024", 2, 1024, 1024, 20),

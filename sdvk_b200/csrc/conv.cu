@@ -19,8 +19,10 @@ namespace {
 
 constexpr int kColThreads = 256;
 
-// grid (ceil(np / 256), K): col[k][p] = x[c][oh*stride + ky + off][ow*stride + kx + off] (0 outside),
-// rows of col ld elements apart.
+// grid (ceil(np / (256 * 8)), K): thread = 8 consecutive output positions p of column-matrix row k,
+// col[k][p] = x[c][oh*stride + ky + off][ow*stride + kx + off] (0 outside), stored with 16-byte
+// vector stores (rows of col ld elements apart, ld % 8 == 0; positions in [np, round_up(np, 8)) are
+// written with values the GEMM never reads).
 template <class T>
 __global__ void __launch_bounds__(kColThreads) im2col3x3_kernel(const T* __restrict__ x, T* __restrict__ col,
                                                                 uint32_t H, uint32_t W, uint32_t OW, uint32_t row0,
@@ -28,14 +30,30 @@ __global__ void __launch_bounds__(kColThreads) im2col3x3_kernel(const T* __restr
     grid_dependency_wait();
     grid_launch_dependents();
     const uint32_t k = blockIdx.y;
-    const uint32_t p = blockIdx.x * kColThreads + threadIdx.x;
-    if (p >= np) return;
+    const uint32_t p0 = (blockIdx.x * kColThreads + threadIdx.x) * 8;
+    if (p0 >= np) return;
     const uint32_t c = k / 9, r = k - c * 9, ky = r / 3, kx = r - ky * 3;
-    const uint32_t oh = row0 + p / OW, ow = p % OW;
-    const int ih = (int)(oh * stride + ky) + off, iw = (int)(ow * stride + kx) + off;
-    T v = T(0.0f);
-    if (ih >= 0 && ih < (int)H && iw >= 0 && iw < (int)W) v = x[((uint64_t)c * H + ih) * W + iw];
-    col[(uint64_t)k * ld + p] = v;
+    uint32_t oh = row0 + p0 / OW, ow = p0 % OW;
+    const T* xc = x + (uint64_t)c * H * W;
+    T v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int ih = (int)(oh * stride + ky) + off, iw = (int)(ow * stride + kx) + off;
+        v[j] = (ih >= 0 && ih < (int)H && iw >= 0 && iw < (int)W) ? xc[(uint64_t)ih * W + iw] : T(0.0f);
+        if (++ow == OW) ow = 0, ++oh;
+    }
+    T* dst = col + (uint64_t)k * ld + p0;
+    if constexpr (sizeof(T) == 2) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w[j] = (uint32_t)__builtin_bit_cast(uint16_t, v[2 * j]) |
+                   ((uint32_t)__builtin_bit_cast(uint16_t, v[2 * j + 1]) << 16);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
 }
 
 }  // namespace
@@ -78,7 +96,7 @@ int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, cons
         uint8_t* yb = static_cast<uint8_t*>(y) + bi * ys;
         for (uint32_t r0 = 0; r0 < OH; r0 += rows) {
             const uint32_t rr = std::min(rows, OH - r0), np = rr * OW;
-            const dim3 grid((np + kColThreads - 1) / kColThreads, K);
+            const dim3 grid((np + 8 * kColThreads - 1) / (8 * kColThreads), K);
             int rc;
             if (x_dtype == SDVK_F32)
                 rc = launch_pdl(im2col3x3_kernel<float>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
