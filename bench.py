@@ -554,6 +554,95 @@ class ConvWorkload:
         return 2.0 * channels * self.H * self.W * K
 
 
+class SamplerWorkload:
+    """One model evaluation's sampler work at the SDXL 1024^2 latent (4 x 128 x 128 floats): the
+    guidance combine, x0, the Euler update and the next scaled model input (the reference's default
+    sampler and cfg 7.5; sdvkgen.cpp:3806-3846, 3770-3776, 4011-4019), one sdvk_sampler_step call.
+    The reference runs this on the host between downloading the model output and uploading the next
+    input."""
+
+    dtype = "f32"
+    unit = "GB/s"
+    launches_per_step = 2  # guide pass, update pass
+
+    def __init__(self, n=4 * 128 * 128):
+        self.name = "sampler"
+        self.n = n
+        # eps_c, eps_u and lat read; x0, lat and the model input written
+        self.bytes = 6.0 * 4 * n
+        self.work = self.bytes
+        self.flop = 12.0 * n
+        self.bound = "hbm"
+        self.metric = f"sampler step GB/s @ latent {n} floats, Euler, cfg 7.5"
+        self.describe = (f"sampler step (evalGuided + x0FromEps + finishX0 + Euler update + input scaling) of an SDXL "
+                         f"1024x1024 latent, {n} fp32 values, cond/uncond model outputs ~N(0,1)")
+        self.rotate = max(2, -(-2 * L2_BYTES // int(5 * 4 * n)))
+        self.cpu_units = 64
+        self.cpu_what = "sampler evaluations (C++ restatement of the host loop, one thread)"
+
+    def make_set(self, torch, device, seed):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        n = self.n
+        ec = torch.randn((n,), generator=g, device=device)
+        eu = torch.randn((n,), generator=g, device=device)
+        lat = torch.randn((n,), generator=g, device=device) * 3.0
+        x0 = torch.empty_like(lat)
+        xm = torch.empty_like(lat)
+        return ec, eu, lat, x0, xm
+
+    def _desc(self, sdvk_b200, st):
+        ec, eu, lat, x0, xm = st
+        d = sdvk_b200.SamplerStepDesc()
+        d.kind, d.phase, d.n = sdvk_b200.SAMPLER_EULER, 0, self.n
+        d.eps_c, d.eps_u, d.cfg = ec.data_ptr(), eu.data_ptr(), 7.5
+        d.lat, d.x0, d.x_model = lat.data_ptr(), x0.data_ptr(), xm.data_ptr()
+        d.sigma, d.sigma_next = 3.0, 2.5
+        return d
+
+    def step(self, torch_ops, st):
+        import sdvk_b200
+
+        torch_ops.context(st[0].device).sampler_step(self._desc(sdvk_b200, st))
+
+    def e2e(self, sdvk_b200, ctx, torch, st):
+        """Per step: pinned cond/uncond model outputs -> device, the sampler step, the next model input
+        -> pinned host (the reference's downloadNow / host loop / uploadNow, reversed in direction)."""
+        ec, eu, lat, x0, xm = st
+        ech = torch.empty(ec.shape, dtype=ec.dtype, pin_memory=True)
+        euh = torch.empty(eu.shape, dtype=eu.dtype, pin_memory=True)
+        ech.copy_(ec.cpu())
+        euh.copy_(eu.cpu())
+        xmh = torch.empty(xm.shape, dtype=xm.dtype, pin_memory=True)
+        d = self._desc(sdvk_b200, st)
+        nb = self.n * 4
+
+        def run():
+            ctx.upload_async(ec.data_ptr(), ech.data_ptr(), nb)
+            ctx.upload_async(eu.data_ptr(), euh.data_ptr(), nb)
+            ctx.sampler_step(d)
+            ctx.download_async(xmh.data_ptr(), xm.data_ptr(), nb)
+
+        return run, 2 * nb, nb, "sdvk_upload_async x2 + sdvk_sampler_step + sdvk_download_async"
+
+    def host_inputs(self):
+        rng = np.random.default_rng(1)
+        n = self.n
+        return (rng.standard_normal(n).astype(np.float32), rng.standard_normal(n).astype(np.float32),
+                (rng.standard_normal(n) * 3).astype(np.float32))
+
+    def cpu_run(self, inputs, evals):
+        from oracle import pyoracle
+
+        ec, eu, lat0 = inputs
+        lat = lat0.copy()
+        x0, xm = np.empty_like(lat), np.empty_like(lat)
+        for _ in range(evals):
+            pyoracle.sampler_eval(kind=0, phase=0, n=self.n, eps_c=ec, eps_u=eu, cfg=7.5, lat=lat, x0=x0,
+                                  x_model=xm, sigma=3.0, sigma_next=2.5)
+        return evals * self.bytes
+
+
 def wl_unit(wl):
     return getattr(wl, "unit", "TFLOP/s")
 
@@ -571,6 +660,7 @@ WORKLOADS = {
     "gemm": GemmWorkload,
     "groupnorm": GroupNormWorkload,
     "conv": ConvWorkload,
+    "sampler": SamplerWorkload,
     "block": BlockWorkload,
     "attn-self-4096": lambda: AttnWorkload("attn-self-4096", 2, 4096, 4096, 10),
     "attn-self-1024": lambda: AttnWorkload("attn-self-1024", 2, 1024, 1024, 20),

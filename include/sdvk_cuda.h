@@ -256,6 +256,65 @@ SDVK_API int sdvk_transformer_block_static(sdvk_ctx* ctx, const sdvk_block_desc*
 SDVK_API int sdvk_cfg_combine(sdvk_ctx* ctx, const float* cond, const float* uncond, float* out, uint64_t n, float cfg,
                      float rescale);
 
+/* ---- the sampler step on the device ------------------------------------------------------- */
+/* Sampler kinds, numbered as SamplerKind (src/Modules/Diffusion/GenParams.hpp:16-26). */
+#define SDVK_SAMPLER_EULER 0
+#define SDVK_SAMPLER_EULER_A 1
+#define SDVK_SAMPLER_HEUN 2
+#define SDVK_SAMPLER_LMS 3
+#define SDVK_SAMPLER_DPM2 4
+#define SDVK_SAMPLER_DPM2_A 5
+#define SDVK_SAMPLER_DPMPP_2M 6
+#define SDVK_SAMPLER_DPMPP_2S_A 7
+#define SDVK_SAMPLER_DDIM 8
+
+/* One model evaluation's share of the generation loop (sdvkgen.cpp:3759-4021), replacing the host
+ * code between downloadNow of the model output and uploadNow of the next model input:
+ *   evalGuided (:3811-3846)  non-finite check, res = u + cfg * (c - u), optional spread rescale;
+ *   x0FromEps (:3770-3776) and finishX0 (:3779-3797)  x0, dynamic threshold, inpaint blend;
+ *   the sampler update (:3859-4019)  phase 0 after the step's first evaluation, phase 1 after the
+ *   second one of Heun, DPM2 and DPM2 a (phase 0 of those writes x_tmp, the latent of the second
+ *   evaluation); the last step (sigma_next <= 0) returns x0.
+ * All buffers are fp32 device memory of n floats.  Results equal the host loop's bit for bit,
+ * except with rescale > 0, whose double-precision sums are added in another order (a result may
+ * move by one ulp).  A NaN/Inf in eps_c or eps_u leaves lat unchanged and makes the next
+ * synchronising call return SDVK_E_NOT_FINITE (the reference stops the generation there). */
+typedef struct sdvk_sampler_step_desc {
+    int32_t kind;            /* SDVK_SAMPLER_* */
+    int32_t phase;           /* 0, or 1 for the second evaluation of Heun, DPM2, DPM2 a */
+    uint64_t n;              /* latent floats */
+    const float* eps_c;      /* conditional model output */
+    const float* eps_u;      /* unconditional model output, or NULL when guidance is off (cfg <= 1.0001) */
+    float cfg, rescale;      /* guidance scale; CFG rescale ("mimic scale") factor, 0 = off */
+    int32_t vpred;           /* v-prediction model */
+    int32_t dynthresh;       /* dynamic thresholding at the 99.5th percentile of |x0| */
+    const float* mask;       /* inpaint mask, mask_cells values indexed by k % mask_cells, or NULL */
+    uint64_t mask_cells;
+    const float* init_lat;   /* the encoded init latent the mask blends toward */
+    float* lat;              /* the latent: read, and replaced by the step's result (phase 0 of a
+                                two-evaluation sampler leaves it and writes x_tmp) */
+    float* x_tmp;            /* two-evaluation samplers: the second evaluation's latent */
+    float* x0;               /* out: this evaluation's finished x0 */
+    const float* x0v;        /* phase 1: the step's first x0 (phase 0's x0 output) */
+    float* x0_prev;          /* DPM++ samplers: the previous step's x0 (read when have_prev), then this step's */
+    float* lms[4];           /* LMS: derivative history, newest first; lms[0] receives this step's */
+    int32_t lms_count;       /* LMS: history entries including this step's (1..4) */
+    const float* noise;      /* ancestral samplers: n standard normals for this step (the reference's
+                                nd(rng) draws, in index order) */
+    float sigma, sigma_next; /* the step's sigmas (sch.sigmas[i], sch.sigmas[i + 1]) */
+    float eta;               /* p.eta (0 selects 1) */
+    float sigma_prev;        /* DPM++ with have_prev: the previous step's sigma */
+    int32_t have_prev;
+    float* x_model;          /* optional: the next evaluation's model input, its latent * 1/sqrt(sigma'^2 + 1) */
+    float* thr;              /* optional, device: the dynamic threshold used (1 without dynthresh) */
+} sdvk_sampler_step_desc;
+
+SDVK_API int sdvk_sampler_step(sdvk_ctx* ctx, const sdvk_sampler_step_desc* desc);
+
+/* out = x * 1/sqrt(sigma^2 + 1): the scaled model input of a step's first evaluation
+ * (sdvkgen.cpp:3808-3809). */
+SDVK_API int sdvk_sampler_scale(sdvk_ctx* ctx, const float* x, float* out, uint64_t n, float sigma);
+
 /* ---- model loading and the ResBlock's normalisation ---------------------------------------- */
 /* GGUF Q8_0 ingest on the device (GgufFile::readQ8Into, src/Modules/Model/Gguf.cpp:559-583, and
  * fp16ToFp32, Gguf.cpp:11-35).  blocks: the tensor's raw data in device memory, rows x cols values

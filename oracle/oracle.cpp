@@ -719,4 +719,163 @@ void orc_cfg_combine(const float* cond, const float* uncond, float* out, uint64_
     }
 }
 
+// ------------------------------------------------------------------ the sampler step
+// ancestralSigma (sdvkgen.cpp:2809-2813)
+static float orc_ancestral_sigma(float s_down, float sigma, float eta) {
+    if (sigma <= 0.0f) return 0.0f;
+    const float inside = s_down * s_down * (sigma * sigma - s_down * s_down) / (sigma * sigma);
+    return eta * std::sqrt(std::max(0.0f, inside));
+}
+
+// One evaluation of the loop body sdvkgen.cpp:3796-4019: evalGuided (:3811-3846), x0FromEps
+// (:3770-3776), finishX0 (:3779-3797), then the sampler's switch (:3859-4019).
+uint64_t orc_sampler_eval(const orc_sampler_args* a) {
+    const uint64_t n = a->n;
+    const bool guided = a->eps_u != nullptr;
+    const float sigma = a->sigma, sn = a->sigma_next, dt = sn - sigma;
+    const bool last = sn <= 0.0f;
+    const float eta = a->eta > 0 ? a->eta : 1.0f;
+    // this evaluation's sigma and latent
+    float sig = sigma;
+    if (a->phase == 1) {
+        if (a->kind == 2) sig = sn;
+        else if (a->kind == 4) sig = sigma + 0.5f * dt;
+        else {
+            const float up = std::min(sn, orc_ancestral_sigma(sn, sigma, eta));
+            const float down = std::sqrt(std::max(0.0f, sn * sn - up * up));
+            sig = sigma + 0.5f * (down - sigma);
+        }
+    }
+    const float* x = a->phase == 0 ? a->lat : a->x_tmp;
+    uint64_t bad = 0;
+    for (uint64_t k = 0; k < n; ++k)
+        if (!std::isfinite(a->eps_c[k]) || (guided && !std::isfinite(a->eps_u[k]))) bad++;
+    if (bad) return bad;
+    std::vector<float> res(n);
+    for (uint64_t k = 0; k < n; ++k) res[k] = guided ? a->eps_u[k] + a->cfg * (a->eps_c[k] - a->eps_u[k]) : a->eps_c[k];
+    if (a->rescale > 0.0f && guided) {
+        double m = 0, s2 = 0, u2 = 0;
+        for (uint64_t k = 0; k < n; ++k) m += res[k];
+        m /= (double)n;
+        for (uint64_t k = 0; k < n; ++k) {
+            const double d = res[k] - m;
+            s2 += d * d;
+        }
+        for (uint64_t k = 0; k < n; ++k) u2 += (double)a->eps_u[k] * a->eps_u[k];
+        const double su = std::sqrt(u2 / (double)n);
+        const double sg = std::sqrt(s2 / (double)n) + 1e-6;
+        for (uint64_t k = 0; k < n; ++k) {
+            const float er = (float)((res[k] - m) * (su / sg) + m);
+            res[k] = (float)(a->rescale * er + (1.0 - a->rescale) * res[k]);
+        }
+    }
+    // x0FromEps
+    const float s2 = sig * sig + 1.0f, root = std::sqrt(s2);
+    float* x0 = a->x0;
+    for (uint64_t k = 0; k < n; ++k) x0[k] = a->vpred ? res[k] * (-sig / root) + x[k] / s2 : x[k] - sig * res[k];
+    // finishX0
+    float thr = 1.0f;
+    if (a->dynthresh) {
+        std::vector<float> absv(n);
+        for (uint64_t k = 0; k < n; ++k) absv[k] = std::abs(x0[k]);
+        const size_t q = (size_t)((double)(n - 1) * 0.995);
+        std::nth_element(absv.begin(), absv.begin() + q, absv.end());
+        thr = std::max(absv[q], 1.0f);
+    }
+    for (uint64_t k = 0; k < n; ++k) {
+        float v = x0[k];
+        if (a->dynthresh) v = std::min(std::max(v, -thr), thr) / thr;
+        if (a->mask) {
+            const float m = a->mask[k % a->mask_cells];
+            v = m * v + (1.0f - m) * a->init_lat[k];
+        }
+        x0[k] = v;
+    }
+    if (a->thr) *a->thr = thr;
+    // the update
+    float* lat = a->lat;
+    std::vector<float> out(n);
+    float next_sigma = sn;
+    bool to_tmp = false;
+    if (last) {
+        for (uint64_t k = 0; k < n; ++k) out[k] = a->phase == 0 ? x0[k] : a->x0v[k];
+    } else if (a->kind == 1) {  // Euler a
+        const float up = orc_ancestral_sigma(sn, sigma, eta);
+        const float down = std::sqrt(std::max(0.0f, sn * sn - up * up));
+        const float ratio = down / sigma;
+        for (uint64_t k = 0; k < n; ++k) out[k] = lat[k] + (lat[k] - x0[k]) * (ratio - 1.0f) + a->noise[k] * up;
+    } else if (a->kind == 2) {  // Heun
+        if (a->phase == 0) {
+            for (uint64_t k = 0; k < n; ++k) out[k] = lat[k] + (lat[k] - x0[k]) / sigma * dt;
+            to_tmp = true;
+        } else {
+            for (uint64_t k = 0; k < n; ++k)
+                out[k] = lat[k] + 0.5f * ((lat[k] - a->x0v[k]) / sigma + (a->x_tmp[k] - x0[k]) / sn) * dt;
+        }
+    } else if (a->kind == 3) {  // LMS
+        static const float coeff[4][4] = {
+            {1.0f, 0.0f, 0.0f, 0.0f},
+            {3.0f / 2.0f, -1.0f / 2.0f, 0.0f, 0.0f},
+            {23.0f / 12.0f, -16.0f / 12.0f, 5.0f / 12.0f, 0.0f},
+            {55.0f / 24.0f, -59.0f / 24.0f, 37.0f / 24.0f, -9.0f / 24.0f},
+        };
+        for (uint64_t k = 0; k < n; ++k) a->lms[0][k] = (lat[k] - x0[k]) / sigma;
+        const float* cf = coeff[a->lms_count - 1];
+        for (uint64_t k = 0; k < n; ++k) {
+            float acc = 0.0f;
+            for (int j = 0; j < a->lms_count; ++j) acc += cf[j] * a->lms[j][k];
+            out[k] = lat[k] + dt * acc;
+        }
+    } else if (a->kind == 4 || a->kind == 5) {  // DPM2, DPM2 a
+        float up = 0.0f, step = dt;
+        if (a->kind == 5) {
+            up = std::min(sn, orc_ancestral_sigma(sn, sigma, eta));
+            step = std::sqrt(std::max(0.0f, sn * sn - up * up)) - sigma;
+        }
+        const float mid = sigma + 0.5f * step;
+        if (a->phase == 0) {
+            for (uint64_t k = 0; k < n; ++k) out[k] = lat[k] + (lat[k] - x0[k]) / sigma * (0.5f * step);
+            to_tmp = true;
+            next_sigma = mid;
+        } else {
+            for (uint64_t k = 0; k < n; ++k) {
+                float v = lat[k] + (a->x_tmp[k] - x0[k]) / mid * step;
+                if (a->kind == 5) v = v + a->noise[k] * up;  // (a + b) + c, left to right
+                out[k] = v;
+            }
+        }
+    } else if (a->kind == 6 || a->kind == 7) {  // DPM++ 2M, DPM++ 2S a
+        float up = 0.0f, num = sn;
+        if (a->kind == 7) {
+            up = std::min(sn, orc_ancestral_sigma(sn, sigma, eta));
+            num = std::sqrt(std::max(0.0f, sn * sn - up * up));
+        }
+        const double t_now = -std::log((double)sigma), t_n = -std::log((double)sn), h = t_n - t_now;
+        if (!a->have_prev) {
+            for (uint64_t k = 0; k < n; ++k) out[k] = (num / sigma) * lat[k] - std::expm1(-h) * x0[k];
+        } else {
+            const double r = (t_now - -std::log((double)a->sigma_prev)) / h;
+            const float c0 = (float)(1.0 + 1.0 / (2.0 * r)), c1 = (float)(1.0 / (2.0 * r));
+            for (uint64_t k = 0; k < n; ++k) {
+                const float x0d = c0 * x0[k] - c1 * a->x0_prev[k];
+                out[k] = (num / sigma) * lat[k] - std::expm1(-h) * x0d;
+            }
+        }
+        if (a->kind == 7)
+            for (uint64_t k = 0; k < n; ++k) out[k] += a->noise[k] * up;
+        for (uint64_t k = 0; k < n; ++k) a->x0_prev[k] = x0[k];
+    } else if (a->kind == 8) {  // DDIM
+        for (uint64_t k = 0; k < n; ++k) out[k] = x0[k] + (sn / sigma) * (lat[k] - x0[k]);
+    } else {  // Euler
+        for (uint64_t k = 0; k < n; ++k) out[k] = lat[k] + (lat[k] - x0[k]) / sigma * dt;
+    }
+    float* dst = to_tmp ? a->x_tmp : lat;
+    for (uint64_t k = 0; k < n; ++k) dst[k] = out[k];
+    if (a->x_model && !last) {  // evalGuided's input scaling for the next evaluation
+        const float inv = 1.0f / std::sqrt(next_sigma * next_sigma + 1.0f);
+        for (uint64_t k = 0; k < n; ++k) a->x_model[k] = dst[k] * inv;
+    }
+    return 0;
+}
+
 }  // extern "C"

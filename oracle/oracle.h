@@ -85,6 +85,35 @@ void orc_layernorm_f64(const double* x, const float* gamma, const float* beta, d
 void orc_gelu_erf_shader(const float* x, float* y, uint64_t n);
 void orc_cfg_combine(const float* cond, const float* uncond, float* out, uint64_t n, float cfg, float rescale);
 
+/* One model evaluation of the generation loop (src/Modules/Diffusion/sdvkgen.cpp:3759-4021): the
+ * guidance combine and rescale, x0FromEps, finishX0 and the sampler update, sequentially in the
+ * host loop's order.  Field meanings as sdvk_sampler_step_desc (include/sdvk_cuda.h).  Returns the
+ * number of non-finite model outputs (then nothing is written). */
+typedef struct orc_sampler_args {
+    int32_t kind, phase;
+    uint64_t n;
+    const float* eps_c;
+    const float* eps_u;
+    float cfg, rescale;
+    int32_t vpred, dynthresh;
+    const float* mask;
+    uint64_t mask_cells;
+    const float* init_lat;
+    float* lat;
+    float* x_tmp;
+    float* x0;
+    const float* x0v;
+    float* x0_prev;
+    float* lms[4];
+    int32_t lms_count;
+    const float* noise;
+    float sigma, sigma_next, eta, sigma_prev;
+    int32_t have_prev;
+    float* x_model;
+    float* thr;
+} orc_sampler_args;
+uint64_t orc_sampler_eval(const orc_sampler_args* a);
+
 /* ---- misc ------------------------------------------------------------------------------------ */
 int orc_num_threads(void);
 void orc_set_num_threads(int n);

@@ -45,6 +45,7 @@ _SIG = {
     "orc_layernorm_f64": (None, [_P, _P, _P, _P, _U32, _U32, ctypes.c_double]),
     "orc_gelu_erf_shader": (None, [_P, _P, _U64]),
     "orc_cfg_combine": (None, [_P, _P, _P, _U64, _F, _F]),
+    "orc_sampler_eval": (_U64, [_P]),
     "orc_num_threads": (_I, []),
     "orc_set_num_threads": (None, [_I]),
 }
@@ -425,6 +426,89 @@ def cfg_combine(cond, uncond, cfg, rescale=0.0):
     out = np.empty_like(c)
     lib().orc_cfg_combine(_p(c), _p(u), _p(out), c.size, cfg, rescale)
     return out
+
+
+class SamplerArgs(ctypes.Structure):
+    """orc_sampler_args (oracle.h)."""
+
+    _fields_ = [
+        ("kind", ctypes.c_int32), ("phase", ctypes.c_int32), ("n", _U64),
+        ("eps_c", _P), ("eps_u", _P), ("cfg", _F), ("rescale", _F),
+        ("vpred", ctypes.c_int32), ("dynthresh", ctypes.c_int32),
+        ("mask", _P), ("mask_cells", _U64), ("init_lat", _P),
+        ("lat", _P), ("x_tmp", _P), ("x0", _P), ("x0v", _P), ("x0_prev", _P), ("lms", _P * 4),
+        ("lms_count", ctypes.c_int32), ("noise", _P),
+        ("sigma", _F), ("sigma_next", _F), ("eta", _F), ("sigma_prev", _F), ("have_prev", ctypes.c_int32),
+        ("x_model", _P), ("thr", _P),
+    ]
+
+
+def sampler_eval(**kw) -> int:
+    """One evaluation of the generation loop on the CPU (orc_sampler_eval).  Array arguments are
+    contiguous float32 numpy arrays (written in place where the step writes them), or None."""
+    a = SamplerArgs()
+    for name, _ in SamplerArgs._fields_:
+        if name not in kw or kw[name] is None:
+            continue
+        v = kw[name]
+        if name == "lms":
+            for j, arr in enumerate(v):
+                if arr is not None:
+                    assert arr.dtype == np.float32 and arr.flags.c_contiguous
+                    a.lms[j] = arr.ctypes.data
+        elif isinstance(v, np.ndarray):
+            assert v.dtype == np.float32 and v.flags.c_contiguous, name
+            setattr(a, name, v.ctypes.data)
+        else:
+            setattr(a, name, v)
+    return int(lib().orc_sampler_eval(ctypes.byref(a)))
+
+
+def sampler_run(kind: int, lat: np.ndarray, sigmas, model, noise=None, cfg=7.5, rescale=0.0, eta=0.0,
+                vpred=False, dynthresh=False, mask=None, init_lat=None):
+    """The generation loop's sampler on the CPU (sdvkgen.cpp:3796-4026): the same driving order as
+    sdvk_b200.sampler.DeviceSampler, each evaluation by orc_sampler_eval.  model(x_model, step,
+    phase, sigma) -> (eps_c, eps_u or None) as float32 arrays; noise(step) -> n float32 normals.
+    Returns (lat, x0 of the last evaluation)."""
+    f32 = np.float32
+    lat = np.array(lat, dtype=f32, copy=True)
+    n = lat.size
+    z = lambda: np.zeros(n, f32)
+    x0, x0b, x_tmp = z(), z(), z()
+    x0_prev = z()
+    lms = [z() for _ in range(4)]
+    lms_count, have_prev, sigma_prev = 0, False, 0.0
+    inv0 = f32(1.0) / np.sqrt(f32(sigmas[0]) * f32(sigmas[0]) + f32(1.0))
+    x_model = (lat * inv0).astype(f32)
+    two = kind in (2, 4, 5)
+    common = dict(n=n, cfg=cfg, rescale=rescale, vpred=int(vpred), dynthresh=int(dynthresh), mask=mask,
+                  mask_cells=0 if mask is None else mask.size, init_lat=init_lat, lat=lat, x_tmp=x_tmp,
+                  x0_prev=x0_prev, eta=eta, x_model=x_model)
+    last_x0 = x0
+    for i in range(len(sigmas) - 1):
+        sigma, sn = float(sigmas[i]), float(sigmas[i + 1])
+        last = sn <= 0.0
+        if kind == 3 and not last:
+            lms = [lms[-1]] + lms[:-1]
+            lms_count = min(lms_count + 1, 4)
+        ec, eu = model(x_model, i, 0, sigma)
+        nz = noise(i) if (not last and kind in (1, 7)) else None
+        bad = sampler_eval(kind=kind, phase=0, eps_c=ec, eps_u=eu, x0=x0, lms=lms, lms_count=lms_count, noise=nz,
+                           sigma=sigma, sigma_next=sn, sigma_prev=sigma_prev, have_prev=int(have_prev), **common)
+        if bad:
+            raise FloatingPointError(f"non-finite model output at step {i + 1}")
+        last_x0 = x0
+        if two and not last:
+            ec, eu = model(x_model, i, 1, sn)
+            nz = noise(i) if kind == 5 else None
+            bad = sampler_eval(kind=kind, phase=1, eps_c=ec, eps_u=eu, x0=x0b, x0v=x0, noise=nz, sigma=sigma,
+                               sigma_next=sn, **common)
+            if bad:
+                raise FloatingPointError(f"non-finite model output at step {i + 1}")
+            last_x0 = x0b
+        if kind in (6, 7) and not last:
+            have_prev, sigma_prev = True, sigma
+    return lat, last_x0.copy()
 
 
 def num_threads() -> int:

@@ -53,6 +53,27 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+class SamplerStepDesc(ctypes.Structure):
+    """sdvk_sampler_step_desc: one model evaluation's share of the generation loop."""
+
+    _fields_ = [
+        ("kind", ctypes.c_int32), ("phase", ctypes.c_int32), ("n", ctypes.c_uint64),
+        ("eps_c", ctypes.c_void_p), ("eps_u", ctypes.c_void_p), ("cfg", ctypes.c_float), ("rescale", ctypes.c_float),
+        ("vpred", ctypes.c_int32), ("dynthresh", ctypes.c_int32),
+        ("mask", ctypes.c_void_p), ("mask_cells", ctypes.c_uint64), ("init_lat", ctypes.c_void_p),
+        ("lat", ctypes.c_void_p), ("x_tmp", ctypes.c_void_p), ("x0", ctypes.c_void_p), ("x0v", ctypes.c_void_p),
+        ("x0_prev", ctypes.c_void_p), ("lms", ctypes.c_void_p * 4), ("lms_count", ctypes.c_int32),
+        ("noise", ctypes.c_void_p), ("sigma", ctypes.c_float), ("sigma_next", ctypes.c_float),
+        ("eta", ctypes.c_float), ("sigma_prev", ctypes.c_float), ("have_prev", ctypes.c_int32),
+        ("x_model", ctypes.c_void_p), ("thr", ctypes.c_void_p),
+    ]
+
+
+# Sampler kinds (SamplerKind, src/Modules/Diffusion/GenParams.hpp:16-26)
+SAMPLER_EULER, SAMPLER_EULER_A, SAMPLER_HEUN, SAMPLER_LMS, SAMPLER_DPM2, SAMPLER_DPM2_A = range(6)
+SAMPLER_DPMPP_2M, SAMPLER_DPMPP_2S_A, SAMPLER_DDIM = 6, 7, 8
+
+
 class Q8Linear(ctypes.Structure):
     """sdvk_q8_linear: int8 weight [N][K], fp32 scale per 32 weights, optional fp32 bias [N]."""
 
@@ -112,6 +133,8 @@ SIGNATURES = {
     "sdvk_attention": (_I, [_P, ctypes.POINTER(AttnDesc)]),
     "sdvk_check_finite": (_I, [_P, _P, _I, _U64]),
     "sdvk_cfg_combine": (_I, [_P, _P, _P, _P, _U64, ctypes.c_float, ctypes.c_float]),
+    "sdvk_sampler_step": (_I, [_P, ctypes.POINTER(SamplerStepDesc)]),
+    "sdvk_sampler_scale": (_I, [_P, _P, _P, _U64, ctypes.c_float]),
     "sdvk_q8_0_ingest": (_I, [_P, _P, _U64, _U64, _P, _U64, _P]),
     "sdvk_conv3x3_workspace": (_U64, [_U32, _U32, _U32, _I, _I]),
     "sdvk_conv3x3_q8": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _U32, _U32, _U32, _U32, _U32, _I, _I, _P, _U64]),
@@ -331,6 +354,14 @@ class Context:
                   silu: bool, workspace: int, workspace_bytes: int) -> None:
         self._check(lib().sdvk_groupnorm(self._h, x, gamma, beta, y, batch, C, P, G, eps, int(silu), workspace or None,
                                          workspace_bytes), "groupnorm")
+
+    def sampler_step(self, desc: SamplerStepDesc) -> None:
+        """sdvk_sampler_step: guidance, x0 and the sampler update of one model evaluation."""
+        self._check(lib().sdvk_sampler_step(self._h, ctypes.byref(desc)), "sampler_step")
+
+    def sampler_scale(self, x: int, out: int, n: int, sigma: float) -> None:
+        """out = x / sqrt(sigma^2 + 1), the first evaluation's model input."""
+        self._check(lib().sdvk_sampler_scale(self._h, x, out, n, sigma), "sampler_scale")
 
     def check_finite(self, ptr: int, dtype: int, n: int) -> bool:
         st = lib().sdvk_check_finite(self._h, ptr, dtype, n)

@@ -68,6 +68,9 @@ int comm_abort(sdvk_comm* c);
 int allgather(sdvk_comm* c, const void* send, void* recv, uint64_t count, int dtype, uint32_t timeout_ms,
               const LaunchEnv& env);
 int comm_wait(sdvk_comm* c, uint32_t timeout_ms, const LaunchEnv& env);
+uint64_t sampler_workspace(int num_sms);
+int sampler_step(const sdvk_sampler_step_desc& d, void* ws, uint64_t ws_bytes, const LaunchEnv& env);
+int sampler_scale(const float* x, float* out, uint64_t n, float sigma, const LaunchEnv& env);
 int check_finite(const void* x, int dtype, uint64_t n, uint32_t* flag_dev, const LaunchEnv& env);
 
 // ingest.cu: GGUF Q8_0 blocks -> (int8 payload, fp32 scales); GroupNorm (+SiLU).

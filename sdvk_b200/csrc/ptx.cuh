@@ -13,7 +13,8 @@ namespace sdvk {
 // Device-side error codes written to the kernel's error word (host maps them to SDVK_E_*).
 enum : uint32_t {
     kErrNone = 0,
-    kErrTimeout = 1,  // a bounded wait ran out (a pipeline partner never arrived)
+    kErrTimeout = 1,    // a bounded wait ran out (a pipeline partner never arrived)
+    kErrNotFinite = 2,  // the sampler step found a NaN/Inf model output
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -11,6 +11,7 @@
 #include <thread>
 
 #include "backend.hpp"
+#include "ptx.cuh"  // the device error codes
 
 struct sdvk_ctx {
     int device = 0;
@@ -28,6 +29,8 @@ struct sdvk_ctx {
     bool step_recorded = false;
     void* scratch = nullptr;  // workspace of name-dispatched kernels that need one (groupnorm)
     uint64_t scratch_bytes = 0;
+    void* samp_ws = nullptr;  // the sampler step's partial sums (a few KB, sized at creation)
+    uint64_t samp_ws_bytes = 0;
     std::string last_error;
     std::string device_name;
 };
@@ -87,8 +90,11 @@ int collect_device_error(sdvk_ctx* ctx) {
     if (e != cudaSuccess) return cuda_err(ctx, e, "reading device error word");
     if (err) {
         cudaMemset(ctx->err_dev, 0, sizeof(uint32_t));
-        return set_err(ctx, SDVK_E_TIMEOUT, "a kernel's bounded wait timed out (device error word " +
-                                                std::to_string(err) + ")");
+        if (err & sdvk::kErrTimeout)
+            return set_err(ctx, SDVK_E_TIMEOUT, "a kernel's bounded wait timed out (device error word " +
+                                                    std::to_string(err) + ")");
+        return set_err(ctx, SDVK_E_NOT_FINITE, "non-finite model output in a sampler step (device error word " +
+                                                   std::to_string(err) + ")");
     }
     return SDVK_OK;
 }
@@ -135,6 +141,10 @@ int sdvk_ctx_create(int device, sdvk_ctx** out) {
     if (!rc) rc = cuda_err(ctx, cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking), "side stream");
     if (!rc) rc = cuda_err(ctx, cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming), "event");
     if (!rc) rc = cuda_err(ctx, cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming), "event");
+    if (!rc) {
+        ctx->samp_ws_bytes = sdvk::sampler_workspace(prop.multiProcessorCount);
+        rc = cuda_err(ctx, cudaMalloc(&ctx->samp_ws, ctx->samp_ws_bytes), "cudaMalloc(sampler workspace)");
+    }
     if (rc) {
         sdvk_ctx_destroy(ctx);
         return rc;
@@ -157,6 +167,7 @@ int sdvk_ctx_destroy(sdvk_ctx* ctx) {
     if (ctx->join) cudaEventDestroy(ctx->join);
     if (ctx->side) cudaStreamDestroy(ctx->side);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
+    if (ctx->samp_ws) cudaFree(ctx->samp_ws);
     if (ctx->scratch) {
         cudaStreamSynchronize(ctx->stream);
         cudaFree(ctx->scratch);
@@ -423,6 +434,18 @@ int sdvk_fused_attention(sdvk_ctx* ctx, const void* q, const void* k, const void
     d.scale = 1.0f / std::sqrt((float)hd);
     d.causal = causal;
     return sdvk_attention(ctx, &d);
+}
+
+int sdvk_sampler_step(sdvk_ctx* ctx, const sdvk_sampler_step_desc* desc) {
+    if (!ctx || !desc) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::sampler_step(*desc, ctx->samp_ws, ctx->samp_ws_bytes, env_of(ctx));
+}
+
+int sdvk_sampler_scale(sdvk_ctx* ctx, const float* x, float* out, uint64_t n, float sigma) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::sampler_scale(x, out, n, sigma, env_of(ctx));
 }
 
 int sdvk_check_finite(sdvk_ctx* ctx, const void* x, int dtype, uint64_t n) {
