@@ -58,7 +58,8 @@ class CfgPair:
     def is_cond(self) -> bool:
         return self.rank == 0
 
-    def guided(self, eps_local: torch.Tensor) -> torch.Tensor:
+    def exchange(self, eps_local: torch.Tensor):
+        """All-gather this rank's prediction: (cond, uncond), flat, the same bytes on both ranks."""
         flat = eps_local.contiguous().view(-1)
         both = torch.empty(2 * flat.numel(), dtype=flat.dtype, device=flat.device)
         try:
@@ -66,4 +67,19 @@ class CfgPair:
         except Exception as e:  # partner raised, exited or timed out
             raise PairFailure(f"guidance exchange failed on pair rank {self.rank}: {e}") from e
         cond, uncond = both.view(2, -1)
+        return cond, uncond
+
+    def guided(self, eps_local: torch.Tensor) -> torch.Tensor:
+        cond, uncond = self.exchange(eps_local)
         return self.combine(cond, uncond, self.cfg, self.rescale).view(eps_local.shape)
+
+    def sampler_model(self, unet: Callable[[torch.Tensor, int, int, float], torch.Tensor]):
+        """A model callback for sdvk_b200.sampler.DeviceSampler: this rank evaluates its own pass with
+        unet(x_model, step, phase, sigma), the pair exchanges the two predictions, and each rank's
+        sampler step (sdvk_sampler_step, guidance combine included) runs on the same bytes, so the
+        latents stay bit-identical (sdvkgen.cpp:3806-3846 with the two passes on two GPUs)."""
+
+        def model(x_model, step, phase, sigma):
+            return self.exchange(unet(x_model, step, phase, sigma))
+
+        return model

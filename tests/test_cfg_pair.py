@@ -106,6 +106,71 @@ def test_cfg_pair_partner_failure_is_reported_not_hung():
     assert dt < 90
 
 
+SIGMAS = [10.0, 4.0, 1.5, 0.5, 0.1, 0.0]
+
+
+def _unet(x: np.ndarray, cond: bool, step: int, phase: int) -> np.ndarray:
+    return np.tanh(x * np.float32(1.3 if cond else 0.7) + np.float32(0.01 * step + 0.003 * phase)).astype(np.float32)
+
+
+def _pair_sampler_worker(rank, port, kind, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch
+    import torch.distributed as dist
+
+    from oracle import pyoracle
+    from sdvk_b200.cfg import CfgPair
+
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=10))
+    try:
+        pair = CfgPair(None, cfg=6.0)
+        unet = lambda x, step, phase, sigma: torch.from_numpy(_unet(x.numpy(), pair.is_cond, step, phase))
+        model_t = pair.sampler_model(unet)
+
+        def model(x, step, phase, sigma):  # numpy in and out, for the oracle's loop
+            c, u = model_t(torch.from_numpy(x), step, phase, sigma)
+            return np.ascontiguousarray(c.numpy()), np.ascontiguousarray(u.numpy())
+
+        lat0 = np.linspace(-3, 3, 4 * 16 * 16, dtype=np.float32)
+        lat, _ = pyoracle.sampler_run(kind, lat0, SIGMAS, model, cfg=6.0)
+        q.put((rank, "ok", lat))
+    except Exception as e:
+        q.put((rank, "raised", repr(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+@pytest.mark.parametrize("kind", [0, 2, 6])  # Euler, Heun (two evaluations a step), DPM++ 2M
+def test_cfg_pair_drives_the_sampler_loop(kind):
+    """CfgPair.sampler_model as the sampler's model: each rank evaluates one pass, the pair exchanges,
+    and both ranks' sampler loops (the oracle's restatement here) end bit-identical and equal to the
+    one-process loop that evaluates both passes."""
+    from oracle import pyoracle
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pair_sampler_worker, args=(r, port, kind, q)) for r in (0, 1)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r = q.get(timeout=120)
+        res[r[0]] = r[1:]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[0][0] == "ok" and res[1][0] == "ok", res
+    one = lambda x, step, phase, sigma: (_unet(x, True, step, phase), _unet(x, False, step, phase))
+    want, _ = pyoracle.sampler_run(kind, np.linspace(-3, 3, 4 * 16 * 16, dtype=np.float32), SIGMAS, one, cfg=6.0)
+    assert np.array_equal(res[0][1], res[1][1])
+    assert np.array_equal(res[0][1], want)
+
+
 def test_cfg_combine_restatement():
     from oracle import pyoracle
 
