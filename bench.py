@@ -643,6 +643,128 @@ class SamplerWorkload:
         return evals * self.bytes
 
 
+class UnetWorkload:
+    """one denoising step of an SDXL 1024^2 CFG generation -- the whole UNet pass
+    over the cond/uncond pair (batch 2, 4 x 128 x 128 latent, sdvk_unet_forward: unetForward,
+    sdvkgen.cpp:1875-1973) followed by the device sampler step (guidance, v-prediction x0, the Euler
+    update and the next scaled model input, sdvk_sampler_step).  A generation is 20 such steps, so the
+    metric is images/s = 1 / (20 x s/step) per GPU; GPUs run independent images (weak scaling)."""
+
+    name = "unet"
+    unit = "images/s"
+    dtype = "f16"
+    bound = "tensor"
+    steps_per_image = 20
+    graph_len = 1
+    default_steps = 10
+    cfg = 5.0
+
+    def __init__(self, B=2, H=128, W=128):
+        self.B, self.H, self.W = B, H, W
+        self.n = 4 * H * W
+        self.unet = None
+        self.flop = None  # set once the UNet exists (sdvk_unet_flops)
+        self.work = 1.0 / self.steps_per_image  # images per step
+        self.metric = "SDXL 1024^2 CFG UNet images/s (20 Euler steps, v-pred, cfg 5.0)"
+        self.describe = ("SDXL UNet (320/640/1280, depths 0/2/10, hd 64, ctx 2048, adm 2816, GN 32) with random "
+                         "Q8_0 weights (int8 U[-127,127], scale |N(0,0.02)|/127), batch 2 (cond/uncond) latent "
+                         "4x128x128 fp32 ~N(0,1), context 2x77x2048 fp16 ~N(0,1), adm N(0,1); one step = UNet pass "
+                         "+ sdvk_sampler_step (Euler, cfg 5.0, v-pred)")
+        self.rotate = 1
+        self.l2_note = "one UNet pass moves ~3 GB of Q8_0 weights and several GB of activations per step (>> 126 MB L2)"
+        self.cpu_units = 9216
+        self.cpu_what = ("rows of the 9216x1280x1280 Q8_0 GEMM (fp32 restatement of gemm_nt_q8_v.comp, the pass's "
+                         "dominant arithmetic), converted to images/s at the pass's FLOP per image")
+        self.bytes = 0
+
+    def _ensure(self, torch, device):
+        if self.unet is None:
+            from sdvk_b200.unet import Unet
+
+            self.unet = Unet(self.B, self.H, self.W, device=device.index)
+            self.unet.init_random(3)
+            self.flop = float(self.unet.flops)
+            self.launches_per_step = self.unet.launches + 2  # + the sampler's guide and update passes
+            # weights once per pass plus the activations' fp32 writes and reads (order of magnitude)
+            self.bytes = 3.0e9
+
+    def make_set(self, torch, device, seed):
+        self._ensure(torch, device)
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        B, n = self.B, self.n
+        lat = torch.randn((n,), generator=g, device=device) * 14.6
+        xin = torch.empty((B, 4, self.H, self.W), device=device)
+        xin[:] = (lat / math.sqrt(14.6 ** 2 + 1)).view(1, 4, self.H, self.W)
+        ts = torch.full((B,), 999.0, device=device)
+        adm = torch.randn((B, 2816), generator=g, device=device)
+        ctx = torch.randn((B, 77, 2048), generator=g, device=device).half()
+        out = torch.empty_like(xin)
+        x0 = torch.empty((n,), device=device)
+        return lat, xin, ts, adm, ctx, out, x0
+
+    def _desc(self, sdvk_b200, st):
+        lat, xin, ts, adm, ctx, out, x0 = st
+        n = self.n
+        d = sdvk_b200.SamplerStepDesc()
+        d.kind, d.phase, d.n = sdvk_b200.SAMPLER_EULER, 0, n
+        d.eps_c, d.eps_u, d.cfg, d.vpred = out.data_ptr(), out.data_ptr() + 4 * n, self.cfg, 1
+        d.lat, d.x0, d.x_model = lat.data_ptr(), x0.data_ptr(), xin.data_ptr()
+        d.sigma, d.sigma_next = 14.6, 12.0
+        return d
+
+    def _run(self, ctx, st, d):
+        lat, xin, ts, adm, cx, out, x0 = st
+        ctx._check(sdvk_b200_lib().sdvk_unet_forward(ctx.handle, self.unet._h, xin.data_ptr(), ts.data_ptr(),
+                                                     adm.data_ptr(), cx.data_ptr(), 1, out.data_ptr()),
+                   "sdvk_unet_forward")
+        ctx.sampler_step(d)
+        ctx.copy(xin.data_ptr() + 4 * self.n, xin.data_ptr(), 4 * self.n)  # the uncond half's input
+
+    def step(self, torch_ops, st):
+        import sdvk_b200
+
+        self._run(torch_ops.context(st[0].device), st, self._desc(sdvk_b200, st))
+
+    def e2e(self, sdvk_b200, ctx, torch, st):
+        """Per step: pinned latent -> device, the UNet pass and the sampler step, the updated latent ->
+        pinned host."""
+        lat = st[0]
+        lh = torch.empty(lat.shape, dtype=lat.dtype, pin_memory=True)
+        lh.copy_(lat.cpu())
+        d = self._desc(sdvk_b200, st)
+        nb = self.n * 4
+
+        def run():
+            ctx.upload_async(lat.data_ptr(), lh.data_ptr(), nb)
+            self._run(ctx, st, d)
+            ctx.download_async(lh.data_ptr(), lat.data_ptr(), nb)
+
+        return run, nb, nb, "sdvk_upload_async + sdvk_unet_forward + sdvk_sampler_step + sdvk_download_async"
+
+    def host_inputs(self):
+        return GemmWorkload().host_inputs()
+
+    def cpu_run(self, inputs, rows):
+        return GemmWorkload().cpu_run(inputs, rows)
+
+    def cpu_value(self, flop_per_s):
+        """images/s at the CPU restatement's FLOP rate (FLOP per image = 20 passes of the batch-2 pass)."""
+        flop = self.flop if self.flop else UNET_PASS_FLOP
+        return flop_per_s / (flop * self.steps_per_image)
+
+
+# FLOP of the batch-2 SDXL 1024^2 pass as sdvk_unet_flops counts it (for the reference arm, which
+# builds no UNet); bench runs of the sdvk arm print the live count in config.
+UNET_PASS_FLOP = 13.0e12
+
+
+def sdvk_b200_lib():
+    import sdvk_b200
+
+    return sdvk_b200.lib()
+
+
 def wl_unit(wl):
     return getattr(wl, "unit", "TFLOP/s")
 
@@ -653,7 +775,13 @@ def wl_work(wl):
 
 
 def wl_scale(wl):
-    return 1e12 if wl_unit(wl) == "TFLOP/s" else 1e9
+    return {"TFLOP/s": 1e12, "GB/s": 1e9}.get(wl_unit(wl), 1.0)
+
+
+def wl_cpu_value(wl, flop_per_s):
+    """A CPU sample's rate in the workload's unit."""
+    conv = getattr(wl, "cpu_value", None)
+    return conv(flop_per_s) if conv else flop_per_s / wl_scale(wl)
 
 
 WORKLOADS = {
@@ -662,6 +790,7 @@ WORKLOADS = {
     "conv": ConvWorkload,
     "sampler": SamplerWorkload,
     "block": BlockWorkload,
+    "unet": UnetWorkload,
     "attn-self-4096": lambda: AttnWorkload("attn-self-4096", 2, 4096, 4096, 10),
     "attn-self-1024": lambda: AttnWorkload("attn-self-1024", 2, 1024, 1024, 20),
     "attn-cross-77": lambda: AttnWorkload("attn-cross-77", 2, 1024, 77, 20),
@@ -700,7 +829,7 @@ def run_reference(args, rank, world, wl):
         return 0
     budget = 60.0
     fps, units, _, dt, threads = cpu_sample(wl, budget, steps=args.steps)
-    value = fps / wl_scale(wl)
+    value = wl_cpu_value(wl, fps)
     sample = f"{units} of {wl.cpu_units} {wl.cpu_what} per step"
     line = {
         "impl": "reference", "metric": wl.metric, "value": value, "unit": wl_unit(wl), "n_gpus": world,
@@ -728,7 +857,8 @@ def main(argv=None):
     args.warmup = max(3, args.warmup)
     wl = WORKLOADS[args.workload]()
     if args.steps is None:
-        args.steps = 3 if args.impl == "reference" else 20000 if wl.flop < 5e10 else 5000
+        args.steps = 3 if args.impl == "reference" else getattr(wl, "default_steps", None) or (
+            20000 if wl.flop < 5e10 else 5000)
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -771,9 +901,10 @@ def main(argv=None):
             graphs[n] = g
         return graphs[n]
 
-    full, rem = divmod(args.steps, GRAPH_LEN)
+    glen = getattr(wl, "graph_len", GRAPH_LEN)
+    full, rem = divmod(args.steps, glen)
     if full:
-        graph_of(GRAPH_LEN).replay()
+        graph_of(glen).replay()
     if rem:
         graph_of(rem).replay()
     torch.cuda.synchronize()
@@ -787,7 +918,7 @@ def main(argv=None):
         stream = torch.cuda.current_stream(device)
         ev0.record(stream)
         for _ in range(full):
-            graph_of(GRAPH_LEN).replay()
+            graph_of(glen).replay()
         if rem:
             graph_of(rem).replay()
         ev1.record(stream)
@@ -828,7 +959,7 @@ def main(argv=None):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         fps, units, runs, secs, threads = cpu_sample(wl, budget_s=15.0)
-        cpu = {"value": fps / wl_scale(wl), "unit": wl_unit(wl), "cores": threads, "kind": "port",
+        cpu = {"value": wl_cpu_value(wl, fps), "unit": wl_unit(wl), "cores": threads, "kind": "port",
                "sample": f"{runs} x {units} of {wl.cpu_units} {wl.cpu_what}, {secs:.1f} s"}
 
     pk, pk_kind = peaks()
@@ -850,7 +981,7 @@ def main(argv=None):
             "config": {"workload": wl.describe, "parallelism": f"replicas x{world}",
                        "l2": getattr(wl, "l2_note", None) or
                        f"{wl.rotate} rotating input/output sets ({wl.rotate * wl.bytes / 1e6:.0f} MB > 126 MB L2)",
-                       "timing": f"CUDA events over CUDA-graph replays of {GRAPH_LEN} launches"},
+                       "timing": f"CUDA events over CUDA-graph replays of {glen} step(s)"},
             "roofline": roof,
             "e2e": {"value": e2e_value, "unit": wl_unit(wl), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "path": path + ", pinned host buffers"},

@@ -368,6 +368,55 @@ SDVK_API int sdvk_comm_wait(sdvk_ctx* ctx, sdvk_comm* comm, uint32_t timeout_ms)
  * sdvkgen.cpp:3819-3823): returns SDVK_E_NOT_FINITE if any value is not finite. */
 SDVK_API int sdvk_check_finite(sdvk_ctx* ctx, const void* x, int dtype, uint64_t n);
 
+/* ---- the whole SDXL UNet pass ------------------------------------------------------------- */
+/* unetForward (src/Modules/Diffusion/sdvkgen.cpp:1875-1973) with resBlock (:1669-1707),
+ * spatialTransformer (:1722-1777), concatCh (:1791-1796) and buildTemb (:1982-1995), over `batch`
+ * images in one pass (the reference runs the CFG halves as two batch-1 passes).  The UNet owns its
+ * parameters (one device arena, each tensor under the reference checkpoint's LDM name, e.g.
+ * "input_blocks.4.1.transformer_blocks.0.attn1.to_q.weight"; conv weights are [cout][cin*9]) and a
+ * workspace sized at creation for the given batch and latent size.
+ *   x:         fp32 [batch][4][H][W] latent (the scaled model input)
+ *   timesteps: fp32 [batch] (the sinusoidal embedding of timeEmbHost is computed on the device)
+ *   adm:       fp32 [batch][adm_dim] (pooled text embedding + size conditioning, as buildTemb concatenates)
+ *   context:   [batch][Tctx][ctx_dim] in ctx_dtype (F16, BF16 or F32)
+ *   out:       fp32 [batch][4][H][W]
+ * SDXL: model_ch {320, 640, 1280}, depth {0, 2, 10}, ctx_dim 2048, adm_dim 2816, temb_dim 1280,
+ * head_dim 64, Tctx 77.  H and W must be multiples of 4.  The latent's 4 input channels run as 32
+ * (zero-padded): "input_blocks.0.0.weight" is [ch0][32*9] and its columns past 4*9 must stay zero.
+ * After parameters change, sdvk_unet_prepare redoes the load-time repacks (GEGLU interleave). */
+typedef struct sdvk_unet sdvk_unet;
+typedef struct sdvk_unet_desc {
+    uint32_t model_ch[3];
+    uint32_t depth[3];
+    uint32_t ctx_dim, adm_dim, temb_dim, head_dim, Tctx;
+    uint32_t batch, H, W;
+} sdvk_unet_desc;
+#define SDVK_UNET_Q8 0  /* int8 [rows][cols] + fp32 scale per 32 */
+#define SDVK_UNET_F32 1 /* fp32 [rows] */
+typedef struct sdvk_unet_tensor_info {
+    const char* name; /* names in parentheses are internal groups and repacks */
+    int kind;
+    uint32_t rows, cols;
+    int8_t* q;
+    float* s;
+    float* f;
+} sdvk_unet_tensor_info;
+SDVK_API int sdvk_unet_create(sdvk_ctx* ctx, const sdvk_unet_desc* desc, sdvk_unet** out);
+SDVK_API int sdvk_unet_destroy(sdvk_unet* unet);
+/* Seeded random parameters: Q8_0 weights int8 uniform in [-127, 127] with binary16 scales
+ * |N(0, 0.02)|/127, linear and conv biases uniform in [-0.02, 0.02], norm weights 1 and biases 0. */
+SDVK_API int sdvk_unet_init_random(sdvk_ctx* ctx, sdvk_unet* unet, uint64_t seed);
+SDVK_API int sdvk_unet_prepare(sdvk_ctx* ctx, sdvk_unet* unet);
+SDVK_API uint32_t sdvk_unet_tensor_count(const sdvk_unet* unet);
+SDVK_API int sdvk_unet_tensor(const sdvk_unet* unet, uint32_t index, sdvk_unet_tensor_info* out);
+/* Algorithmic FLOP of one pass (GEMMs, convolutions at their real input channels, attention). */
+SDVK_API uint64_t sdvk_unet_flops(const sdvk_unet* unet);
+SDVK_API uint64_t sdvk_unet_workspace_bytes(const sdvk_unet* unet);
+/* Kernel launches of one pass (this library's kernels; the concat copies are not counted). */
+SDVK_API uint64_t sdvk_unet_launches(const sdvk_unet* unet);
+SDVK_API int sdvk_unet_forward(sdvk_ctx* ctx, sdvk_unet* unet, const float* x, const float* timesteps, const float* adm,
+                               const void* context, int ctx_dtype, float* out);
+
 #ifdef __cplusplus
 }
 #endif

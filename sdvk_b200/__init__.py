@@ -97,6 +97,28 @@ class BlockDesc(ctypes.Structure):
     ]
 
 
+class UnetDesc(ctypes.Structure):
+    """sdvk_unet_desc: the SDXL UNet's architecture and the pass's batch and latent size."""
+
+    _fields_ = [
+        ("model_ch", ctypes.c_uint32 * 3), ("depth", ctypes.c_uint32 * 3),
+        ("ctx_dim", ctypes.c_uint32), ("adm_dim", ctypes.c_uint32), ("temb_dim", ctypes.c_uint32),
+        ("head_dim", ctypes.c_uint32), ("Tctx", ctypes.c_uint32),
+        ("batch", ctypes.c_uint32), ("H", ctypes.c_uint32), ("W", ctypes.c_uint32),
+    ]
+
+
+class UnetTensorInfo(ctypes.Structure):
+    """sdvk_unet_tensor_info: one named parameter of the UNet's arena."""
+
+    _fields_ = [
+        ("name", ctypes.c_char_p), ("kind", ctypes.c_int), ("rows", ctypes.c_uint32), ("cols", ctypes.c_uint32),
+        ("q", ctypes.c_void_p), ("s", ctypes.c_void_p), ("f", ctypes.c_void_p),
+    ]
+
+
+UNET_Q8, UNET_F32 = 0, 1
+
 # name -> (restype, argtypes) for every symbol include/sdvk_cuda.h declares
 _P, _U32, _U64, _I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
 SIGNATURES = {
@@ -153,6 +175,16 @@ SIGNATURES = {
     "sdvk_transformer_block_workspace": (_U64, [ctypes.POINTER(BlockDesc)]),
     "sdvk_transformer_block": (_I, [_P, ctypes.POINTER(BlockDesc), _P, _U64]),
     "sdvk_transformer_block_static": (_I, [_P, ctypes.POINTER(BlockDesc)]),
+    "sdvk_unet_create": (_I, [_P, ctypes.POINTER(UnetDesc), ctypes.POINTER(_P)]),
+    "sdvk_unet_destroy": (_I, [_P]),
+    "sdvk_unet_init_random": (_I, [_P, _P, _U64]),
+    "sdvk_unet_prepare": (_I, [_P, _P]),
+    "sdvk_unet_tensor_count": (_U32, [_P]),
+    "sdvk_unet_tensor": (_I, [_P, _U32, ctypes.POINTER(UnetTensorInfo)]),
+    "sdvk_unet_flops": (_U64, [_P]),
+    "sdvk_unet_workspace_bytes": (_U64, [_P]),
+    "sdvk_unet_launches": (_U64, [_P]),
+    "sdvk_unet_forward": (_I, [_P, _P, _P, _P, _P, _P, _I, _P]),
 }
 
 

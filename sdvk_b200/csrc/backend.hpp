@@ -82,8 +82,30 @@ uint64_t conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, uint32_t stride
 int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, void* y, int y_dtype,
                uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W, uint32_t stride, int off,
                void* workspace, uint64_t ws_bytes, const LaunchEnv& env);
+// The same convolution with image b's bias at bias + b * bias_stride (the UNet's conv bias plus that
+// image's time-embedding projection) and, with accumulate, y += conv(x) (F32 y: the residual add).
+int conv3x3_q8_ex(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, uint64_t bias_stride,
+                  bool accumulate, void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H,
+                  uint32_t W, uint32_t stride, int off, void* workspace, uint64_t ws_bytes, const LaunchEnv& env);
 int groupnorm(const float* x, const float* gamma, const float* beta, float* y, uint32_t batch, uint32_t C, uint32_t P,
               uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes, const LaunchEnv& env);
+// The same GroupNorm with y in F32 or F16 (the UNet feeds the F16 form to its convolutions).
+int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y, int y_dtype, uint32_t batch,
+                 uint32_t C, uint32_t P, uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes,
+                 const LaunchEnv& env);
+
+// unet.cu: the SDXL UNet pass over the kernels above.
+int unet_create(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env);
+int unet_destroy(sdvk_unet* u);
+int unet_init_random(sdvk_unet* u, uint64_t seed, const LaunchEnv& env);
+int unet_prepare(sdvk_unet* u, const LaunchEnv& env);
+int unet_forward(sdvk_unet* u, const float* x, const float* timesteps, const float* adm, const void* ctx, int ctx_dtype,
+                 float* out, const LaunchEnv& env);
+uint64_t unet_flops(const sdvk_unet* u);
+uint64_t unet_launches(const sdvk_unet* u);
+uint64_t unet_workspace_bytes(const sdvk_unet* u);
+int unet_tensor(const sdvk_unet* u, uint32_t i, sdvk_unet_tensor_info* out);
+uint32_t unet_tensor_count(const sdvk_unet* u);
 
 inline int dtype_size(int dt) { return dt == SDVK_F32 ? 4 : (dt == SDVK_F16 || dt == SDVK_BF16) ? 2 : 0; }
 

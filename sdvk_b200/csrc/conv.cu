@@ -67,7 +67,15 @@ uint64_t conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, uint32_t stride
 int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, void* y, int y_dtype,
                uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W, uint32_t stride, int off,
                void* workspace, uint64_t ws_bytes, const LaunchEnv& env) {
+    return conv3x3_q8_ex(x, x_dtype, q, s, bias, 0, false, y, y_dtype, batch, cin, cout, H, W, stride, off, workspace,
+                         ws_bytes, env);
+}
+
+int conv3x3_q8_ex(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, uint64_t bias_stride,
+                  bool accumulate, void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H,
+                  uint32_t W, uint32_t stride, int off, void* workspace, uint64_t ws_bytes, const LaunchEnv& env) {
     if (!x || !q || !s || !y) return fail(env, SDVK_E_ARG, "null pointer");
+    if (accumulate && y_dtype != SDVK_F32) return fail(env, SDVK_E_ARG, "an accumulating conv needs an F32 output");
     if (x_dtype != SDVK_F16 && x_dtype != SDVK_BF16 && x_dtype != SDVK_F32)
         return fail(env, SDVK_E_ARG, "conv input must be F16, BF16 or F32");
     if (y_dtype != SDVK_F16 && y_dtype != SDVK_F32) return fail(env, SDVK_E_ARG, "conv output must be F16 or F32");
@@ -118,7 +126,8 @@ int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, cons
             d.wq = q;
             d.ws = s;
             d.ldw = K;
-            d.bias = bias;
+            d.bias = bias ? bias + (uint64_t)bi * bias_stride : nullptr;
+            d.accumulate = accumulate;
             d.c = yb + (uint64_t)r0 * OW * dtype_size(y_dtype);
             d.c_dtype = y_dtype;
             d.ldc = P;

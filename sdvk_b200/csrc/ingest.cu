@@ -144,8 +144,9 @@ __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const float* __res
 // (Chan et al.'s pairwise update of count, mean and M2, in a fixed order) into (mean,
 // 1/sqrt(var + eps)), then the CTA writes y = (x - mean) * rstd * gamma[c] + beta[c] (+ SiLU
 // v / (1 + e^-v)).
+template <class TY>
 __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
-                                                              const float* __restrict__ beta, float* __restrict__ y,
+                                                              const float* __restrict__ beta, TY* __restrict__ y,
                                                               uint32_t C, uint32_t P, uint32_t G, float eps,
                                                               uint32_t act, const GnStat* __restrict__ stats,
                                                               uint32_t chunks, bool vec) {
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(const float* __res
     const float mean = norm.x, sc = norm.y * gamma[c], sh = beta[c];
     const uint64_t off = ((uint64_t)b * C + c) * P;
     const float* xr = x + off;
-    float* yr = y + off;
+    TY* yr = y + off;
     // SiLU with the fast exponential and a correctly rounded reciprocal (a few ulp, against a full
     // division and expf that made the apply pass issue-bound rather than HBM-bound)
     auto f = [&](float v) {
@@ -196,10 +197,16 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(const float* __res
 #pragma unroll 4
         for (uint32_t i = 4 * threadIdx.x; i < P; i += 4 * kGnThreads) {
             const float4 v = __ldcs(reinterpret_cast<const float4*>(xr + i));  // last use of x
-            *reinterpret_cast<float4*>(yr + i) = make_float4(f(v.x), f(v.y), f(v.z), f(v.w));
+            if constexpr (sizeof(TY) == 4) {
+                *reinterpret_cast<float4*>(yr + i) = make_float4(f(v.x), f(v.y), f(v.z), f(v.w));
+            } else {
+                const __half2 lo = __floats2half2_rn(f(v.x), f(v.y)), hi = __floats2half2_rn(f(v.z), f(v.w));
+                *reinterpret_cast<uint2*>(yr + i) = make_uint2(*reinterpret_cast<const uint32_t*>(&lo),
+                                                               *reinterpret_cast<const uint32_t*>(&hi));
+            }
         }
     } else {
-        for (uint32_t i = threadIdx.x; i < P; i += kGnThreads) yr[i] = f(xr[i]);
+        for (uint32_t i = threadIdx.x; i < P; i += kGnThreads) yr[i] = TY(f(xr[i]));
     }
 }
 
@@ -231,7 +238,14 @@ uint64_t groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G)
 
 int groupnorm(const float* x, const float* gamma, const float* beta, float* y, uint32_t batch, uint32_t C, uint32_t P,
               uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes, const LaunchEnv& env) {
+    return groupnorm_ex(x, gamma, beta, y, SDVK_F32, batch, C, P, G, eps, act, workspace, ws_bytes, env);
+}
+
+int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y, int y_dtype, uint32_t batch,
+                 uint32_t C, uint32_t P, uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes,
+                 const LaunchEnv& env) {
     if (!x || !gamma || !beta || !y) return fail(env, SDVK_E_ARG, "null pointer");
+    if (y_dtype != SDVK_F32 && y_dtype != SDVK_F16) return fail(env, SDVK_E_ARG, "GroupNorm output must be F32 or F16");
     if (batch == 0 || C == 0 || P == 0) return SDVK_OK;
     if (G == 0 || C % G || G > 65535 || batch > 65535)
         return fail(env, SDVK_E_SHAPE, "GroupNorm needs C % G == 0 and at most 65535 groups and images");
@@ -246,8 +260,12 @@ int groupnorm(const float* x, const float* gamma, const float* beta, float* y, u
     if (int rc = launch_pdl(gn_stats_kernel, dim3(chunks, G, batch), dim3(kGnThreads), 0, env, "gn_stats_kernel launch",
                             x, C, P, G, vec, st))
         return rc;
-    return launch_pdl(gn_apply_kernel, dim3(C, batch), dim3(kGnThreads), 0, env, "gn_apply_kernel launch", x, gamma,
-                      beta, y, C, P, G, eps, act, (const GnStat*)st, chunks, vec);
+    if (y_dtype == SDVK_F16)
+        return launch_pdl(gn_apply_kernel<__half>, dim3(C, batch), dim3(kGnThreads), 0, env, "gn_apply_kernel launch",
+                          x, gamma, beta, static_cast<__half*>(y), C, P, G, eps, act, (const GnStat*)st, chunks,
+                          vec && (reinterpret_cast<uintptr_t>(y) & 7u) == 0);
+    return launch_pdl(gn_apply_kernel<float>, dim3(C, batch), dim3(kGnThreads), 0, env, "gn_apply_kernel launch", x,
+                      gamma, beta, static_cast<float*>(y), C, P, G, eps, act, (const GnStat*)st, chunks, vec);
 }
 
 }  // namespace sdvk

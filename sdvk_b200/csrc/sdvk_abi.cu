@@ -721,3 +721,43 @@ int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint3
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ the SDXL UNet pass
+int sdvk_unet_create(sdvk_ctx* ctx, const sdvk_unet_desc* desc, sdvk_unet** out) {
+    if (!ctx || !desc || !out) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::unet_create(*desc, out, env_of(ctx));
+}
+
+int sdvk_unet_destroy(sdvk_unet* unet) { return sdvk::unet_destroy(unet); }
+
+int sdvk_unet_init_random(sdvk_ctx* ctx, sdvk_unet* unet, uint64_t seed) {
+    if (!ctx || !unet) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::unet_init_random(unet, seed, env_of(ctx));
+}
+
+int sdvk_unet_prepare(sdvk_ctx* ctx, sdvk_unet* unet) {
+    if (!ctx || !unet) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::unet_prepare(unet, env_of(ctx));
+}
+
+uint32_t sdvk_unet_tensor_count(const sdvk_unet* unet) { return sdvk::unet_tensor_count(unet); }
+
+int sdvk_unet_tensor(const sdvk_unet* unet, uint32_t index, sdvk_unet_tensor_info* out) {
+    return sdvk::unet_tensor(unet, index, out);
+}
+
+uint64_t sdvk_unet_flops(const sdvk_unet* unet) { return sdvk::unet_flops(unet); }
+
+uint64_t sdvk_unet_workspace_bytes(const sdvk_unet* unet) { return sdvk::unet_workspace_bytes(unet); }
+
+uint64_t sdvk_unet_launches(const sdvk_unet* unet) { return sdvk::unet_launches(unet); }
+
+int sdvk_unet_forward(sdvk_ctx* ctx, sdvk_unet* unet, const float* x, const float* timesteps, const float* adm,
+                      const void* context, int ctx_dtype, float* out) {
+    if (!ctx || !unet) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::unet_forward(unet, x, timesteps, adm, context, ctx_dtype, out, env_of(ctx));
+}

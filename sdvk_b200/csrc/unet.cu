@@ -1,0 +1,849 @@
+// unet.cu -- the SDXL UNet denoiser pass (unetForward, src/Modules/Diffusion/sdvkgen.cpp:1875-1973;
+// resBlock :1669-1707, spatialTransformer :1722-1777, concatCh :1791-1796, buildTemb :1982-1995,
+// timeEmbHost :1779-1789) composed from the back end's kernels, for a batch of images at once (the
+// reference runs the CFG halves as two batch-1 passes).
+//
+// Activations between modules are fp32 channel-major [B][C][H][W], as in the reference.  Per module:
+//   ResBlock     h = conv1(GN+SiLU(x)) + (b1 + emb_proj[b]);  out = skip(x) + conv2(GN+SiLU(h))
+//                GN writes fp16, the convolutions are im2col + the Q8_0 NN GEMM; the per-image bias of
+//                conv1 is one accumulating GEMM for every ResBlock of the pass (all emb_layers weights
+//                lie back to back), and conv2 reduce-adds into the skip path's output.
+//   Transformer  g = GN(x) (fp16) -> tokens-major -> t = proj_in(g) (fp32 [B*P][C]) -> N blocks in place
+//                -> fp16 channel-major -> x += proj_out(.) (an accumulating NN GEMM)
+//   Down / up    stride-2 conv; nearest 2x upsample fused into the fp32 -> fp16 conversion, then conv
+//   conv_in      the 4 latent channels are zero-padded to 32 (cin*9 must hold whole Q8_0 blocks); the
+//                weight's padded columns are zero, so the result is the 4-channel convolution.
+// Parameters live in one device arena under the reference checkpoint's names (LDM keys), so a loader
+// can fill them by name (sdvk_unet_tensor); sdvk_unet_init_random fills them with seeded random Q8_0
+// weights instead.  Every intermediate sits at an address fixed when the UNet is created (a dry run
+// of the pass sizes the workspace), so a captured pass replays.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "backend.hpp"
+#include "ptx.cuh"
+
+namespace sdvk {
+namespace {
+
+constexpr uint32_t kGroups = 32;  // GroupNorm groups throughout the SDXL UNet
+constexpr uint32_t kInCh = 4, kInPad = 32, kOutCh = 4;
+
+uint64_t a256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+// ---------------------------------------------------------------- glue kernels
+
+// diffusers get_timestep_embedding with flip_sin_to_cos (timeEmbHost, sdvkgen.cpp:1779-1789):
+// e[i] = cos(t f_i), e[half + i] = sin(t f_i), f_i = exp(-ln(10000) i / half).
+__global__ void temb_sin_kernel(const float* __restrict__ t, float* __restrict__ out, uint32_t B, uint32_t dim) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const uint32_t half = dim / 2;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < B * half; i += gridDim.x * blockDim.x) {
+        const uint32_t b = i / half, j = i - b * half;
+        const float f = expf(-logf(10000.0f) * (float)j / (float)half);
+        out[(uint64_t)b * dim + j] = cosf(t[b] * f);
+        out[(uint64_t)b * dim + half + j] = sinf(t[b] * f);
+    }
+}
+
+// y = x / (1 + e^-x) (unary_fwd.comp mode 2)
+__global__ void silu_kernel(const float* __restrict__ x, float* __restrict__ y, uint64_t n) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        y[i] = v / (1.0f + expf(-v));
+    }
+}
+
+// out[b][j] = a[j] + c[j]: the per-image starting value of every ResBlock's conv1 bias (emb_layers.1
+// bias + in_layers.2 bias) before the accumulating emb GEMM adds silu(temb) W_emb^T.
+__global__ void bias_pair_kernel(const float* __restrict__ a, const float* __restrict__ c, float* __restrict__ out,
+                                 uint32_t n, uint32_t B) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n * B; i += gridDim.x * blockDim.x) {
+        const uint32_t j = i % n;
+        out[i] = a[j] + c[j];
+    }
+}
+
+// y[b][c][oh][ow] = c < Cin ? x[b][c][oh >> up][ow >> up] : 0, fp32 -> fp16: the nearest 2x upsample
+// (up2, sdvkgen.cpp:1191-1197) or a plain conversion (up = 0), with zero channels appended up to Cout.
+__global__ void to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, uint32_t B, uint32_t Cin,
+                              uint32_t Cout, uint32_t H, uint32_t W, uint32_t up) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const uint32_t OH = H << up, OW = W << up;
+    const uint64_t n = (uint64_t)B * Cout * OH * OW;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t ow = (uint32_t)(i % OW);
+        uint64_t r = i / OW;
+        const uint32_t oh = (uint32_t)(r % OH);
+        r /= OH;
+        const uint32_t c = (uint32_t)(r % Cout), b = (uint32_t)(r / Cout);
+        const float v = c < Cin ? x[(((uint64_t)b * Cin + c) * H + (oh >> up)) * W + (ow >> up)] : 0.0f;
+        y[i] = __float2half_rn(v);
+    }
+}
+
+// out[b][j][i] = in[b][i][j] for in [B][R][Cc] (fp32 or fp16) -> fp16 out [B][Cc][R]: 32 x 32 tiles
+// through shared memory, coalesced on both sides.  grid (ceil(Cc/32), ceil(R/32), B), block (32, 8).
+template <class TI>
+__global__ void __launch_bounds__(256) transpose_f16_kernel(const TI* __restrict__ in, __half* __restrict__ out,
+                                                            uint32_t R, uint32_t Cc) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    __shared__ float tile[32][33];
+    const uint32_t b = blockIdx.z, i0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+    const TI* src = in + (uint64_t)b * R * Cc;
+    __half* dst = out + (uint64_t)b * R * Cc;
+    for (uint32_t r = threadIdx.y; r < 32; r += 8) {
+        const uint32_t i = i0 + r, j = j0 + threadIdx.x;
+        if (i < R && j < Cc) tile[r][threadIdx.x] = (float)src[(uint64_t)i * Cc + j];
+    }
+    __syncthreads();
+    for (uint32_t r = threadIdx.y; r < 32; r += 8) {
+        const uint32_t j = j0 + r, i = i0 + threadIdx.x;
+        if (i < R && j < Cc) dst[(uint64_t)j * R + i] = __float2half_rn(tile[threadIdx.x][r]);
+    }
+}
+
+// ---- seeded random parameters (SplitMix64 per element: independent of launch shape)
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// int8 uniform in [-127, 127]
+__global__ void rand_q8_kernel(int8_t* __restrict__ q, uint64_t n, uint64_t seed) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        q[i] = (int8_t)((int)(mix64(seed ^ (i * 0xD1B54A32D192ED03ull)) % 255u) - 127);
+}
+
+// Q8_0 block scale as GGUF stores it: binary16(|N(0, sigma)| / 127), widened to fp32 (Box-Muller).
+__global__ void rand_scale_kernel(float* __restrict__ s, uint64_t n, uint64_t seed, float sigma) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t h = mix64(seed ^ (i * 0x8CB92BA72F3D8DD7ull));
+        const float u1 = ((float)(h >> 40) + 1.0f) * (1.0f / 16777217.0f), u2 = (float)((h >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
+        const float g = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+        s[i] = __half2float(__float2half_rn(fabsf(g) * sigma / 127.0f));
+    }
+}
+
+// mode 0: constant v; mode 1: uniform in [-v, v]
+__global__ void fill_f32_kernel(float* __restrict__ f, uint64_t n, uint64_t seed, int mode, float v) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        if (mode == 0) {
+            f[i] = v;
+        } else {
+            const uint64_t h = mix64(seed ^ (i * 0xA24BAED4963EE407ull));
+            f[i] = v * (2.0f * (float)(h >> 40) * (1.0f / 16777216.0f) - 1.0f);
+        }
+    }
+}
+
+// zero q[r][k] for k >= kreal in every row of a [rows][K] weight (conv_in's padded input channels)
+__global__ void zero_cols_kernel(int8_t* __restrict__ q, uint32_t rows, uint32_t K, uint32_t kreal) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < rows * K; i += gridDim.x * blockDim.x)
+        if (i % K >= kreal) q[i] = 0;
+}
+
+}  // namespace
+}  // namespace sdvk
+
+// ---------------------------------------------------------------- the UNet object
+
+struct sdvk_unet {
+    struct Tensor {
+        std::string name;
+        int kind;  // SDVK_UNET_Q8 or SDVK_UNET_F32
+        int init;  // F32: 0 = ones, 1 = zeros, 2 = random bias
+        uint32_t rows, cols;
+        uint64_t q_off, s_off, f_off;
+    };
+    struct Lin {  // a Q8 weight, its optional bias, by tensor index
+        int w = -1, b = -1;
+    };
+    struct Res {
+        uint32_t cin, cout, emb_off;  // emb_off: row of this block's emb_layers weight in the emb group
+        int gn1w, gn1b, gn2w, gn2b;
+        Lin conv1, conv2, skip;
+    };
+    struct Blk {
+        int ln[6];
+        Lin q, k, v, o, q2, k2, v2, o2, ff1, ff2;
+        int ff1_il_q = -1;  // internal GEGLU-interleaved copy of ff1 (tensor index of a hidden Q8 tensor)
+    };
+    struct St {
+        uint32_t C;
+        int gnw, gnb;
+        Lin proj_in, proj_out;
+        std::vector<Blk> blocks;
+    };
+    sdvk_unet_desc d{};
+    int device = 0;
+    std::vector<Tensor> t;
+    uint64_t q_bytes = 0, s_bytes = 0, f_bytes = 0;
+    uint8_t* arena = nullptr;
+    uint8_t* ws = nullptr;
+    uint64_t ws_bytes = 0;
+    uint64_t flops = 0, launches = 0;
+    // emb group: one [emb_rows][temb] weight holding every ResBlock's emb_layers.1, their biases and the
+    // ResBlocks' in_layers.2 biases in the same row order
+    int emb_w = -1, emb_b = -1, conv1_b = -1;
+    uint32_t emb_rows = 0;
+    Lin te0, te2, le0, le2, conv_in, conv_out, down[2], up[2];
+    int out_gnw = -1, out_gnb = -1;
+    std::vector<Res> res;
+    std::vector<St> st;
+    bool prepared = false;
+    uint64_t plan[8] = {};  // workspace offsets of the pass's scratch regions (fixed at creation)
+
+    int8_t* q(int i) const { return reinterpret_cast<int8_t*>(arena + t[i].q_off); }
+    float* s(int i) const { return reinterpret_cast<float*>(arena + t[i].s_off); }
+    float* f(int i) const { return i < 0 ? nullptr : reinterpret_cast<float*>(arena + t[i].f_off); }
+};
+
+namespace sdvk {
+namespace {
+
+using U = sdvk_unet;
+
+// ---- parameter registry (offsets first, one allocation after)
+struct Registry {
+    U& u;
+    int add_q8(const std::string& name, uint32_t rows, uint32_t cols) {
+        U::Tensor x{name, SDVK_UNET_Q8, 0, rows, cols, u.q_bytes, u.s_bytes, 0};
+        u.q_bytes = a256(u.q_bytes + (uint64_t)rows * cols);
+        u.s_bytes = a256(u.s_bytes + (uint64_t)rows * cols / 32 * 4);
+        u.t.push_back(x);
+        return (int)u.t.size() - 1;
+    }
+    int add_f32(const std::string& name, uint32_t n, int init) {
+        U::Tensor x{name, SDVK_UNET_F32, init, n, 1, 0, 0, u.f_bytes};
+        u.f_bytes = a256(u.f_bytes + (uint64_t)n * 4);
+        u.t.push_back(x);
+        return (int)u.t.size() - 1;
+    }
+    // a view of rows [r0, r0 + rows) of a Q8 tensor (or elements of an F32 one) under its own name
+    int view(const std::string& name, int parent, uint32_t r0, uint32_t rows) {
+        U::Tensor x = u.t[parent];
+        x.name = name;
+        x.rows = rows;
+        if (x.kind == SDVK_UNET_Q8) {
+            x.q_off += (uint64_t)r0 * x.cols;
+            x.s_off += (uint64_t)r0 * x.cols / 32 * 4;
+        } else {
+            x.f_off += (uint64_t)r0 * 4;
+        }
+        x.init = -1;  // filled through its parent
+        u.t.push_back(x);
+        return (int)u.t.size() - 1;
+    }
+    U::Lin lin(const std::string& p, uint32_t rows, uint32_t cols, bool bias = true) {
+        U::Lin l;
+        l.w = add_q8(p + ".weight", rows, cols);
+        if (bias) l.b = add_f32(p + ".bias", rows, 2);
+        return l;
+    }
+    void norm(const std::string& p, uint32_t C, int& w, int& b) {
+        w = add_f32(p + ".weight", C, 0);
+        b = add_f32(p + ".bias", C, 1);
+    }
+};
+
+struct ResSpec {
+    std::string name;
+    uint32_t cin, cout;
+};
+
+// The SDXL layout (unetForward, sdvkgen.cpp:1875-1973): the ResBlock list in pass order.
+std::vector<ResSpec> res_specs(const sdvk_unet_desc& d) {
+    std::vector<ResSpec> r;
+    const uint32_t* ch = d.model_ch;
+    std::vector<uint32_t> skip{ch[0]};
+    uint32_t c = ch[0];
+    const char* in_names[6] = {"input_blocks.1", "input_blocks.2", "input_blocks.4", "input_blocks.5", "input_blocks.7",
+                               "input_blocks.8"};
+    for (int lv = 0, i = 0; lv < 3; ++lv) {
+        for (int k = 0; k < 2; ++k, ++i) {
+            r.push_back({std::string(in_names[i]) + ".0", c, ch[lv]});
+            c = ch[lv];
+            skip.push_back(c);
+        }
+        if (lv < 2) skip.push_back(c);  // the downsampler's output
+    }
+    r.push_back({"middle_block.0", c, c});
+    r.push_back({"middle_block.2", c, c});
+    for (int j = 0; j < 9; ++j) {
+        const uint32_t lv = 2 - j / 3, cs = skip.back();
+        skip.pop_back();
+        r.push_back({"output_blocks." + std::to_string(j) + ".0", c + cs, ch[lv]});
+        c = ch[lv];
+    }
+    return r;
+}
+
+void build(U& u) {
+    const sdvk_unet_desc& d = u.d;
+    Registry R{u};
+    const uint32_t E = d.temb_dim;
+    // time and label embeddings (buildTemb, sdvkgen.cpp:1982-1995)
+    u.te0 = R.lin("time_embed.0", E, d.model_ch[0]);
+    u.te2 = R.lin("time_embed.2", E, E);
+    u.le0 = R.lin("label_emb.0.0", E, d.adm_dim);
+    u.le2 = R.lin("label_emb.0.2", E, E);
+    // the emb group
+    const std::vector<ResSpec> rs = res_specs(d);
+    for (const ResSpec& s : rs) u.emb_rows += s.cout;
+    u.emb_w = R.add_q8("(emb_layers group)", u.emb_rows, E);
+    u.emb_b = R.add_f32("(emb_layers bias group)", u.emb_rows, 2);
+    u.conv1_b = R.add_f32("(in_layers.2 bias group)", u.emb_rows, 2);
+    uint32_t off = 0;
+    for (const ResSpec& s : rs) {
+        U::Res r{};
+        r.cin = s.cin;
+        r.cout = s.cout;
+        r.emb_off = off;
+        const std::string& p = s.name;
+        R.norm(p + ".in_layers.0", s.cin, r.gn1w, r.gn1b);
+        r.conv1.w = R.add_q8(p + ".in_layers.2.weight", s.cout, s.cin * 9);
+        r.conv1.b = R.view(p + ".in_layers.2.bias", u.conv1_b, off, s.cout);
+        R.view(p + ".emb_layers.1.weight", u.emb_w, off, s.cout);
+        R.view(p + ".emb_layers.1.bias", u.emb_b, off, s.cout);
+        R.norm(p + ".out_layers.0", s.cout, r.gn2w, r.gn2b);
+        r.conv2 = R.lin(p + ".out_layers.3", s.cout, s.cout * 9);
+        if (s.cin != s.cout) r.skip = R.lin(p + ".skip_connection", s.cout, s.cin);
+        off += s.cout;
+        u.res.push_back(r);
+    }
+    // spatial transformers, in pass order
+    auto add_st = [&](const std::string& p, uint32_t C, uint32_t depth) {
+        U::St s{};
+        s.C = C;
+        R.norm(p + ".norm", C, s.gnw, s.gnb);
+        s.proj_in = R.lin(p + ".proj_in", C, C);
+        for (uint32_t i = 0; i < depth; ++i) {
+            const std::string b = p + ".transformer_blocks." + std::to_string(i);
+            U::Blk k{};
+            R.norm(b + ".norm1", C, k.ln[0], k.ln[1]);
+            R.norm(b + ".norm2", C, k.ln[2], k.ln[3]);
+            R.norm(b + ".norm3", C, k.ln[4], k.ln[5]);
+            // to_q | to_k | to_v back to back (one [3C][C] GEMM); SDXL's q/k/v projections have no bias
+            const int qkv = R.add_q8("(" + b + ".attn1.qkv group)", 3 * C, C);
+            k.q.w = R.view(b + ".attn1.to_q.weight", qkv, 0, C);
+            k.k.w = R.view(b + ".attn1.to_k.weight", qkv, C, C);
+            k.v.w = R.view(b + ".attn1.to_v.weight", qkv, 2 * C, C);
+            k.o = R.lin(b + ".attn1.to_out.0", C, C);
+            k.q2 = R.lin(b + ".attn2.to_q", C, C, false);
+            const int kv = R.add_q8("(" + b + ".attn2.kv group)", 2 * C, d.ctx_dim);
+            k.k2.w = R.view(b + ".attn2.to_k.weight", kv, 0, C);
+            k.v2.w = R.view(b + ".attn2.to_v.weight", kv, C, C);
+            k.o2 = R.lin(b + ".attn2.to_out.0", C, C);
+            k.ff1 = R.lin(b + ".ff.net.0.proj", 8 * C, C);
+            k.ff1_il_q = R.add_q8("(" + b + ".ff.net.0.proj interleaved)", 8 * C, C);
+            R.add_f32("(" + b + ".ff.net.0.proj interleaved bias)", 8 * C, -1);
+            k.ff2 = R.lin(b + ".ff.net.2", C, 4 * C);
+            s.blocks.push_back(k);
+        }
+        s.proj_out = R.lin(p + ".proj_out", C, C);
+        u.st.push_back(s);
+    };
+    const uint32_t* ch = d.model_ch;
+    if (d.depth[1]) add_st("input_blocks.4.1", ch[1], d.depth[1]), add_st("input_blocks.5.1", ch[1], d.depth[1]);
+    if (d.depth[2]) add_st("input_blocks.7.1", ch[2], d.depth[2]), add_st("input_blocks.8.1", ch[2], d.depth[2]);
+    if (d.depth[2]) add_st("middle_block.1", ch[2], d.depth[2]);
+    for (int j = 0; j < 6; ++j) {
+        const uint32_t lv = 2 - j / 3;
+        if (d.depth[lv]) add_st("output_blocks." + std::to_string(j) + ".1", ch[lv], d.depth[lv]);
+    }
+    if (d.depth[0])
+        for (int j = 6; j < 9; ++j) add_st("output_blocks." + std::to_string(j) + ".1", ch[0], d.depth[0]);
+    if (d.depth[0]) add_st("input_blocks.1.1", ch[0], d.depth[0]), add_st("input_blocks.2.1", ch[0], d.depth[0]);
+    // convolutions outside the ResBlocks; conv_in's weight is [ch0][32 * 9] with channels 4..31 zero
+    u.conv_in = R.lin("input_blocks.0.0", ch[0], kInPad * 9);
+    u.down[0] = R.lin("input_blocks.3.0.op", ch[0], ch[0] * 9);
+    u.down[1] = R.lin("input_blocks.6.0.op", ch[1], ch[1] * 9);
+    u.up[0] = R.lin(d.depth[2] ? "output_blocks.2.2.conv" : "output_blocks.2.1.conv", ch[2], ch[2] * 9);
+    u.up[1] = R.lin(d.depth[1] ? "output_blocks.5.2.conv" : "output_blocks.5.1.conv", ch[1], ch[1] * 9);
+    R.norm("out.0", ch[0], u.out_gnw, u.out_gnb);
+    u.conv_out = R.lin("out.2", kOutCh, ch[0] * 9);
+}
+
+// the spatial transformer of a module, by its name's prefix (null if the module has none)
+const U::St* find_st(const U& u, const std::string& prefix) {
+    for (const U::St& s : u.st) {
+        const U::Tensor& t = u.t[s.gnw];
+        if (t.name.compare(0, prefix.size() + 2, prefix + ".1") == 0 && t.name[prefix.size() + 2] == '.') return &s;
+    }
+    return nullptr;
+}
+
+// ---- one pass: run for real, or dry (sizes and FLOPs only)
+struct Pass {
+    U& u;
+    const LaunchEnv& env;
+    bool dry;
+    // workspace plan: bump region for module outputs + fixed scratch regions sized to their maxima
+    uint64_t bump = 0;
+    uint64_t need_h16 = 0, need_h32 = 0, need_col = 0, need_gn = 0, need_blk = 0, need_tok = 0, need_small = 0;
+    uint64_t o_h16 = 0, o_h32 = 0, o_col = 0, o_gn = 0, o_blk = 0, o_tok = 0, o_small = 0, o_bump = 0;
+    uint64_t flops = 0;
+    uint64_t launches = 0;  // kernels of this library per pass (memcpy nodes not counted)
+    int rc = SDVK_OK;
+
+    uint8_t* at(uint64_t off) const { return u.ws + off; }
+    float* out_buf(uint64_t floats) {
+        const uint64_t o = bump;
+        bump = a256(bump + floats * 4);
+        return dry ? nullptr : reinterpret_cast<float*>(at(o_bump + o));
+    }
+    template <class T>
+    T* scratch(uint64_t& need, uint64_t off, uint64_t bytes) {
+        need = std::max(need, bytes);
+        return dry ? nullptr : reinterpret_cast<T*>(at(off));
+    }
+    bool ok() const { return rc == SDVK_OK; }
+    void run(int r) {
+        if (rc == SDVK_OK) rc = r;
+    }
+    static uint32_t grid_for(uint64_t n) { return (uint32_t)std::min<uint64_t>((n + 255) / 256, 148ull * 8); }
+
+    // GroupNorm (+SiLU) to fp16
+    __half* gn16(const float* x, int w, int b, uint32_t C, uint32_t P, float eps, bool silu) {
+        const uint32_t B = u.d.batch;
+        __half* y = scratch<__half>(need_h16, o_h16, (uint64_t)B * C * P * 2);
+        void* ws = scratch<void>(need_gn, o_gn, groupnorm_workspace(B, C, P, kGroups));
+        launches += 2;
+        if (!dry && ok())
+            run(groupnorm_ex(x, u.f(w), u.f(b), y, SDVK_F16, B, C, P, kGroups, eps, silu ? 1u : 0u, ws,
+                             groupnorm_workspace(B, C, P, kGroups), env));
+        return y;
+    }
+    // 3x3 convolution of fp16 x [B][cin][H][W] (cin_real channels count toward the FLOPs)
+    void conv(const __half* x, const U::Lin& l, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W, uint32_t stride,
+              float* y, const float* bias, uint64_t bias_stride, bool acc, uint32_t cin_real = 0) {
+        const uint32_t B = u.d.batch;
+        const uint64_t wsb = conv3x3_workspace(cin, H, W, stride, SDVK_F16);
+        void* col = scratch<void>(need_col, o_col, wsb);
+        const uint32_t OH = stride == 1 ? H : H / 2, OW = stride == 1 ? W : W / 2;
+        flops += 2ull * B * OH * OW * cout * (cin_real ? cin_real : cin) * 9;
+        launches += 2ull * B;  // im2col + GEMM per image (the workspace holds a whole image's column matrix)
+        if (!dry && ok())
+            run(conv3x3_q8_ex(x, SDVK_F16, u.q(l.w), u.s(l.w), bias ? bias : u.f(l.b), bias ? bias_stride : 0, acc, y,
+                              SDVK_F32, B, cin, cout, H, W, stride, -1, col, wsb, env));
+    }
+    void copy(float* dst, const float* src, uint64_t floats) {
+        if (!dry && ok()) run(cuda_check(env, cudaMemcpyAsync(dst, src, floats * 4, cudaMemcpyDeviceToDevice, env.stream), "copy"));
+    }
+    void to_f16(const float* x, __half* y, uint32_t Cin, uint32_t Cout, uint32_t H, uint32_t W, uint32_t up) {
+        const uint64_t n = (uint64_t)u.d.batch * Cout * (H << up) * (W << up);
+        ++launches;
+        if (!dry && ok())
+            run(launch_pdl(to_f16_kernel, dim3(grid_for(n)), dim3(256), 0, env, "to_f16_kernel launch", x, y, u.d.batch,
+                           Cin, Cout, H, W, up));
+    }
+    template <class TI>
+    void transpose(const TI* in, __half* out, uint32_t R, uint32_t Cc) {
+        ++launches;
+        if (!dry && ok())
+            run(launch_pdl(transpose_f16_kernel<TI>, dim3((Cc + 31) / 32, (R + 31) / 32, u.d.batch), dim3(32, 8), 0, env,
+                           "transpose_f16_kernel launch", in, out, R, Cc));
+    }
+    // NT linear over rows of fp32 or fp16 A (the time-embedding MLPs and proj_in)
+    void linear(const void* a, int a_dtype, uint32_t rows, uint32_t K, const U::Lin& l, float* c, uint64_t ldc,
+                bool acc, const float* bias_override = nullptr) {
+        const U::Tensor& w = u.t[l.w];
+        flops += 2ull * rows * w.rows * K;
+        ++launches;
+        if (dry || !ok()) return;
+        GemmQ8Desc g{};
+        g.x = a;
+        g.x_dtype = a_dtype;
+        g.ldx = K;
+        g.wq = u.q(l.w);
+        g.ws = u.s(l.w);
+        g.ldw = K;
+        g.bias = bias_override ? bias_override : u.f(l.b);
+        g.c = c;
+        g.c_dtype = SDVK_F32;
+        g.ldc = ldc;
+        g.xrows = rows;
+        g.wrows = w.rows;
+        g.K = K;
+        g.batch = 1;
+        g.accumulate = acc;
+        run(gemm_q8(g, env));
+    }
+    // 1x1 convolution, channel-major: y[b] (=|+=) W x[b] (+ bias), x in a_dtype [B][cin][P]
+    void conv1x1(const void* x, int x_dtype, const U::Lin& l, uint32_t cin, uint32_t cout, uint32_t P, float* y,
+                 bool acc) {
+        const uint32_t B = u.d.batch;
+        flops += 2ull * B * P * cout * cin;
+        ++launches;
+        if (dry || !ok()) return;
+        GemmQ8Desc g{};
+        g.x = x;
+        g.x_dtype = x_dtype;
+        g.ldx = P;
+        g.sx = (uint64_t)cin * P;
+        g.wq = u.q(l.w);
+        g.ws = u.s(l.w);
+        g.ldw = cin;
+        g.sw = 0;
+        g.bias = u.f(l.b);
+        g.c = y;
+        g.c_dtype = SDVK_F32;
+        g.ldc = P;
+        g.sc = (uint64_t)cout * P;
+        g.xrows = P;
+        g.wrows = cout;
+        g.K = cin;
+        g.batch = B;
+        g.nn = true;
+        g.accumulate = acc;
+        run(gemm_q8(g, env));
+    }
+
+    // resBlock (sdvkgen.cpp:1669-1707)
+    float* resblock(const float* x, const U::Res& r, uint32_t H, uint32_t W, const float* ebias) {
+        const uint32_t B = u.d.batch, P = H * W;
+        __half* h16 = gn16(x, r.gn1w, r.gn1b, r.cin, P, 1e-5f, true);
+        float* h = scratch<float>(need_h32, o_h32, (uint64_t)B * r.cout * P * 4);
+        conv(h16, r.conv1, r.cin, r.cout, H, W, 1, h, dry ? nullptr : ebias + r.emb_off, u.emb_rows, false);
+        flops += 2ull * B * r.cout * u.d.temb_dim;  // its share of the emb GEMM
+        __half* g16 = gn16(h, r.gn2w, r.gn2b, r.cout, P, 1e-5f, true);
+        float* out = out_buf((uint64_t)B * r.cout * P);
+        if (r.cin == r.cout) copy(out, x, (uint64_t)B * r.cout * P);
+        else conv1x1(x, SDVK_F32, r.skip, r.cin, r.cout, P, out, false);
+        conv(g16, r.conv2, r.cout, r.cout, H, W, 1, out, nullptr, 0, true);
+        return out;
+    }
+
+    // spatialTransformer (sdvkgen.cpp:1722-1777), x updated in place
+    void transformer(float* x, const U::St& s, uint32_t H, uint32_t W, const void* ctx, int ctx_dtype) {
+        const uint32_t B = u.d.batch, P = H * W, C = s.C;
+        __half* g16 = gn16(x, s.gnw, s.gnb, C, P, 1e-6f, false);
+        __half* a16 = scratch<__half>(need_tok, o_tok, (uint64_t)B * P * C * 2);
+        transpose(g16, a16, C, P);  // [B][C][P] -> [B][P][C]
+        float* t = scratch<float>(need_h32, o_h32, (uint64_t)B * P * C * 4);
+        linear(a16, SDVK_F16, B * P, C, s.proj_in, t, C, false);
+        for (const U::Blk& k : s.blocks) {
+            sdvk_block_desc bd{};
+            bd.x = t;
+            bd.ctx = ctx;
+            bd.ctx_dtype = ctx_dtype;
+            bd.batch = B;
+            bd.T = P;
+            bd.C = C;
+            bd.heads = C / u.d.head_dim;
+            bd.Tctx = u.d.Tctx;
+            bd.Cctx = u.d.ctx_dim;
+            bd.ff_inner = 4 * C;
+            bd.eps = 1e-5f;
+            const uint64_t wsb = block_workspace_bytes(bd);
+            void* bws = scratch<void>(need_blk, o_blk, wsb);
+            const uint64_t T = P, Tc = u.d.Tctx, F = 4ull * C;
+            launches += 13;  // 3 LayerNorms, 7 GEMMs (QKV fused, GEGLU in FF1), the K|V reduce, 2 attentions
+            flops += 2ull * B * (T * 3 * C * C + T * C * C + T * C * C + Tc * 2 * C * u.d.ctx_dim + T * C * C +
+                                 T * 2 * F * C + T * C * F) +
+                     4ull * B * T * T * C + 4ull * B * T * Tc * C;
+            if (dry || !ok()) continue;
+            bd.ln1_w = u.f(k.ln[0]), bd.ln1_b = u.f(k.ln[1]);
+            bd.ln2_w = u.f(k.ln[2]), bd.ln2_b = u.f(k.ln[3]);
+            bd.ln3_w = u.f(k.ln[4]), bd.ln3_b = u.f(k.ln[5]);
+            auto L = [&](const U::Lin& l) { return sdvk_q8_linear{u.q(l.w), u.s(l.w), u.f(l.b)}; };
+            bd.q = L(k.q), bd.k = L(k.k), bd.v = L(k.v), bd.o = L(k.o);
+            bd.q2 = L(k.q2), bd.k2 = L(k.k2), bd.v2 = L(k.v2), bd.o2 = L(k.o2);
+            bd.ff1 = sdvk_q8_linear{u.q(k.ff1_il_q), u.s(k.ff1_il_q), u.f(k.ff1_il_q + 1)};
+            bd.ff1_geglu_interleaved = 1;
+            bd.ff2 = L(k.ff2);
+            run(transformer_block(bd, bws, wsb, env));
+        }
+        __half* u16 = scratch<__half>(need_tok, o_tok, (uint64_t)B * P * C * 2);
+        transpose(t, u16, P, C);  // [B][P][C] fp32 -> [B][C][P] fp16
+        conv1x1(u16, SDVK_F16, s.proj_out, C, C, P, x, true);
+    }
+
+    // unetForward (sdvkgen.cpp:1875-1973)
+    void forward(const float* x_in, const float* timesteps, const float* adm, const void* ctx, int ctx_dtype,
+                 float* out) {
+        const sdvk_unet_desc& d = u.d;
+        const uint32_t B = d.batch, E = d.temb_dim, c0 = d.model_ch[0];
+        // ---- time embedding (buildTemb): temb = te2(silu(te0(sin(t)))) + le2(silu(le0(adm)))
+        float* small = scratch<float>(need_small, o_small,
+                                      a256((uint64_t)B * c0 * 4) + 3 * a256((uint64_t)B * E * 4) +
+                                          a256((uint64_t)B * u.emb_rows * 4));
+        float* sinb = small;
+        float* t1 = dry ? nullptr : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(small) + a256((uint64_t)B * c0 * 4));
+        float* temb = dry ? nullptr : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(t1) + a256((uint64_t)B * E * 4));
+        float* t2 = dry ? nullptr : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(temb) + a256((uint64_t)B * E * 4));
+        float* ebias = dry ? nullptr : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(t2) + a256((uint64_t)B * E * 4));
+        launches += 5;  // the sinusoid, three SiLUs, the bias pair
+        if (!dry && ok())
+            run(launch_pdl(temb_sin_kernel, dim3(grid_for((uint64_t)B * c0 / 2)), dim3(256), 0, env,
+                           "temb_sin_kernel launch", timesteps, sinb, B, c0));
+        auto silu = [&](const float* a, float* y, uint64_t n) {
+            if (!dry && ok())
+                run(launch_pdl(silu_kernel, dim3(grid_for(n)), dim3(256), 0, env, "silu_kernel launch", a, y, n));
+        };
+        linear(sinb, SDVK_F32, B, c0, u.te0, t1, E, false);
+        silu(t1, t1, (uint64_t)B * E);
+        linear(t1, SDVK_F32, B, E, u.te2, temb, E, false);
+        linear(adm, SDVK_F32, B, d.adm_dim, u.le0, t2, E, false);
+        silu(t2, t2, (uint64_t)B * E);
+        linear(t2, SDVK_F32, B, E, u.le2, temb, E, true);
+        silu(temb, t2, (uint64_t)B * E);  // silu(temb) feeds every ResBlock's emb_layers
+        if (!dry && ok())
+            run(launch_pdl(bias_pair_kernel, dim3(grid_for((uint64_t)B * u.emb_rows)), dim3(256), 0, env,
+                           "bias_pair_kernel launch", (const float*)u.f(u.emb_b), (const float*)u.f(u.conv1_b), ebias,
+                           u.emb_rows, B));
+        {
+            U::Lin eg{u.emb_w, -1};
+            const uint64_t f0 = flops;
+            linear(t2, SDVK_F32, B, E, eg, ebias, u.emb_rows, true);
+            flops = f0;  // counted per ResBlock
+        }
+        // ---- conv_in
+        uint32_t H = d.H, W = d.W, ch = c0;
+        __half* xin16 = scratch<__half>(need_h16, o_h16, (uint64_t)B * kInPad * H * W * 2);
+        to_f16(x_in, xin16, kInCh, kInPad, H, W, 0);
+        float* x = out_buf((uint64_t)B * ch * H * W);
+        conv(xin16, u.conv_in, kInPad, ch, H, W, 1, x, nullptr, 0, false, kInCh);
+        std::vector<float*> hs{x};
+        std::vector<uint32_t> hch{ch};
+        size_t ri = 0;
+        auto module = [&](const std::string& prefix) {
+            const U::Res& r = u.res[ri++];
+            x = resblock(x, r, H, W, ebias);
+            ch = r.cout;
+            if (const U::St* s = find_st(u, prefix)) transformer(x, *s, H, W, ctx, ctx_dtype);
+        };
+        const char* in_names[6] = {"input_blocks.1", "input_blocks.2", "input_blocks.4", "input_blocks.5",
+                                   "input_blocks.7", "input_blocks.8"};
+        for (int lv = 0, i = 0; lv < 3; ++lv) {
+            for (int k = 0; k < 2; ++k, ++i) {
+                module(in_names[i]);
+                hs.push_back(x);
+                hch.push_back(ch);
+            }
+            if (lv < 2) {  // conv3s2 (sdvkgen.cpp:1162-1178)
+                __half* x16 = scratch<__half>(need_h16, o_h16, (uint64_t)B * ch * H * W * 2);
+                to_f16(x, x16, ch, ch, H, W, 0);
+                float* y = out_buf((uint64_t)B * ch * (H / 2) * (W / 2));
+                conv(x16, u.down[lv], ch, ch, H, W, 2, y, nullptr, 0, false);
+                x = y;
+                H /= 2, W /= 2;
+                hs.push_back(x);
+                hch.push_back(ch);
+            }
+        }
+        module("middle_block.0");
+        if (const U::St* s = find_st(u, "middle_block")) transformer(x, *s, H, W, ctx, ctx_dtype);
+        {
+            const U::Res& r = u.res[ri++];
+            x = resblock(x, r, H, W, ebias);
+        }
+        for (int j = 0; j < 9; ++j) {
+            const uint32_t cs = hch.back(), P = H * W;
+            const float* skip = hs.back();
+            hs.pop_back();
+            hch.pop_back();
+            // concatCh (sdvkgen.cpp:1791-1796), per image
+            float* cat = out_buf((uint64_t)B * (ch + cs) * P);
+            if (!dry && ok()) {
+                run(cuda_check(env, cudaMemcpy2DAsync(cat, (uint64_t)(ch + cs) * P * 4, x, (uint64_t)ch * P * 4,
+                                                      (uint64_t)ch * P * 4, B, cudaMemcpyDeviceToDevice, env.stream),
+                               "concat"));
+                run(cuda_check(env, cudaMemcpy2DAsync(cat + (uint64_t)ch * P, (uint64_t)(ch + cs) * P * 4, skip,
+                                                      (uint64_t)cs * P * 4, (uint64_t)cs * P * 4, B,
+                                                      cudaMemcpyDeviceToDevice, env.stream),
+                               "concat"));
+            }
+            x = cat;
+            ch += cs;
+            module("output_blocks." + std::to_string(j));
+            if (j == 2 || j == 5) {  // up2 + conv3Raw
+                __half* x16 = scratch<__half>(need_h16, o_h16, (uint64_t)B * ch * H * W * 4 * 2);
+                to_f16(x, x16, ch, ch, H, W, 1);
+                H *= 2, W *= 2;
+                float* y = out_buf((uint64_t)B * ch * H * W);
+                conv(x16, u.up[j == 2 ? 0 : 1], ch, ch, H, W, 1, y, nullptr, 0, false);
+                x = y;
+            }
+        }
+        // ---- out: GN + SiLU, conv 3x3 to the 4 latent channels
+        __half* h16 = gn16(x, u.out_gnw, u.out_gnb, ch, H * W, 1e-5f, true);
+        conv(h16, u.conv_out, ch, kOutCh, H, W, 1, out, nullptr, 0, false);
+    }
+
+    void layout() {
+        uint64_t o = 0;
+        auto put = [&](uint64_t& off, uint64_t need) {
+            off = o;
+            o = a256(o + need);
+        };
+        put(o_h16, need_h16);
+        put(o_h32, need_h32);
+        put(o_col, need_col);
+        put(o_gn, need_gn);
+        put(o_blk, need_blk);
+        put(o_tok, need_tok);
+        put(o_small, need_small);
+        put(o_bump, bump);
+        u.ws_bytes = o;
+        const uint64_t v[8] = {o_h16, o_h32, o_col, o_gn, o_blk, o_tok, o_small, o_bump};
+        std::memcpy(u.plan, v, sizeof v);
+    }
+    void use_plan() {
+        o_h16 = u.plan[0], o_h32 = u.plan[1], o_col = u.plan[2], o_gn = u.plan[3];
+        o_blk = u.plan[4], o_tok = u.plan[5], o_small = u.plan[6], o_bump = u.plan[7];
+    }
+};
+
+int check_desc(const sdvk_unet_desc& d, const LaunchEnv& env) {
+    const uint32_t* c = d.model_ch;
+    if (!d.batch || !d.H || !d.W || d.H % 4 || d.W % 4)
+        return fail(env, SDVK_E_SHAPE, "the latent's height and width must be positive multiples of 4");
+    if (d.head_dim == 0 || d.head_dim > 64) return fail(env, SDVK_E_SHAPE, "head_dim must be in 1..64");
+    for (int i = 0; i < 3; ++i)
+        if (!c[i] || c[i] % 32 || c[i] % d.head_dim || (d.depth[i] && c[i] > 3072))
+            return fail(env, SDVK_E_SHAPE, "model channels must be multiples of 32 and of head_dim (<= 3072 with attention)");
+    if (!d.temb_dim || d.temb_dim % 32 || !d.adm_dim || d.adm_dim % 32 || c[0] % 2 || !d.ctx_dim || d.ctx_dim % 32 ||
+        !d.Tctx)
+        return fail(env, SDVK_E_SHAPE, "temb_dim, adm_dim and ctx_dim must be positive multiples of 32");
+    return SDVK_OK;
+}
+
+}  // namespace
+
+int unet_create(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env) {
+    if (!out) return fail(env, SDVK_E_ARG, "null pointer");
+    *out = nullptr;
+    if (int rc = check_desc(d, env)) return rc;
+    U* u = new (std::nothrow) U();
+    if (!u) return fail(env, SDVK_E_OOM, "host allocation");
+    u->d = d;
+    u->device = env.device;
+    build(*u);
+    Pass plan{*u, env, true};
+    plan.forward(nullptr, nullptr, nullptr, nullptr, SDVK_F16, nullptr);
+    plan.layout();
+    u->flops = plan.flops;
+    u->launches = plan.launches;
+    const uint64_t q0 = 0, s0 = a256(u->q_bytes), f0 = s0 + a256(u->s_bytes), total = f0 + a256(u->f_bytes);
+    for (U::Tensor& t : u->t) {
+        t.s_off += s0;
+        t.f_off += f0;
+        t.q_off += q0;
+    }
+    if (cudaMalloc(&u->arena, total) != cudaSuccess || cudaMalloc(&u->ws, u->ws_bytes ? u->ws_bytes : 256) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(u->arena);
+        delete u;
+        return fail(env, SDVK_E_OOM, "device allocation of " + std::to_string(total) + " parameter bytes and a workspace");
+    }
+    if (cudaMemsetAsync(u->arena, 0, total, env.stream) != cudaSuccess) {
+        cudaFree(u->arena);
+        cudaFree(u->ws);
+        delete u;
+        return fail(env, SDVK_E_CUDA, "clearing the parameter arena");
+    }
+    *out = u;
+    return SDVK_OK;
+}
+
+int unet_destroy(sdvk_unet* u) {
+    if (!u) return SDVK_OK;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != u->device) cudaSetDevice(u->device);
+    cudaFree(u->arena);
+    cudaFree(u->ws);
+    if (cur >= 0 && cur != u->device) cudaSetDevice(cur);
+    delete u;
+    return SDVK_OK;
+}
+
+int unet_prepare(sdvk_unet* u, const LaunchEnv& env) {
+    for (const U::St& s : u->st)
+        for (const U::Blk& k : s.blocks) {
+            const uint32_t F = 4 * s.C;
+            if (int rc = geglu_interleave(u->q(k.ff1.w), u->s(k.ff1.w), u->f(k.ff1.b), F, s.C, u->q(k.ff1_il_q),
+                                          u->s(k.ff1_il_q), u->f(k.ff1_il_q + 1), env))
+                return rc;
+        }
+    u->prepared = true;
+    return SDVK_OK;
+}
+
+int unet_init_random(sdvk_unet* u, uint64_t seed, const LaunchEnv& env) {
+    const uint64_t total_q = [&] {
+        uint64_t m = 0;
+        for (const U::Tensor& t : u->t)
+            if (t.kind == SDVK_UNET_Q8) m = std::max(m, t.q_off + (uint64_t)t.rows * t.cols);
+        return m;
+    }();
+    uint64_t total_s = 0, s_begin = ~0ull;
+    for (const U::Tensor& t : u->t)
+        if (t.kind == SDVK_UNET_Q8) {
+            total_s = std::max(total_s, t.s_off + (uint64_t)t.rows * t.cols / 32 * 4);
+            s_begin = std::min(s_begin, t.s_off);
+        }
+    const uint32_t grid = (uint32_t)env.num_sms * 8;
+    rand_q8_kernel<<<grid, 256, 0, env.stream>>>(reinterpret_cast<int8_t*>(u->arena), total_q, seed);
+    rand_scale_kernel<<<grid, 256, 0, env.stream>>>(reinterpret_cast<float*>(u->arena + s_begin), (total_s - s_begin) / 4,
+                                                    seed ^ 0x5CA1Eull, 0.02f);
+    for (size_t i = 0; i < u->t.size(); ++i) {
+        const U::Tensor& t = u->t[i];
+        if (t.kind != SDVK_UNET_F32 || t.init < 0) continue;
+        fill_f32_kernel<<<(t.rows + 255) / 256, 256, 0, env.stream>>>(u->f((int)i), t.rows, seed + 1000003ull * i,
+                                                                       t.init == 2 ? 1 : 0,
+                                                                       t.init == 0 ? 1.0f : t.init == 1 ? 0.0f : 0.02f);
+    }
+    const U::Tensor& ci = u->t[u->conv_in.w];
+    zero_cols_kernel<<<64, 256, 0, env.stream>>>(u->q(u->conv_in.w), ci.rows, ci.cols, kInCh * 9);
+    if (int rc = cuda_check(env, cudaGetLastError(), "UNet random init")) return rc;
+    return unet_prepare(u, env);
+}
+
+int unet_forward(sdvk_unet* u, const float* x, const float* timesteps, const float* adm, const void* ctx, int ctx_dtype,
+                 float* out, const LaunchEnv& env) {
+    if (!x || !timesteps || !adm || !ctx || !out) return fail(env, SDVK_E_ARG, "null pointer");
+    if (ctx_dtype != SDVK_F16 && ctx_dtype != SDVK_BF16 && ctx_dtype != SDVK_F32)
+        return fail(env, SDVK_E_ARG, "context dtype must be F16, BF16 or F32");
+    if (!u->prepared) return fail(env, SDVK_E_ARG, "sdvk_unet_prepare (or sdvk_unet_init_random) has not run");
+    Pass p{*u, env, false};
+    p.use_plan();
+    p.forward(x, timesteps, adm, ctx, ctx_dtype, out);
+    return p.rc;
+}
+
+uint64_t unet_flops(const sdvk_unet* u) { return u ? u->flops : 0; }
+uint64_t unet_launches(const sdvk_unet* u) { return u ? u->launches : 0; }
+uint64_t unet_workspace_bytes(const sdvk_unet* u) { return u ? u->ws_bytes : 0; }
+
+int unet_tensor(const sdvk_unet* u, uint32_t i, sdvk_unet_tensor_info* out) {
+    if (!u || !out || i >= u->t.size()) return SDVK_E_ARG;
+    const U::Tensor& t = u->t[i];
+    out->name = t.name.c_str();
+    out->kind = t.kind;
+    out->rows = t.rows;
+    out->cols = t.cols;
+    out->q = t.kind == SDVK_UNET_Q8 ? u->q((int)i) : nullptr;
+    out->s = t.kind == SDVK_UNET_Q8 ? u->s((int)i) : nullptr;
+    out->f = t.kind == SDVK_UNET_F32 ? u->f((int)i) : nullptr;
+    return SDVK_OK;
+}
+
+uint32_t unet_tensor_count(const sdvk_unet* u) { return u ? (uint32_t)u->t.size() : 0; }
+
+}  // namespace sdvk
