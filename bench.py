@@ -885,9 +885,13 @@ def main(argv=None):
     def step(i):
         wl.step(torch_ops, sets[i % wl.rotate])
 
-    # warm-up (also the first launch's attribute setup), then graphs of GRAPH_LEN steps
+    # warm-up (also the first launch's attribute setup), then graphs of GRAPH_LEN steps; each eager
+    # warm-up step is an NVTX range "step", so a profiler can select one step's launches
+    # (ncu --nvtx --nvtx-include "step/")
     for i in range(args.warmup):
+        torch.cuda.nvtx.range_push("step")
         step(i)
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     cap = torch.cuda.Stream(device)
     graphs = {}

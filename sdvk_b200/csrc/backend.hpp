@@ -36,6 +36,7 @@ struct GemmQ8Desc {
     const float* ws;
     uint64_t ldw, sw;
     const float* bias;  // per w row, or null
+    uint64_t sbias;     // bias batch stride (elements; 0 = one bias for every batch)
     void* c;
     int c_dtype;
     uint64_t ldc, sc;

@@ -19,16 +19,19 @@ namespace {
 
 constexpr int kColThreads = 256;
 
-// grid (ceil(np / (256 * 8)), K): thread = 8 consecutive output positions p of column-matrix row k,
+// grid (ceil(np / (256 * 8)), K, images): thread = 8 consecutive output positions p of column-matrix row k,
 // col[k][p] = x[c][oh*stride + ky + off][ow*stride + kx + off] (0 outside), stored with 16-byte
 // vector stores (rows of col ld elements apart, ld % 8 == 0; positions in [np, round_up(np, 8)) are
 // written with values the GEMM never reads).
 template <class T>
 __global__ void __launch_bounds__(kColThreads) im2col3x3_kernel(const T* __restrict__ x, T* __restrict__ col,
                                                                 uint32_t H, uint32_t W, uint32_t OW, uint32_t row0,
-                                                                uint32_t np, uint64_t ld, uint32_t stride, int off) {
+                                                                uint32_t np, uint64_t ld, uint32_t stride, int off,
+                                                                uint64_t xbs, uint64_t cbs) {
     grid_dependency_wait();
     grid_launch_dependents();
+    x += blockIdx.z * xbs;  // image z: its input, and its column matrix cbs elements further on
+    col += blockIdx.z * cbs;
     const uint32_t k = blockIdx.y;
     const uint32_t p0 = (blockIdx.x * kColThreads + threadIdx.x) * 8;
     if (p0 >= np) return;
@@ -99,6 +102,47 @@ int conv3x3_q8_ex(const void* x, int x_dtype, const int8_t* q, const float* s, c
         return fail(env, SDVK_E_ARG, "conv workspace too small for one aligned band of output rows, or misaligned");
     const uint64_t pitch = (uint64_t)rows * OW;
     const uint64_t xs = (uint64_t)cin * H * W * es, ys = (uint64_t)cout * P * dtype_size(y_dtype);
+    if (rows == OH && batch > 1 && ws_bytes / ((uint64_t)K * P * es) >= batch && P % 8 == 0) {
+        // Every image's column matrix fits: one im2col launch over the images and one batched GEMM
+        // (image z's columns at z*K*P, its output at z*cout*P, its bias at z*bias_stride).
+        const dim3 grid((uint32_t)((P + 8 * kColThreads - 1) / (8 * kColThreads)), K, batch);
+        const uint64_t xbe = (uint64_t)cin * H * W, cbe = (uint64_t)K * P;
+        int rc;
+        if (x_dtype == SDVK_F32)
+            rc = launch_pdl(im2col3x3_kernel<float>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
+                            static_cast<const float*>(x), static_cast<float*>(workspace), H, W, OW, 0u, (uint32_t)P,
+                            P, stride, off, xbe, cbe);
+        else if (x_dtype == SDVK_F16)
+            rc = launch_pdl(im2col3x3_kernel<__half>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
+                            static_cast<const __half*>(x), static_cast<__half*>(workspace), H, W, OW, 0u, (uint32_t)P,
+                            P, stride, off, xbe, cbe);
+        else
+            rc = launch_pdl(im2col3x3_kernel<__nv_bfloat16>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
+                            static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(workspace), H, W, OW, 0u,
+                            (uint32_t)P, P, stride, off, xbe, cbe);
+        if (rc) return rc;
+        GemmQ8Desc d{};
+        d.x = workspace;
+        d.x_dtype = x_dtype;
+        d.ldx = P;
+        d.sx = cbe;
+        d.wq = q;
+        d.ws = s;
+        d.ldw = K;
+        d.bias = bias;
+        d.sbias = bias ? bias_stride : 0;
+        d.c = y;
+        d.c_dtype = y_dtype;
+        d.ldc = P;
+        d.sc = (uint64_t)cout * P;
+        d.xrows = (uint32_t)P;
+        d.wrows = cout;
+        d.K = K;
+        d.batch = batch;
+        d.nn = true;
+        d.accumulate = accumulate;
+        return gemm_q8(d, env);
+    }
     for (uint32_t bi = 0; bi < batch; ++bi) {
         const uint8_t* xb = static_cast<const uint8_t*>(x) + bi * xs;
         uint8_t* yb = static_cast<uint8_t*>(y) + bi * ys;
@@ -109,15 +153,16 @@ int conv3x3_q8_ex(const void* x, int x_dtype, const int8_t* q, const float* s, c
             if (x_dtype == SDVK_F32)
                 rc = launch_pdl(im2col3x3_kernel<float>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
                                 reinterpret_cast<const float*>(xb), static_cast<float*>(workspace), H, W, OW, r0, np,
-                                pitch, stride, off);
+                                pitch, stride, off, (uint64_t)0, (uint64_t)0);
             else if (x_dtype == SDVK_F16)
                 rc = launch_pdl(im2col3x3_kernel<__half>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
                                 reinterpret_cast<const __half*>(xb), static_cast<__half*>(workspace), H, W, OW, r0, np,
-                                pitch, stride, off);
+                                pitch, stride, off, (uint64_t)0, (uint64_t)0);
             else
                 rc = launch_pdl(im2col3x3_kernel<__nv_bfloat16>, grid, dim3(kColThreads), 0, env,
                                 "im2col3x3_kernel launch", reinterpret_cast<const __nv_bfloat16*>(xb),
-                                static_cast<__nv_bfloat16*>(workspace), H, W, OW, r0, np, pitch, stride, off);
+                                static_cast<__nv_bfloat16*>(workspace), H, W, OW, r0, np, pitch, stride, off,
+                                (uint64_t)0, (uint64_t)0);
             if (rc) return rc;
             GemmQ8Desc d{};
             d.x = workspace;

@@ -131,6 +131,7 @@ int launch(const GemmQ8Desc& d, const LaunchEnv& env) {
     p.num_tiles = p.tiles_x * p.tiles_w * d.batch;
     p.k_stages = (d.K + Cfg::kBK - 1) / Cfg::kBK;
     p.accumulate = d.accumulate ? 1u : 0u;
+    p.sbias = d.sbias;
     p.err = env.err_dev;
     p.timeout_ns = env.timeout_ns;
     p.c = d.c;
@@ -192,6 +193,7 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     p.num_tiles = p.tiles_x * p.tiles_w * d.batch;
     p.k_stages = (d.K + Cfg::kBK - 1) / Cfg::kBK;
     p.accumulate = d.accumulate ? 1u : 0u;
+    p.sbias = d.sbias;
     p.err = env.err_dev;
     p.timeout_ns = env.timeout_ns;
     p.c = d.c;

@@ -29,6 +29,7 @@ struct GemmQ8Params {
     const int8_t* wq;       // weight payload, element (row, k) of batch z at wq[z*sW + row*ldw + k]
     const float* ws;        // fp32 scale per 32 payload elements (flat index >> 5)
     const float* bias;      // per weight row (NT: per output column, NN: per output row), or null
+    uint64_t sbias;         // bias batch stride in elements (0: one bias for all batches)
     uint32_t xrows;         // activation rows (tensor-core M extent)
     uint32_t wrows;         // weight rows (tensor-core N extent)
     uint32_t K;
@@ -626,10 +627,11 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
                 if (p.bias) {
+                    const float* bz = p.bias + z * p.sbias;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const uint32_t n = (uint32_t)w0 + j;
-                        v[j] += (n < p.wrows) ? __ldg(p.bias + n) : 0.0f;
+                        v[j] += (n < p.wrows) ? __ldg(bz + n) : 0.0f;
                     }
                 }
                 uint8_t* buf = ebuf + (nstore & 1) * 4096;

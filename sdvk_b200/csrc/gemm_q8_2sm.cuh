@@ -342,7 +342,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             tc_fence_after();
             const int w0 = (int)(wt * 2 * Cfg::kBW + rank * Cfg::kBW) + q * 32;  // this warp's first weight row
             const uint32_t n = (uint32_t)w0 + lane;                           // this thread's weight row
-            const float b = (p.bias && n < p.wrows) ? __ldg(p.bias + n) : 0.0f;
+            const float b = (p.bias && n < p.wrows) ? __ldg(p.bias + z * p.sbias + n) : 0.0f;
 #pragma unroll 1
             for (int cc = 0; cc < Cfg::kBNX / 32; ++cc, ++nstore) {
                 const int x0 = (int)(xt * Cfg::kBNX) + cc * 32;

@@ -432,11 +432,11 @@ struct Pass {
     void conv(const __half* x, const U::Lin& l, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W, uint32_t stride,
               float* y, const float* bias, uint64_t bias_stride, bool acc, uint32_t cin_real = 0) {
         const uint32_t B = u.d.batch;
-        const uint64_t wsb = conv3x3_workspace(cin, H, W, stride, SDVK_F16);
+        const uint64_t wsb = conv3x3_workspace(cin, H, W, stride, SDVK_F16) * B;  // every image's columns: one GEMM
         void* col = scratch<void>(need_col, o_col, wsb);
         const uint32_t OH = stride == 1 ? H : H / 2, OW = stride == 1 ? W : W / 2;
         flops += 2ull * B * OH * OW * cout * (cin_real ? cin_real : cin) * 9;
-        launches += 2ull * B;  // im2col + GEMM per image (the workspace holds a whole image's column matrix)
+        launches += 2;  // im2col and GEMM, each over all images (the workspace holds every column matrix)
         if (!dry && ok())
             run(conv3x3_q8_ex(x, SDVK_F16, u.q(l.w), u.s(l.w), bias ? bias : u.f(l.b), bias ? bias_stride : 0, acc, y,
                               SDVK_F32, B, cin, cout, H, W, stride, -1, col, wsb, env));
