@@ -59,6 +59,122 @@ __global__ void __launch_bounds__(kColThreads) im2col3x3_kernel(const T* __restr
     }
 }
 
+// 8 consecutive values of T from a 16-byte aligned address, widened to float
+template <class T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(p));
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[2 * j] = (float)__builtin_bit_cast(T, (uint16_t)(u[j] & 0xFFFFu));
+            v[2 * j + 1] = (float)__builtin_bit_cast(T, (uint16_t)(u[j] >> 16));
+        }
+    }
+}
+
+// 8 floats stored as T (exact: every value came from a T) to a 16-byte aligned address
+template <class T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w[j] = (uint32_t)__builtin_bit_cast(uint16_t, T(v[2 * j])) |
+                   ((uint32_t)__builtin_bit_cast(uint16_t, T(v[2 * j + 1])) << 16);
+        *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// Row-segment im2col: grid (ceil(rows * OW/8 / 256), cin, images); a thread owns 8 consecutive output
+// positions of one output row and one input channel c.  It reads the three input rows it needs once
+// (the aligned 8*S values under the segment as 16-byte vectors, plus a one-value halo on either side)
+// and writes all nine column-matrix rows k = c*9 + ky*3 + kx for its positions, 16 bytes each.
+// Requires OW % 8 == 0, W % 8 == 0 and a 16-byte aligned x (every row and segment start aligned).
+template <class T, int S, int OFF>
+__global__ void __launch_bounds__(kColThreads) im2col3x3_rows_kernel(const T* __restrict__ x, T* __restrict__ col,
+                                                                     uint32_t H, uint32_t W, uint32_t OW,
+                                                                     uint32_t row0, uint32_t nrows, uint64_t ld,
+                                                                     uint64_t xbs, uint64_t cbs) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const uint32_t segs = OW / 8, seg = blockIdx.x * kColThreads + threadIdx.x;
+    if (seg >= nrows * segs) return;
+    const uint32_t c = blockIdx.y, r = seg / segs, ow0 = (seg - r * segs) * 8, oh = row0 + r;
+    const T* xc = x + blockIdx.z * xbs + (uint64_t)c * H * W;
+    T* dst = col + blockIdx.z * cbs + (uint64_t)c * 9 * ld + (uint64_t)r * OW + ow0;
+    const uint32_t a0 = ow0 * S;  // first input column under the segment (8-aligned)
+    constexpr int NV = 8 * S + 2;  // v[i] holds input column a0 - 1 + i
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky) {
+        const int ih = (int)(oh * S) + ky + OFF;
+        float v[NV];
+        if (ih >= 0 && ih < (int)H) {
+            const T* row = xc + (uint64_t)ih * W;
+            v[0] = a0 >= 1 ? (float)row[a0 - 1] : 0.0f;
+#pragma unroll
+            for (int h = 0; h < S; ++h) {
+                float t[8];
+                load8(row + a0 + 8 * h, t);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[1 + 8 * h + j] = t[j];
+            }
+            v[NV - 1] = a0 + 8 * S < W ? (float)row[a0 + 8 * S] : 0.0f;
+        } else {
+#pragma unroll
+            for (int i = 0; i < NV; ++i) v[i] = 0.0f;
+        }
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+            float o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = v[j * S + kx + OFF + 1];
+            store8(dst + (uint64_t)(ky * 3 + kx) * ld, o);
+        }
+    }
+}
+
+// im2col of output rows [row0, row0 + nrows) of `images` images into col (row pitch ld elements; image z
+// at x + z*xbs, its columns at col + z*cbs): the row-segment kernel where the shape allows, else the
+// per-element one.
+template <class T>
+int im2col_launch(const T* x, T* col, uint32_t cin, uint32_t H, uint32_t W, uint32_t OW, uint32_t row0,
+                  uint32_t nrows, uint64_t ld, uint32_t stride, int off, uint32_t images, uint64_t xbs, uint64_t cbs,
+                  const LaunchEnv& env) {
+    const bool rows_ok = OW % 8 == 0 && W % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                         (xbs * sizeof(T)) % 16 == 0 && ld % 8 == 0 && (cbs * sizeof(T)) % 16 == 0;
+    if (rows_ok) {
+        const dim3 grid((nrows * (OW / 8) + kColThreads - 1) / kColThreads, cin, images);
+        auto kern = stride == 1 ? im2col3x3_rows_kernel<T, 1, -1>
+                                : off == 0 ? im2col3x3_rows_kernel<T, 2, 0> : im2col3x3_rows_kernel<T, 2, -1>;
+        return launch_pdl(kern, grid, dim3(kColThreads), 0, env, "im2col3x3_rows_kernel launch", x, col, H, W, OW, row0,
+                          nrows, ld, xbs, cbs);
+    }
+    const uint32_t np = nrows * OW;
+    const dim3 grid((np + 8 * kColThreads - 1) / (8 * kColThreads), cin * 9, images);
+    return launch_pdl(im2col3x3_kernel<T>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch", x, col, H, W,
+                      OW, row0, np, ld, stride, off, xbs, cbs);
+}
+
+int im2col_any(const void* x, int x_dtype, void* col, uint32_t cin, uint32_t H, uint32_t W, uint32_t OW,
+               uint32_t row0, uint32_t nrows, uint64_t ld, uint32_t stride, int off, uint32_t images, uint64_t xbs,
+               uint64_t cbs, const LaunchEnv& env) {
+    if (x_dtype == SDVK_F32)
+        return im2col_launch(static_cast<const float*>(x), static_cast<float*>(col), cin, H, W, OW, row0, nrows, ld,
+                             stride, off, images, xbs, cbs, env);
+    if (x_dtype == SDVK_F16)
+        return im2col_launch(static_cast<const __half*>(x), static_cast<__half*>(col), cin, H, W, OW, row0, nrows, ld,
+                             stride, off, images, xbs, cbs, env);
+    return im2col_launch(static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(col), cin, H, W, OW, row0,
+                         nrows, ld, stride, off, images, xbs, cbs, env);
+}
+
 }  // namespace
 
 uint64_t conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, uint32_t stride, int dtype) {
@@ -105,21 +221,8 @@ int conv3x3_q8_ex(const void* x, int x_dtype, const int8_t* q, const float* s, c
     if (rows == OH && batch > 1 && ws_bytes / ((uint64_t)K * P * es) >= batch && P % 8 == 0) {
         // Every image's column matrix fits: one im2col launch over the images and one batched GEMM
         // (image z's columns at z*K*P, its output at z*cout*P, its bias at z*bias_stride).
-        const dim3 grid((uint32_t)((P + 8 * kColThreads - 1) / (8 * kColThreads)), K, batch);
         const uint64_t xbe = (uint64_t)cin * H * W, cbe = (uint64_t)K * P;
-        int rc;
-        if (x_dtype == SDVK_F32)
-            rc = launch_pdl(im2col3x3_kernel<float>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
-                            static_cast<const float*>(x), static_cast<float*>(workspace), H, W, OW, 0u, (uint32_t)P,
-                            P, stride, off, xbe, cbe);
-        else if (x_dtype == SDVK_F16)
-            rc = launch_pdl(im2col3x3_kernel<__half>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
-                            static_cast<const __half*>(x), static_cast<__half*>(workspace), H, W, OW, 0u, (uint32_t)P,
-                            P, stride, off, xbe, cbe);
-        else
-            rc = launch_pdl(im2col3x3_kernel<__nv_bfloat16>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
-                            static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(workspace), H, W, OW, 0u,
-                            (uint32_t)P, P, stride, off, xbe, cbe);
+        int rc = im2col_any(x, x_dtype, workspace, cin, H, W, OW, 0u, OH, P, stride, off, batch, xbe, cbe, env);
         if (rc) return rc;
         GemmQ8Desc d{};
         d.x = workspace;
@@ -148,21 +251,7 @@ int conv3x3_q8_ex(const void* x, int x_dtype, const int8_t* q, const float* s, c
         uint8_t* yb = static_cast<uint8_t*>(y) + bi * ys;
         for (uint32_t r0 = 0; r0 < OH; r0 += rows) {
             const uint32_t rr = std::min(rows, OH - r0), np = rr * OW;
-            const dim3 grid((np + 8 * kColThreads - 1) / (8 * kColThreads), K);
-            int rc;
-            if (x_dtype == SDVK_F32)
-                rc = launch_pdl(im2col3x3_kernel<float>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
-                                reinterpret_cast<const float*>(xb), static_cast<float*>(workspace), H, W, OW, r0, np,
-                                pitch, stride, off, (uint64_t)0, (uint64_t)0);
-            else if (x_dtype == SDVK_F16)
-                rc = launch_pdl(im2col3x3_kernel<__half>, grid, dim3(kColThreads), 0, env, "im2col3x3_kernel launch",
-                                reinterpret_cast<const __half*>(xb), static_cast<__half*>(workspace), H, W, OW, r0, np,
-                                pitch, stride, off, (uint64_t)0, (uint64_t)0);
-            else
-                rc = launch_pdl(im2col3x3_kernel<__nv_bfloat16>, grid, dim3(kColThreads), 0, env,
-                                "im2col3x3_kernel launch", reinterpret_cast<const __nv_bfloat16*>(xb),
-                                static_cast<__nv_bfloat16*>(workspace), H, W, OW, r0, np, pitch, stride, off,
-                                (uint64_t)0, (uint64_t)0);
+            int rc = im2col_any(xb, x_dtype, workspace, cin, H, W, OW, r0, rr, pitch, stride, off, 1u, 0, 0, env);
             if (rc) return rc;
             GemmQ8Desc d{};
             d.x = workspace;

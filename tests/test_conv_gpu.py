@@ -18,6 +18,10 @@ CONV_CASES = [
     (1, 32, 64, 16, 24, 2, 0, "f32", "f32"),
     (2, 320, 320, 32, 32, 1, -1, "f16", "f32"),  # an SDXL level-1 conv at a 256^2 latent
     (1, 96, 128, 24, 40, 2, -1, "bf16", "f32"),
+    # the row-segment im2col (OW % 8 == 0): both stride-2 paddings and an fp32 input
+    (2, 64, 64, 32, 48, 2, -1, "f16", "f32"),
+    (1, 32, 64, 32, 32, 2, 0, "bf16", "f32"),
+    (1, 32, 32, 16, 16, 1, -1, "f32", "f32"),
 ]
 _TT = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
 
