@@ -402,6 +402,10 @@ typedef struct sdvk_unet_tensor_info {
     float* f;
 } sdvk_unet_tensor_info;
 SDVK_API int sdvk_unet_create(sdvk_ctx* ctx, const sdvk_unet_desc* desc, sdvk_unet** out);
+/* The same UNet without device memory or a device (host only): its parameter table (null pointers),
+ * FLOP, launch count and the device bytes sdvk_unet_create would allocate.  Forward, init and prepare
+ * return SDVK_E_STATE on it. */
+SDVK_API int sdvk_unet_plan(const sdvk_unet_desc* desc, sdvk_unet** out);
 SDVK_API int sdvk_unet_destroy(sdvk_unet* unet);
 /* Seeded random parameters: Q8_0 weights int8 uniform in [-127, 127] with binary16 scales
  * |N(0, 0.02)|/127, linear and conv biases uniform in [-0.02, 0.02], norm weights 1 and biases 0. */
@@ -412,6 +416,7 @@ SDVK_API int sdvk_unet_tensor(const sdvk_unet* unet, uint32_t index, sdvk_unet_t
 /* Algorithmic FLOP of one pass (GEMMs, convolutions at their real input channels, attention). */
 SDVK_API uint64_t sdvk_unet_flops(const sdvk_unet* unet);
 SDVK_API uint64_t sdvk_unet_workspace_bytes(const sdvk_unet* unet);
+SDVK_API uint64_t sdvk_unet_parameter_bytes(const sdvk_unet* unet);
 /* Kernel launches of one pass (this library's kernels; the concat copies are not counted). */
 SDVK_API uint64_t sdvk_unet_launches(const sdvk_unet* unet);
 SDVK_API int sdvk_unet_forward(sdvk_ctx* ctx, sdvk_unet* unet, const float* x, const float* timesteps, const float* adm,

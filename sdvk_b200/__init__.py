@@ -176,6 +176,7 @@ SIGNATURES = {
     "sdvk_transformer_block": (_I, [_P, ctypes.POINTER(BlockDesc), _P, _U64]),
     "sdvk_transformer_block_static": (_I, [_P, ctypes.POINTER(BlockDesc)]),
     "sdvk_unet_create": (_I, [_P, ctypes.POINTER(UnetDesc), ctypes.POINTER(_P)]),
+    "sdvk_unet_plan": (_I, [ctypes.POINTER(UnetDesc), ctypes.POINTER(_P)]),
     "sdvk_unet_destroy": (_I, [_P]),
     "sdvk_unet_init_random": (_I, [_P, _P, _U64]),
     "sdvk_unet_prepare": (_I, [_P, _P]),
@@ -184,6 +185,7 @@ SIGNATURES = {
     "sdvk_unet_flops": (_U64, [_P]),
     "sdvk_unet_workspace_bytes": (_U64, [_P]),
     "sdvk_unet_launches": (_U64, [_P]),
+    "sdvk_unet_parameter_bytes": (_U64, [_P]),
     "sdvk_unet_forward": (_I, [_P, _P, _P, _P, _P, _P, _I, _P]),
 }
 

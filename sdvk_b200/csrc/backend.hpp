@@ -96,6 +96,7 @@ int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y,
                  const LaunchEnv& env);
 
 // unet.cu: the SDXL UNet pass over the kernels above.
+int unet_plan(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env);
 int unet_create(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env);
 int unet_destroy(sdvk_unet* u);
 int unet_init_random(sdvk_unet* u, uint64_t seed, const LaunchEnv& env);
@@ -105,6 +106,7 @@ int unet_forward(sdvk_unet* u, const float* x, const float* timesteps, const flo
 uint64_t unet_flops(const sdvk_unet* u);
 uint64_t unet_launches(const sdvk_unet* u);
 uint64_t unet_workspace_bytes(const sdvk_unet* u);
+uint64_t unet_parameter_bytes(const sdvk_unet* u);
 int unet_tensor(const sdvk_unet* u, uint32_t i, sdvk_unet_tensor_info* out);
 uint32_t unet_tensor_count(const sdvk_unet* u);
 

@@ -729,6 +729,12 @@ int sdvk_unet_create(sdvk_ctx* ctx, const sdvk_unet_desc* desc, sdvk_unet** out)
     return sdvk::unet_create(*desc, out, env_of(ctx));
 }
 
+int sdvk_unet_plan(const sdvk_unet_desc* desc, sdvk_unet** out) {
+    if (!desc || !out) return SDVK_E_ARG;
+    const sdvk::LaunchEnv env{nullptr, nullptr, 0, -1, 148, nullptr, SDVK_PRECISION_REFERENCE, nullptr, nullptr, nullptr};
+    return sdvk::unet_plan(*desc, out, env);
+}
+
 int sdvk_unet_destroy(sdvk_unet* unet) { return sdvk::unet_destroy(unet); }
 
 int sdvk_unet_init_random(sdvk_ctx* ctx, sdvk_unet* unet, uint64_t seed) {
@@ -754,6 +760,8 @@ uint64_t sdvk_unet_flops(const sdvk_unet* unet) { return sdvk::unet_flops(unet);
 uint64_t sdvk_unet_workspace_bytes(const sdvk_unet* unet) { return sdvk::unet_workspace_bytes(unet); }
 
 uint64_t sdvk_unet_launches(const sdvk_unet* unet) { return sdvk::unet_launches(unet); }
+
+uint64_t sdvk_unet_parameter_bytes(const sdvk_unet* unet) { return sdvk::unet_parameter_bytes(unet); }
 
 int sdvk_unet_forward(sdvk_ctx* ctx, sdvk_unet* unet, const float* x, const float* timesteps, const float* adm,
                       const void* context, int ctx_dtype, float* out) {

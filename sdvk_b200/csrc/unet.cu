@@ -205,6 +205,7 @@ struct sdvk_unet {
     std::vector<Res> res;
     std::vector<St> st;
     bool prepared = false;
+    uint64_t arena_bytes = 0;  // parameters (null arena: a plan without device memory)
     uint64_t plan[8] = {};  // workspace offsets of the pass's scratch regions (fixed at creation)
 
     int8_t* q(int i) const { return reinterpret_cast<int8_t*>(arena + t[i].q_off); }
@@ -725,7 +726,7 @@ int check_desc(const sdvk_unet_desc& d, const LaunchEnv& env) {
 
 }  // namespace
 
-int unet_create(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env) {
+int unet_plan(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env) {
     if (!out) return fail(env, SDVK_E_ARG, "null pointer");
     *out = nullptr;
     if (int rc = check_desc(d, env)) return rc;
@@ -739,12 +740,21 @@ int unet_create(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env) 
     plan.layout();
     u->flops = plan.flops;
     u->launches = plan.launches;
-    const uint64_t q0 = 0, s0 = a256(u->q_bytes), f0 = s0 + a256(u->s_bytes), total = f0 + a256(u->f_bytes);
+    const uint64_t s0 = a256(u->q_bytes), f0 = s0 + a256(u->s_bytes);
     for (U::Tensor& t : u->t) {
         t.s_off += s0;
         t.f_off += f0;
-        t.q_off += q0;
     }
+    u->arena_bytes = f0 + a256(u->f_bytes);
+    *out = u;
+    return SDVK_OK;
+}
+
+int unet_create(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env) {
+    if (int rc = unet_plan(d, out, env)) return rc;
+    U* u = *out;
+    *out = nullptr;
+    const uint64_t total = u->arena_bytes;
     if (cudaMalloc(&u->arena, total) != cudaSuccess || cudaMalloc(&u->ws, u->ws_bytes ? u->ws_bytes : 256) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(u->arena);
@@ -763,6 +773,10 @@ int unet_create(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env) 
 
 int unet_destroy(sdvk_unet* u) {
     if (!u) return SDVK_OK;
+    if (!u->arena) {  // a plan: no device memory, no CUDA call
+        delete u;
+        return SDVK_OK;
+    }
     int cur = -1;
     cudaGetDevice(&cur);
     if (cur != u->device) cudaSetDevice(u->device);
@@ -774,6 +788,7 @@ int unet_destroy(sdvk_unet* u) {
 }
 
 int unet_prepare(sdvk_unet* u, const LaunchEnv& env) {
+    if (!u->arena) return fail(env, SDVK_E_STATE, "a UNet plan has no device memory (sdvk_unet_create makes one that has)");
     for (const U::St& s : u->st)
         for (const U::Blk& k : s.blocks) {
             const uint32_t F = 4 * s.C;
@@ -786,6 +801,7 @@ int unet_prepare(sdvk_unet* u, const LaunchEnv& env) {
 }
 
 int unet_init_random(sdvk_unet* u, uint64_t seed, const LaunchEnv& env) {
+    if (!u->arena) return fail(env, SDVK_E_STATE, "a UNet plan has no device memory (sdvk_unet_create makes one that has)");
     const uint64_t total_q = [&] {
         uint64_t m = 0;
         for (const U::Tensor& t : u->t)
@@ -820,7 +836,8 @@ int unet_forward(sdvk_unet* u, const float* x, const float* timesteps, const flo
     if (!x || !timesteps || !adm || !ctx || !out) return fail(env, SDVK_E_ARG, "null pointer");
     if (ctx_dtype != SDVK_F16 && ctx_dtype != SDVK_BF16 && ctx_dtype != SDVK_F32)
         return fail(env, SDVK_E_ARG, "context dtype must be F16, BF16 or F32");
-    if (!u->prepared) return fail(env, SDVK_E_ARG, "sdvk_unet_prepare (or sdvk_unet_init_random) has not run");
+    if (!u->arena) return fail(env, SDVK_E_STATE, "a UNet plan has no device memory (sdvk_unet_create makes one that has)");
+    if (!u->prepared) return fail(env, SDVK_E_STATE, "sdvk_unet_prepare (or sdvk_unet_init_random) has not run");
     Pass p{*u, env, false};
     p.use_plan();
     p.forward(x, timesteps, adm, ctx, ctx_dtype, out);
@@ -830,6 +847,7 @@ int unet_forward(sdvk_unet* u, const float* x, const float* timesteps, const flo
 uint64_t unet_flops(const sdvk_unet* u) { return u ? u->flops : 0; }
 uint64_t unet_launches(const sdvk_unet* u) { return u ? u->launches : 0; }
 uint64_t unet_workspace_bytes(const sdvk_unet* u) { return u ? u->ws_bytes : 0; }
+uint64_t unet_parameter_bytes(const sdvk_unet* u) { return u ? u->arena_bytes : 0; }
 
 int unet_tensor(const sdvk_unet* u, uint32_t i, sdvk_unet_tensor_info* out) {
     if (!u || !out || i >= u->t.size()) return SDVK_E_ARG;
@@ -838,9 +856,10 @@ int unet_tensor(const sdvk_unet* u, uint32_t i, sdvk_unet_tensor_info* out) {
     out->kind = t.kind;
     out->rows = t.rows;
     out->cols = t.cols;
-    out->q = t.kind == SDVK_UNET_Q8 ? u->q((int)i) : nullptr;
-    out->s = t.kind == SDVK_UNET_Q8 ? u->s((int)i) : nullptr;
-    out->f = t.kind == SDVK_UNET_F32 ? u->f((int)i) : nullptr;
+    const bool dev = u->arena != nullptr;
+    out->q = dev && t.kind == SDVK_UNET_Q8 ? u->q((int)i) : nullptr;
+    out->s = dev && t.kind == SDVK_UNET_Q8 ? u->s((int)i) : nullptr;
+    out->f = dev && t.kind == SDVK_UNET_F32 ? u->f((int)i) : nullptr;
     return SDVK_OK;
 }
 

@@ -19,18 +19,50 @@ SDXL = dict(model_ch=(320, 640, 1280), depth=(0, 2, 10), ctx_dim=2048, adm_dim=2
             Tctx=77)
 
 
+def _desc(batch: int, H: int, W: int, arch: dict) -> UnetDesc:
+    d = UnetDesc()
+    d.model_ch[:] = list(arch["model_ch"])
+    d.depth[:] = list(arch["depth"])
+    for k in ("ctx_dim", "adm_dim", "temb_dim", "head_dim", "Tctx"):
+        setattr(d, k, arch[k])
+    d.batch, d.H, d.W = batch, H, W
+    return d
+
+
+def plan(batch: int, H: int, W: int, **arch) -> dict:
+    """The UNet's plan without a device (sdvk_unet_plan): {"tensors": {name: (kind, rows, cols)},
+    "flops", "launches", "workspace_bytes", "parameter_bytes"}; internal groups (names in
+    parentheses) are left out of "tensors"."""
+    a = dict(SDXL)
+    a.update(arch)
+    h = ctypes.c_void_p()
+    st = lib().sdvk_unet_plan(ctypes.byref(_desc(batch, H, W, a)), ctypes.byref(h))
+    if st != 0:
+        from . import SdvkError
+
+        raise SdvkError(st, "sdvk_unet_plan rejected the description")
+    try:
+        tensors = {}
+        for i in range(lib().sdvk_unet_tensor_count(h)):
+            info = UnetTensorInfo()
+            lib().sdvk_unet_tensor(h, i, ctypes.byref(info))
+            name = info.name.decode()
+            if not name.startswith("("):
+                tensors[name] = (info.kind, info.rows, info.cols)
+        return {"tensors": tensors, "flops": int(lib().sdvk_unet_flops(h)), "launches": int(lib().sdvk_unet_launches(h)),
+                "workspace_bytes": int(lib().sdvk_unet_workspace_bytes(h)),
+                "parameter_bytes": int(lib().sdvk_unet_parameter_bytes(h))}
+    finally:
+        lib().sdvk_unet_destroy(h)
+
+
 class Unet:
     def __init__(self, batch: int, H: int, W: int, device: int = 0, **arch):
         a = dict(SDXL)
         a.update(arch)
         self.arch = a
         self.batch, self.H, self.W = batch, H, W
-        d = UnetDesc()
-        d.model_ch[:] = list(a["model_ch"])
-        d.depth[:] = list(a["depth"])
-        for k in ("ctx_dim", "adm_dim", "temb_dim", "head_dim", "Tctx"):
-            setattr(d, k, a[k])
-        d.batch, d.H, d.W = batch, H, W
+        d = _desc(batch, H, W, a)
         self.desc = d
         with torch.cuda.device(device):
             self.ctx = context(torch.device("cuda", device))
