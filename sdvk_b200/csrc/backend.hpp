@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -59,6 +60,10 @@ int layernorm(const float* x, const float* gamma, const float* beta, void* y, in
 int geglu(const void* h, void* y, uint32_t rows, uint32_t F, uint64_t ldh, uint64_t ldy, const LaunchEnv& env);
 uint64_t block_workspace_bytes(const sdvk_block_desc& d);
 int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, const LaunchEnv& env);
+// The block with the cross-attention's K|V already projected by the caller: kv_pre [batch][Tctx][ld_kv]
+// fp16 holding this block's K at columns 0..C-1 and V at C..2C-1 (no K|V GEMM, no side-stream fork).
+int transformer_block_ex(const sdvk_block_desc& d, const __half* kv_pre, uint64_t ld_kv, void* ws, uint64_t ws_bytes,
+                         const LaunchEnv& env);
 int static_scratch(int device, void** ptr, const LaunchEnv& env);
 int cfg_combine(const float* cond, const float* uncond, float* out, uint64_t n, float cfg, float rescale,
                 const LaunchEnv& env);

@@ -308,6 +308,11 @@ sdvk_attn_desc attn_desc(const __half* q, uint64_t ldq, uint64_t sq, const __hal
 uint64_t block_workspace_bytes(const sdvk_block_desc& d) { return block_layout(d).total; }
 
 int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, const LaunchEnv& env) {
+    return transformer_block_ex(d, nullptr, 0, ws, ws_bytes, env);
+}
+
+int transformer_block_ex(const sdvk_block_desc& d, const __half* kv_pre, uint64_t ld_kv, void* ws, uint64_t ws_bytes,
+                         const LaunchEnv& env) {
     if (!d.x || !ws) return fail(env, SDVK_E_ARG, "null pointer");
     if (d.batch == 0 || d.T == 0) return SDVK_OK;
     if (d.heads == 0 || d.C % d.heads || d.C / d.heads > 64)
@@ -332,13 +337,15 @@ int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, con
     const sdvk_q8_linear kv_w[2] = {d.k2, d.v2};
     LaunchEnv side = env;
     side.stream = env.side;
-    const bool fork = crow && env.side && env.fork && env.join;
+    const bool fork = crow && !kv_pre && env.side && env.fork && env.join;
     if (fork) {
         if ((rc = cuda_check(env, cudaEventRecord(env.fork, env.stream), "fork"))) return rc;
         if ((rc = cuda_check(env, cudaStreamWaitEvent(env.side, env.fork, 0), "fork"))) return rc;
     }
     const LaunchEnv& kv_env = fork ? side : env;
-    if (crow && kv_split(crow, d.Cctx) && contiguous(kv_w, 2, C, d.Cctx) && C % 2 == 0) {
+    if (kv_pre) {
+        // K|V precomputed by the caller (the context is the same for every block): nothing to fork
+    } else if (crow && kv_split(crow, d.Cctx) && contiguous(kv_w, 2, C, d.Cctx) && C % 2 == 0) {
         if ((rc = kv_linear_split(d.ctx, d.ctx_dtype, d.Cctx, kv_w, C, d.Cctx, kv2, 2ull * C, crow,
                                   reinterpret_cast<float*>(base + L.part), kv_env)))
             return rc;
@@ -359,8 +366,12 @@ int transformer_block(const sdvk_block_desc& d, void* ws, uint64_t ws_bytes, con
     if ((rc = layernorm(d.x, d.ln2_w, d.ln2_b, n, SDVK_F16, rows, C, C, C, eps, env))) return rc;
     if ((rc = gemm_q8(linear_desc(n, SDVK_F16, C, d.q2, C, C, q2, SDVK_F16, C, rows, false), env))) return rc;
     if (fork && (rc = cuda_check(env, cudaStreamWaitEvent(env.stream, env.join, 0), "join"))) return rc;
-    at = attn_desc(q2, C, (uint64_t)d.T * C, kv2, kv2 + C, 2ull * C, (uint64_t)d.Tctx * 2 * C, a, C, (uint64_t)d.T * C,
-                   d.batch, H, d.T, d.Tctx, hd);
+    if (kv_pre)
+        at = attn_desc(q2, C, (uint64_t)d.T * C, kv_pre, kv_pre + C, ld_kv, (uint64_t)d.Tctx * ld_kv, a, C,
+                       (uint64_t)d.T * C, d.batch, H, d.T, d.Tctx, hd);
+    else
+        at = attn_desc(q2, C, (uint64_t)d.T * C, kv2, kv2 + C, 2ull * C, (uint64_t)d.Tctx * 2 * C, a, C,
+                       (uint64_t)d.T * C, d.batch, H, d.T, d.Tctx, hd);
     if ((rc = attention(at, env))) return rc;
     if ((rc = gemm_q8(linear_desc(a, SDVK_F16, C, d.o2, C, C, d.x, SDVK_F32, C, rows, true), env))) return rc;
     // ---- GEGLU feed-forward

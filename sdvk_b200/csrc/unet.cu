@@ -114,6 +114,57 @@ __global__ void __launch_bounds__(256) transpose_f16_kernel(const TI* __restrict
     }
 }
 
+// C[m][n] (=|+=) sum_k X[m][k] * (q[n][k] * s[(n*K + k) >> 5]) (+ bias[n]) for M <= 4 rows of fp32 X
+// (the time/label MLPs and the ResBlocks' emb projection, M = batch): X staged in shared memory, one
+// warp per weight row, lanes on 4 consecutive int8 each, weights streamed once (HBM-bound).
+template <int M>
+__global__ void __launch_bounds__(256) gemv_q8_kernel(const float* __restrict__ X, const int8_t* __restrict__ q,
+                                                      const float* __restrict__ s, const float* __restrict__ bias,
+                                                      float* __restrict__ C, uint32_t N, uint32_t K, uint64_t ldc,
+                                                      int acc) {
+    extern __shared__ float4 xs4[];
+    float* xs = reinterpret_cast<float*>(xs4);
+    grid_dependency_wait();
+    grid_launch_dependents();
+    for (uint32_t i = threadIdx.x; i < M * K; i += blockDim.x) xs[i] = X[i];
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31, warps = blockDim.x / 32;
+    for (uint32_t n = blockIdx.x * warps + threadIdx.x / 32; n < N; n += gridDim.x * warps) {
+        float a[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) a[m] = 0.0f;
+        const int8_t* qr = q + (uint64_t)n * K;
+        const uint64_t sbase = (uint64_t)n * K;
+        for (uint32_t k0 = 4 * lane; k0 < K; k0 += 128) {
+            const int w4 = __ldg(reinterpret_cast<const int*>(qr + k0));
+            const float sc = __ldg(s + ((sbase + k0) >> 5));
+            const float w[4] = {(float)(int8_t)(w4 & 0xFF) * sc, (float)(int8_t)((w4 >> 8) & 0xFF) * sc,
+                                (float)(int8_t)((w4 >> 16) & 0xFF) * sc, (float)(int8_t)(w4 >> 24) * sc};
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                const float4 x = *reinterpret_cast<const float4*>(xs + m * K + k0);
+                a[m] = fmaf(x.x, w[0], a[m]);
+                a[m] = fmaf(x.y, w[1], a[m]);
+                a[m] = fmaf(x.z, w[2], a[m]);
+                a[m] = fmaf(x.w, w[3], a[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) a[m] += __shfl_xor_sync(0xffffffffu, a[m], o);
+        }
+        if (lane == 0) {
+            const float b = bias ? bias[n] : 0.0f;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                float* c = C + (uint64_t)m * ldc + n;
+                *c = (acc ? *c : 0.0f) + (a[m] + b);
+            }
+        }
+    }
+}
+
 // ---- seeded random parameters (SplitMix64 per element: independent of launch shape)
 __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z += 0x9E3779B97F4A7C15ull;
@@ -185,6 +236,7 @@ struct sdvk_unet {
     struct St {
         uint32_t C;
         int gnw, gnb;
+        int kv = -1;  // every block's attn2 to_k | to_v, back to back: [depth * 2C][ctx_dim]
         Lin proj_in, proj_out;
         std::vector<Blk> blocks;
     };
@@ -206,7 +258,7 @@ struct sdvk_unet {
     std::vector<St> st;
     bool prepared = false;
     uint64_t arena_bytes = 0;  // parameters (null arena: a plan without device memory)
-    uint64_t plan[8] = {};  // workspace offsets of the pass's scratch regions (fixed at creation)
+    uint64_t plan[9] = {};  // workspace offsets of the pass's scratch regions (fixed at creation)
 
     int8_t* q(int i) const { return reinterpret_cast<int8_t*>(arena + t[i].q_off); }
     float* s(int i) const { return reinterpret_cast<float*>(arena + t[i].s_off); }
@@ -332,6 +384,7 @@ void build(U& u) {
         s.C = C;
         R.norm(p + ".norm", C, s.gnw, s.gnb);
         s.proj_in = R.lin(p + ".proj_in", C, C);
+        s.kv = R.add_q8("(" + p + " attn2 K|V group)", depth * 2 * C, d.ctx_dim);
         for (uint32_t i = 0; i < depth; ++i) {
             const std::string b = p + ".transformer_blocks." + std::to_string(i);
             U::Blk k{};
@@ -345,9 +398,8 @@ void build(U& u) {
             k.v.w = R.view(b + ".attn1.to_v.weight", qkv, 2 * C, C);
             k.o = R.lin(b + ".attn1.to_out.0", C, C);
             k.q2 = R.lin(b + ".attn2.to_q", C, C, false);
-            const int kv = R.add_q8("(" + b + ".attn2.kv group)", 2 * C, d.ctx_dim);
-            k.k2.w = R.view(b + ".attn2.to_k.weight", kv, 0, C);
-            k.v2.w = R.view(b + ".attn2.to_v.weight", kv, C, C);
+            k.k2.w = R.view(b + ".attn2.to_k.weight", s.kv, 2 * C * i, C);
+            k.v2.w = R.view(b + ".attn2.to_v.weight", s.kv, 2 * C * i + C, C);
             k.o2 = R.lin(b + ".attn2.to_out.0", C, C);
             k.ff1 = R.lin(b + ".ff.net.0.proj", 8 * C, C);
             k.ff1_il_q = R.add_q8("(" + b + ".ff.net.0.proj interleaved)", 8 * C, C);
@@ -396,7 +448,8 @@ struct Pass {
     // workspace plan: bump region for module outputs + fixed scratch regions sized to their maxima
     uint64_t bump = 0;
     uint64_t need_h16 = 0, need_h32 = 0, need_col = 0, need_gn = 0, need_blk = 0, need_tok = 0, need_small = 0;
-    uint64_t o_h16 = 0, o_h32 = 0, o_col = 0, o_gn = 0, o_blk = 0, o_tok = 0, o_small = 0, o_bump = 0;
+    uint64_t need_kv = 0;
+    uint64_t o_h16 = 0, o_h32 = 0, o_col = 0, o_gn = 0, o_blk = 0, o_tok = 0, o_small = 0, o_bump = 0, o_kv = 0;
     uint64_t flops = 0;
     uint64_t launches = 0;  // kernels of this library per pass (memcpy nodes not counted)
     int rc = SDVK_OK;
@@ -466,6 +519,20 @@ struct Pass {
         flops += 2ull * rows * w.rows * K;
         ++launches;
         if (dry || !ok()) return;
+        const float* bias = bias_override ? bias_override : u.f(l.b);
+        if (a_dtype == SDVK_F32 && rows <= 4 && K % 4 == 0 && (uint64_t)rows * K * 4 <= 48 * 1024) {
+            // few rows: stream the weight once (gemv_q8_kernel) instead of tensor-core tiles
+            const uint32_t grid = (uint32_t)std::min<uint64_t>((w.rows + 7) / 8, (uint64_t)env.num_sms * 4);
+            const size_t smem = (size_t)rows * K * 4;
+            const float* X = static_cast<const float*>(a);
+            const int8_t* wq = u.q(l.w);
+            const float* wsc = u.s(l.w);
+            auto kern = rows == 1 ? gemv_q8_kernel<1> : rows == 2 ? gemv_q8_kernel<2>
+                                  : rows == 3 ? gemv_q8_kernel<3> : gemv_q8_kernel<4>;
+            run(launch_pdl(kern, dim3(grid), dim3(256), smem, env, "gemv_q8_kernel launch", X, wq, wsc, bias, c,
+                           w.rows, K, ldc, (int)acc));
+            return;
+        }
         GemmQ8Desc g{};
         g.x = a;
         g.x_dtype = a_dtype;
@@ -473,7 +540,7 @@ struct Pass {
         g.wq = u.q(l.w);
         g.ws = u.s(l.w);
         g.ldw = K;
-        g.bias = bias_override ? bias_override : u.f(l.b);
+        g.bias = bias;
         g.c = c;
         g.c_dtype = SDVK_F32;
         g.ldc = ldc;
@@ -537,6 +604,30 @@ struct Pass {
         transpose(g16, a16, C, P);  // [B][C][P] -> [B][P][C]
         float* t = scratch<float>(need_h32, o_h32, (uint64_t)B * P * C * 4);
         linear(a16, SDVK_F16, B * P, C, s.proj_in, t, C, false);
+        // every block's cross-attention K|V from the context at once (the context is the same for all):
+        // kv [B * Tctx][depth * 2C] fp16, block i's K at columns 2C*i, its V at 2C*i + C
+        const uint32_t depth = (uint32_t)s.blocks.size(), crow = B * u.d.Tctx, nkv = depth * 2 * C;
+        __half* kv = scratch<__half>(need_kv, o_kv, (uint64_t)crow * nkv * 2);
+        flops += 2ull * crow * nkv * u.d.ctx_dim;
+        ++launches;
+        if (!dry && ok()) {
+            GemmQ8Desc g{};
+            g.x = ctx;
+            g.x_dtype = ctx_dtype;
+            g.ldx = u.d.ctx_dim;
+            g.wq = u.q(s.kv);
+            g.ws = u.s(s.kv);
+            g.ldw = u.d.ctx_dim;
+            g.c = kv;
+            g.c_dtype = SDVK_F16;
+            g.ldc = nkv;
+            g.xrows = crow;
+            g.wrows = nkv;
+            g.K = u.d.ctx_dim;
+            g.batch = 1;
+            run(gemm_q8(g, env));
+        }
+        uint32_t bi = 0;
         for (const U::Blk& k : s.blocks) {
             sdvk_block_desc bd{};
             bd.x = t;
@@ -553,10 +644,10 @@ struct Pass {
             const uint64_t wsb = block_workspace_bytes(bd);
             void* bws = scratch<void>(need_blk, o_blk, wsb);
             const uint64_t T = P, Tc = u.d.Tctx, F = 4ull * C;
-            launches += 13;  // 3 LayerNorms, 7 GEMMs (QKV fused, GEGLU in FF1), the K|V reduce, 2 attentions
-            flops += 2ull * B * (T * 3 * C * C + T * C * C + T * C * C + Tc * 2 * C * u.d.ctx_dim + T * C * C +
-                                 T * 2 * F * C + T * C * F) +
+            launches += 11;  // 3 LayerNorms, 6 GEMMs (QKV fused, GEGLU in FF1), 2 attentions
+            flops += 2ull * B * (T * 3 * C * C + T * C * C + T * C * C + T * C * C + T * 2 * F * C + T * C * F) +
                      4ull * B * T * T * C + 4ull * B * T * Tc * C;
+            const uint32_t i = bi++;
             if (dry || !ok()) continue;
             bd.ln1_w = u.f(k.ln[0]), bd.ln1_b = u.f(k.ln[1]);
             bd.ln2_w = u.f(k.ln[2]), bd.ln2_b = u.f(k.ln[3]);
@@ -567,7 +658,7 @@ struct Pass {
             bd.ff1 = sdvk_q8_linear{u.q(k.ff1_il_q), u.s(k.ff1_il_q), u.f(k.ff1_il_q + 1)};
             bd.ff1_geglu_interleaved = 1;
             bd.ff2 = L(k.ff2);
-            run(transformer_block(bd, bws, wsb, env));
+            run(transformer_block_ex(bd, kv + (uint64_t)i * 2 * C, nkv, bws, wsb, env));
         }
         __half* u16 = scratch<__half>(need_tok, o_tok, (uint64_t)B * P * C * 2);
         transpose(t, u16, P, C);  // [B][P][C] fp32 -> [B][C][P] fp16
@@ -700,13 +791,14 @@ struct Pass {
         put(o_tok, need_tok);
         put(o_small, need_small);
         put(o_bump, bump);
+        put(o_kv, need_kv);
         u.ws_bytes = o;
-        const uint64_t v[8] = {o_h16, o_h32, o_col, o_gn, o_blk, o_tok, o_small, o_bump};
+        const uint64_t v[9] = {o_h16, o_h32, o_col, o_gn, o_blk, o_tok, o_small, o_bump, o_kv};
         std::memcpy(u.plan, v, sizeof v);
     }
     void use_plan() {
         o_h16 = u.plan[0], o_h32 = u.plan[1], o_col = u.plan[2], o_gn = u.plan[3];
-        o_blk = u.plan[4], o_tok = u.plan[5], o_small = u.plan[6], o_bump = u.plan[7];
+        o_blk = u.plan[4], o_tok = u.plan[5], o_small = u.plan[6], o_bump = u.plan[7], o_kv = u.plan[8];
     }
 };
 
