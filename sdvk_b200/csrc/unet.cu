@@ -495,8 +495,9 @@ struct Pass {
             run(conv3x3_q8_ex(x, SDVK_F16, u.q(l.w), u.s(l.w), bias ? bias : u.f(l.b), bias ? bias_stride : 0, acc, y,
                               SDVK_F32, B, cin, cout, H, W, stride, -1, col, wsb, env));
     }
-    void copy(float* dst, const float* src, uint64_t floats) {
-        if (!dry && ok()) run(cuda_check(env, cudaMemcpyAsync(dst, src, floats * 4, cudaMemcpyDeviceToDevice, env.stream), "copy"));
+    void copy(float* dst, const float* src, uint64_t floats, const LaunchEnv* on = nullptr) {
+        const LaunchEnv& e = on ? *on : env;
+        if (!dry && ok()) run(cuda_check(e, cudaMemcpyAsync(dst, src, floats * 4, cudaMemcpyDeviceToDevice, e.stream), "copy"));
     }
     void to_f16(const float* x, __half* y, uint32_t Cin, uint32_t Cout, uint32_t H, uint32_t W, uint32_t up) {
         const uint64_t n = (uint64_t)u.d.batch * Cout * (H << up) * (W << up);
@@ -553,7 +554,7 @@ struct Pass {
     }
     // 1x1 convolution, channel-major: y[b] (=|+=) W x[b] (+ bias), x in a_dtype [B][cin][P]
     void conv1x1(const void* x, int x_dtype, const U::Lin& l, uint32_t cin, uint32_t cout, uint32_t P, float* y,
-                 bool acc) {
+                 bool acc, const LaunchEnv* on = nullptr) {
         const uint32_t B = u.d.batch;
         flops += 2ull * B * P * cout * cin;
         ++launches;
@@ -578,20 +579,32 @@ struct Pass {
         g.batch = B;
         g.nn = true;
         g.accumulate = acc;
-        run(gemm_q8(g, env));
+        run(gemm_q8(g, on ? *on : env));
     }
 
     // resBlock (sdvkgen.cpp:1669-1707)
     float* resblock(const float* x, const U::Res& r, uint32_t H, uint32_t W, const float* ebias) {
         const uint32_t B = u.d.batch, P = H * W;
+        // The skip path (x itself, or the 1x1 conv) depends on x alone: it runs on the context's side
+        // stream, forked here and joined before conv2 reduce-adds into its output, so its tensor work
+        // overlaps the memory-bound GroupNorm and im2col passes of the main path.
+        float* out = out_buf((uint64_t)B * r.cout * P);
+        const bool fork = !dry && ok() && env.side && env.fork && env.join;
+        LaunchEnv side = env;
+        side.stream = env.side;
+        if (fork) {
+            run(cuda_check(env, cudaEventRecord(env.fork, env.stream), "fork"));
+            run(cuda_check(env, cudaStreamWaitEvent(env.side, env.fork, 0), "fork"));
+        }
+        if (r.cin == r.cout) copy(out, x, (uint64_t)B * r.cout * P, fork ? &side : nullptr);
+        else conv1x1(x, SDVK_F32, r.skip, r.cin, r.cout, P, out, false, fork ? &side : nullptr);
+        if (fork) run(cuda_check(env, cudaEventRecord(env.join, env.side), "join"));
         __half* h16 = gn16(x, r.gn1w, r.gn1b, r.cin, P, 1e-5f, true);
         float* h = scratch<float>(need_h32, o_h32, (uint64_t)B * r.cout * P * 4);
         conv(h16, r.conv1, r.cin, r.cout, H, W, 1, h, dry ? nullptr : ebias + r.emb_off, u.emb_rows, false);
         flops += 2ull * B * r.cout * u.d.temb_dim;  // its share of the emb GEMM
         __half* g16 = gn16(h, r.gn2w, r.gn2b, r.cout, P, 1e-5f, true);
-        float* out = out_buf((uint64_t)B * r.cout * P);
-        if (r.cin == r.cout) copy(out, x, (uint64_t)B * r.cout * P);
-        else conv1x1(x, SDVK_F32, r.skip, r.cin, r.cout, P, out, false);
+        if (fork) run(cuda_check(env, cudaStreamWaitEvent(env.stream, env.join, 0), "join"));
         conv(g16, r.conv2, r.cout, r.cout, H, W, 1, out, nullptr, 0, true);
         return out;
     }
