@@ -2,16 +2,23 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sdvk|reference] [--workload NAME]
 
-Workloads (synthetic seeded inputs of the stated shapes):
-  gemm             (default) Q8_0 dequant GEMM Y[9216,1280] = X[9216,1280] . dequant(W[1280,1280])^T,
-                   fp16 X, GGUF Q8_0 W (int8 + per-32 scale), fp32 Y
-  block            one SDXL BasicTransformerBlock, batch 2 x 1024 tokens x 1280 channels (13 launches)
-  attn-self-4096   fused attention, batch 2, 4096 tokens, 10 heads x 64, fp16
-  attn-self-1024   fused attention, batch 2, 1024 tokens, 20 heads x 64, fp16
-  attn-cross-77    fused attention, batch 2, 1024 queries x 77 keys, 20 heads x 64, fp16
+Workloads (synthetic seeded inputs of the stated shapes, random-init Q8_0 weights):
+  unet             (default) one SDXL 1024^2 CFG denoising step: the whole UNet pass over the
+                   cond/uncond pair (batch 2, 4x128x128 latent, 77x2048 context) + the device sampler
+                   step (Euler, cfg 5.0, v-pred); metric images/s at 20 steps per image (configs 3/4:
+                   --gpus N runs N independent images)
+  unet-cfg-pair    the same step with the CFG halves on a GPU pair (NCCL all-gather), --gpus even
+  gemm             Q8_0 dequant GEMM Y[9216,1280] = X[9216,1280] . dequant(W[1280,1280])^T,
+                   fp16 X, GGUF Q8_0 W (int8 + per-32 scale), fp32 Y (config 0)
+  block            one SDXL BasicTransformerBlock, batch 2 x 1024 tokens x 1280 channels (config 2)
+  attn-self-4096   fused attention, batch 2, 4096 tokens, 10 heads x 64, fp16 (config 1a)
+  attn-self-1024   fused attention, batch 2, 1024 tokens, 20 heads x 64, fp16 (config 1b)
+  attn-cross-77    fused attention, batch 2, 1024 queries x 77 keys, 20 heads x 64, fp16 (config 1c)
+  conv, groupnorm, sampler   the next-row kernels at SDXL level-0 shapes
 
-One step = one launch of the hot-path kernel (for `block`, the block's 13 launches) over one set of
-inputs.  Rotating input/output sets
+One step = one launch of the hot-path kernel (for `block`, the block's launches; for `unet`, a
+denoising step of about 1030 launches replayed from one CUDA graph) over one set of inputs.
+Rotating input/output sets
 whose total exceeds the 126 MB L2 keep every step's operands out of L2.  Steps are captured in CUDA
 graphs and replayed; the timed region is bracketed by a barrier and a device synchronize and timed
 with CUDA events on the launching stream; the job time is the max over ranks.  Multi-GPU runs are
@@ -671,7 +678,8 @@ class UnetWorkload:
                          "4x128x128 fp32 ~N(0,1), context 2x77x2048 fp16 ~N(0,1), adm N(0,1); one step = UNet pass "
                          "+ sdvk_sampler_step (Euler, cfg 5.0, v-pred)")
         self.rotate = 1
-        self.l2_note = "one UNet pass moves ~3 GB of Q8_0 weights and several GB of activations per step (>> 126 MB L2)"
+        self.l2_note = ("one UNet pass reads 2.9 GB of Q8_0 weights and scales and several GB of activations per "
+                        "step (>> 126 MB L2)")
         self.cpu_units = 9216
         self.cpu_what = ("rows of the 9216x1280x1280 Q8_0 GEMM (fp32 restatement of gemm_nt_q8_v.comp, the pass's "
                          "dominant arithmetic), converted to images/s at the pass's FLOP per image")
@@ -685,8 +693,12 @@ class UnetWorkload:
             self.unet.init_random(3)
             self.flop = float(self.unet.flops)
             self.launches_per_step = self.unet.launches + 2  # + the sampler's guide and update passes
-            # weights once per pass plus the activations' fp32 writes and reads (order of magnitude)
-            self.bytes = 3.0e9
+            # lower bound of the pass's DRAM traffic: every Q8_0 weight (int8 + fp32 scale per 32) read once
+            from sdvk_b200 import UNET_Q8
+            from sdvk_b200.unet import plan
+
+            tens = plan(self.B, self.H, self.W)["tensors"].values()
+            self.bytes = float(sum(r * c * 1.125 for kind, r, c in tens if kind == UNET_Q8))
 
     def make_set(self, torch, device, seed):
         self._ensure(torch, device)
@@ -917,7 +929,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: about 1 s of GPU work)")
     ap.add_argument("--warmup", type=int, default=100)
     ap.add_argument("--impl", default="sdvk", choices=["sdvk", "reference"])
-    ap.add_argument("--workload", default="gemm", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="unet", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
