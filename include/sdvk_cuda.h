@@ -383,7 +383,10 @@ SDVK_API int sdvk_check_finite(sdvk_ctx* ctx, const void* x, int dtype, uint64_t
  * SDXL: model_ch {320, 640, 1280}, depth {0, 2, 10}, ctx_dim 2048, adm_dim 2816, temb_dim 1280,
  * head_dim 64, Tctx 77.  H and W must be multiples of 4.  The latent's 4 input channels run as 32
  * (zero-padded): "input_blocks.0.0.weight" is [ch0][32*9] and its columns past 4*9 must stay zero.
- * After parameters change, sdvk_unet_prepare redoes the load-time repacks (GEGLU interleave). */
+ * After parameters change, sdvk_unet_prepare redoes the load-time repacks (GEGLU interleave).
+ * Every pass of one UNet uses the same workspace (fixed addresses, so a captured pass replays): passes
+ * of one UNet that can overlap on the GPU race; run them on one stream, or create a UNet per stream.
+ * The context must be on the device the UNet was created on (SDVK_E_ARG otherwise). */
 typedef struct sdvk_unet sdvk_unet;
 typedef struct sdvk_unet_desc {
     uint32_t model_ch[3];

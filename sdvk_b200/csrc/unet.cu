@@ -892,7 +892,16 @@ int unet_destroy(sdvk_unet* u) {
     return SDVK_OK;
 }
 
+// a UNet's memory lives on the device it was created on; work for it must come from a context there
+static int same_device(const sdvk_unet* u, const LaunchEnv& env) {
+    if (u->arena && env.device != u->device)
+        return fail(env, SDVK_E_ARG, "the context's device (" + std::to_string(env.device) + ") is not the UNet's (" +
+                                         std::to_string(u->device) + ")");
+    return SDVK_OK;
+}
+
 int unet_prepare(sdvk_unet* u, const LaunchEnv& env) {
+    if (int rc = same_device(u, env)) return rc;
     if (!u->arena) return fail(env, SDVK_E_STATE, "a UNet plan has no device memory (sdvk_unet_create makes one that has)");
     for (const U::St& s : u->st)
         for (const U::Blk& k : s.blocks) {
@@ -906,6 +915,7 @@ int unet_prepare(sdvk_unet* u, const LaunchEnv& env) {
 }
 
 int unet_init_random(sdvk_unet* u, uint64_t seed, const LaunchEnv& env) {
+    if (int rc = same_device(u, env)) return rc;
     if (!u->arena) return fail(env, SDVK_E_STATE, "a UNet plan has no device memory (sdvk_unet_create makes one that has)");
     const uint64_t total_q = [&] {
         uint64_t m = 0;
@@ -939,6 +949,7 @@ int unet_init_random(sdvk_unet* u, uint64_t seed, const LaunchEnv& env) {
 int unet_forward(sdvk_unet* u, const float* x, const float* timesteps, const float* adm, const void* ctx, int ctx_dtype,
                  float* out, const LaunchEnv& env) {
     if (!x || !timesteps || !adm || !ctx || !out) return fail(env, SDVK_E_ARG, "null pointer");
+    if (int rc = same_device(u, env)) return rc;
     if (ctx_dtype != SDVK_F16 && ctx_dtype != SDVK_BF16 && ctx_dtype != SDVK_F32)
         return fail(env, SDVK_E_ARG, "context dtype must be F16, BF16 or F32");
     if (!u->arena) return fail(env, SDVK_E_STATE, "a UNet plan has no device memory (sdvk_unet_create makes one that has)");
