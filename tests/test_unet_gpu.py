@@ -220,3 +220,30 @@ def test_unet_rejects_bad_shapes():
         Unet(2, 18, 16, device=0, **SMALL)  # latent sides must be multiples of 4
     with pytest.raises(sdvk_b200.SdvkError):
         Unet(2, 16, 16, device=0, **dict(SMALL, model_ch=(48, 128, 192)))  # 48 is not a multiple of head_dim
+
+
+def test_unet_error_paths():
+    """A device-less plan cannot run a pass (SDVK_E_STATE), and a UNet whose parameters were never
+    prepared refuses to run rather than reading uninitialised repacks."""
+    import ctypes
+
+    import sdvk_b200
+    from sdvk_b200 import lib
+    from sdvk_b200.torch_ops import context
+    from sdvk_b200.unet import Unet, _desc
+
+    dev = torch.device("cuda", 0)
+    x, t, adm, ctx = _inputs(SMALL, 2, 16, 16, 3, dev)
+    out = torch.empty_like(x)
+    h = ctypes.c_void_p()
+    assert lib().sdvk_unet_plan(ctypes.byref(_desc(2, 16, 16, dict(SMALL))), ctypes.byref(h)) == sdvk_b200.OK
+    c = context(dev)
+    st = lib().sdvk_unet_forward(c.handle, h, x.data_ptr(), t.data_ptr(), adm.data_ptr(), ctx.data_ptr(),
+                                 sdvk_b200.F16, out.data_ptr())
+    assert st == sdvk_b200.E_STATE
+    lib().sdvk_unet_destroy(h)
+    u = Unet(2, 16, 16, device=0, **SMALL)  # created, never initialised or prepared
+    with pytest.raises(sdvk_b200.SdvkError) as e:
+        u.forward(x, t, adm, ctx)
+    assert e.value.status == sdvk_b200.E_STATE
+    u.close()
