@@ -116,6 +116,22 @@ void orc_mt19937_uniform_int(void* h, int32_t lo, int32_t hi, int32_t* out, uint
     for (uint64_t i = 0; i < n; ++i) out[i] = d(r);
 }
 
+// The generation loop's noise source (src/Modules/Diffusion/sdvkgen.cpp:3732-3734, draws at :3869,
+// :3946, :3996): one std::mt19937(seed) and one std::normal_distribution<float>(0, 1) kept for the
+// whole run, so the initial latent and every ancestral step's draws continue one sequence (the
+// distribution object carries its second polar-method value from call to call).
+struct OrcGenRng {
+    std::mt19937 rng;
+    std::normal_distribution<float> nd{0.0f, 1.0f};
+    explicit OrcGenRng(uint32_t seed) : rng(seed) {}
+};
+void* orc_gen_rng_new(uint32_t seed) { return new OrcGenRng(seed); }
+void orc_gen_rng_free(void* h) { delete (OrcGenRng*)h; }
+void orc_gen_rng_normal(void* h, float* out, uint64_t n) {
+    OrcGenRng& g = *(OrcGenRng*)h;
+    for (uint64_t i = 0; i < n; ++i) out[i] = g.nd(g.rng);
+}
+
 void orc_normal_f32(uint64_t seed, uint64_t stream, float std_dev, float* out, uint64_t n) {
     uint64_t key = stream_key(seed, stream);
 #pragma omp parallel for schedule(static)

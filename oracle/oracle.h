@@ -114,6 +114,46 @@ typedef struct orc_sampler_args {
 } orc_sampler_args;
 uint64_t orc_sampler_eval(const orc_sampler_args* a);
 
+/* ---- the rest of the reference's kernel table (refkernels.cpp) -------------------------------- */
+/* Push-constant blocks as the walker fills them (Pg, Pnd: sdvkgen.cpp:901-907; the ew2 block of mul2 :1003-1019). */
+typedef struct orc_pg {
+    uint32_t M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, pad;
+} orc_pg;
+typedef struct orc_pnd {
+    uint32_t n, d0, d1, d2, d3, os0, os1, os2, os3, ss0, ss1, ss2, ss3, mode;
+    float scale;
+} orc_pnd;
+typedef struct orc_pew2 {
+    uint32_t n, d0, d1, d2, d3, as0, as1, as2, as3, bs0, bs1, bs2, bs3, mode;
+} orc_pew2;
+void orc_add2_shader(float* c, const float* a, const float* b, uint32_t n);
+void orc_bias_add_shader(float* x, const float* b, uint32_t C, uint32_t P);
+void orc_copy_nd_shader(float* d, const float* s, const orc_pnd* p);
+void orc_ew2_shader(float* c, const float* a, const float* b, const orc_pew2* p);
+void orc_unary_shader(const float* x, float* y, uint32_t n, uint32_t mode);
+void orc_upsample2x_shader(const float* x, float* y, uint32_t C, uint32_t H, uint32_t W);
+void orc_im2col_shader(const float* x, float* col, uint32_t C, uint32_t H, uint32_t W, uint32_t row0, uint32_t rows);
+void orc_im2col_s2_shader(const float* x, float* col, uint32_t C, uint32_t H, uint32_t W, uint32_t OH, uint32_t OW,
+                          int32_t off);
+/* nt = 1: gemm_nt.comp, nt = 0: gemm_nn.comp; batch = the dispatch's z extent. */
+void orc_gemm_fp32_shader(int nt, const float* A, const float* B, float* C, const orc_pg* p, uint32_t batch);
+void orc_softmax_shader(const float* x, float* y, uint32_t rows, uint32_t cols);
+void orc_causal_mask_shader(float* s, uint32_t batch, uint32_t rows, uint32_t cols);
+
+/* ---- the generation loop's host arithmetic ---------------------------------------------------- */
+/* std::mt19937(seed) + one std::normal_distribution<float>(0, 1) for the whole run (the latent and
+ * the ancestral draws continue one sequence). */
+void* orc_gen_rng_new(uint32_t seed);
+void orc_gen_rng_free(void* h);
+void orc_gen_rng_normal(void* h, float* out, uint64_t n);
+/* buildEuler: steps timesteps and steps + 1 sigmas; returns the initial noise sigma. */
+float orc_euler_schedule(int steps, int trailing, int numTrain, int offset, int zsnr, float* timesteps, float* sigmas);
+
+/* ---- the seeded UNet parameters of sdvk_unet_init_random, rebuilt on the host ---------------- */
+void orc_unet_rand_q8(uint64_t seed, uint64_t first, uint64_t n, int8_t* out);
+void orc_unet_rand_scale(uint64_t seed, uint64_t first, uint64_t n, float* out);
+void orc_unet_rand_f32(uint64_t seed, uint32_t t, int init, uint64_t n, float* out);
+
 /* ---- misc ------------------------------------------------------------------------------------ */
 int orc_num_threads(void);
 void orc_set_num_threads(int n);

@@ -46,6 +46,21 @@ _SIG = {
     "orc_gelu_erf_shader": (None, [_P, _P, _U64]),
     "orc_cfg_combine": (None, [_P, _P, _P, _U64, _F, _F]),
     "orc_sampler_eval": (_U64, [_P]),
+    "orc_add2_shader": (None, [_P, _P, _P, _U32]),
+    "orc_bias_add_shader": (None, [_P, _P, _U32, _U32]),
+    "orc_copy_nd_shader": (None, [_P, _P, _P]),
+    "orc_ew2_shader": (None, [_P, _P, _P, _P]),
+    "orc_unary_shader": (None, [_P, _P, _U32, _U32]),
+    "orc_upsample2x_shader": (None, [_P, _P, _U32, _U32, _U32]),
+    "orc_im2col_shader": (None, [_P, _P] + [_U32] * 5),
+    "orc_im2col_s2_shader": (None, [_P, _P] + [_U32] * 5 + [ctypes.c_int32]),
+    "orc_gemm_fp32_shader": (None, [_I, _P, _P, _P, _P, _U32]),
+    "orc_softmax_shader": (None, [_P, _P, _U32, _U32]),
+    "orc_causal_mask_shader": (None, [_P, _U32, _U32, _U32]),
+    "orc_gen_rng_new": (_P, [_U32]),
+    "orc_gen_rng_free": (None, [_P]),
+    "orc_gen_rng_normal": (None, [_P, _P, _U64]),
+    "orc_euler_schedule": (_F, [_I, _I, _I, _I, _I, _P, _P]),
     "orc_num_threads": (_I, []),
     "orc_set_num_threads": (None, [_I]),
 }
@@ -54,8 +69,9 @@ _SIG = {
 def build() -> None:
     """Build liboracle.so (and, when the reference sources are present, the _ref/ checkers)."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if os.path.isdir("/root/reference"):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    ref = os.environ.get("SDVK_REFERENCE", "")
+    if ref and os.path.isdir(ref):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
 
 
 def lib():
@@ -509,6 +525,79 @@ def sampler_run(kind: int, lat: np.ndarray, sigmas, model, noise=None, cfg=7.5, 
         if kind in (6, 7) and not last:
             have_prev, sigma_prev = True, sigma
     return lat, last_x0.copy()
+
+
+# ------------------------------------------------------------------ the rest of the kernel table
+# Each takes numpy float32 arrays and the kernel's push constants as a tuple of uint32 (the float
+# fields of copy_nd's Pnd -- its last -- packed as their bits), exactly as the walker fills them.
+def pack_push(fields, float_last: bool = False) -> bytes:
+    import struct as _st
+
+    if float_last:
+        return _st.pack(f"<{len(fields) - 1}If", *fields)
+    return _st.pack(f"<{len(fields)}I", *[int(v) & 0xFFFFFFFF for v in fields])
+
+
+def table_kernel(name: str, bufs, push: bytes, gz: int = 1) -> None:
+    """Runs the restatement of one kernel-table entry in place on the float32 arrays of `bufs`
+    (the binding order of vk_engine.cpp:51-125)."""
+    import struct as _st
+
+    L = lib()
+    P = [_p(b) for b in bufs]
+    u = _st.unpack(f"<{len(push) // 4}I", push)
+    pb = ctypes.create_string_buffer(push, len(push))
+    pp = ctypes.cast(pb, ctypes.c_void_p)
+    if name == "add2":
+        L.orc_add2_shader(P[0], P[1], P[2], u[0])
+    elif name == "bias_add":
+        L.orc_bias_add_shader(P[0], P[1], u[0], u[1])
+    elif name == "copy_nd":
+        L.orc_copy_nd_shader(P[0], P[1], pp)
+    elif name == "ew2":
+        L.orc_ew2_shader(P[0], P[1], P[2], pp)
+    elif name == "unary_fwd":
+        L.orc_unary_shader(P[0], P[1], u[0], u[1])
+    elif name == "upsample2x":
+        L.orc_upsample2x_shader(P[0], P[1], u[0], u[1], u[2])
+    elif name == "im2col":
+        L.orc_im2col_shader(P[0], P[1], *u[:5])
+    elif name == "im2col_s2":
+        L.orc_im2col_s2_shader(P[0], P[1], *u[:5], _st.unpack("<i", push[20:24])[0])
+    elif name in ("gemm_nt", "gemm_nn"):
+        L.orc_gemm_fp32_shader(int(name == "gemm_nt"), P[0], P[1], P[2], pp, gz)
+    elif name == "softmax_fwd":
+        L.orc_softmax_shader(P[0], P[1], u[0], u[1])
+    elif name == "causal_mask":
+        L.orc_causal_mask_shader(P[0], u[0], u[1], u[2])
+    else:
+        raise KeyError(name)
+
+
+class GenRng:
+    """The generation loop's noise source: std::mt19937(seed) and one std::normal_distribution<float>
+    for the whole run (sdvkgen.cpp:3732-3734), so successive calls continue the reference's sequence."""
+
+    def __init__(self, seed: int):
+        self.h = lib().orc_gen_rng_new(seed)
+
+    def normal(self, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        lib().orc_gen_rng_normal(self.h, _p(out), n)
+        return out
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_gen_rng_free(self.h)
+            self.h = None
+
+
+def euler_schedule(steps: int, spacing: str = "leading", zsnr: bool = False, num_train: int = 1000, offset: int = 1):
+    """buildEuler (sdvkgen.cpp:2723-2765): (timesteps [steps], sigmas [steps + 1], init noise sigma)."""
+    ts = np.empty(steps, np.float32)
+    sg = np.empty(steps + 1, np.float32)
+    init = lib().orc_euler_schedule(steps, int(spacing == "trailing"), num_train, offset, int(zsnr), _p(ts), _p(sg))
+    return ts, sg, float(np.float32(init))
 
 
 def num_threads() -> int:

@@ -179,13 +179,18 @@ __global__ void rand_q8_kernel(int8_t* __restrict__ q, uint64_t n, uint64_t seed
         q[i] = (int8_t)((int)(mix64(seed ^ (i * 0xD1B54A32D192ED03ull)) % 255u) - 127);
 }
 
-// Q8_0 block scale as GGUF stores it: binary16(|N(0, sigma)| / 127), widened to fp32 (Box-Muller).
+// Q8_0 block scale as GGUF stores it: binary16(|N(0, sigma)| / 127), widened to fp32.  Box-Muller in
+// double, rounded to fp32 and then to binary16, so a host generator with any faithful libm lands on
+// the same binary16 value (two double results within an ulp of each other straddle an fp32 and then
+// a binary16 rounding boundary with probability about 2^-40 per value).
 __global__ void rand_scale_kernel(float* __restrict__ s, uint64_t n, uint64_t seed, float sigma) {
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t h = mix64(seed ^ (i * 0x8CB92BA72F3D8DD7ull));
-        const float u1 = ((float)(h >> 40) + 1.0f) * (1.0f / 16777217.0f), u2 = (float)((h >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
-        const float g = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
-        s[i] = __half2float(__float2half_rn(fabsf(g) * sigma / 127.0f));
+        const double u1 = ((double)(h >> 40) + 1.0) * (1.0 / 16777217.0);
+        const double u2 = (double)((h >> 16) & 0xFFFFFF) * (1.0 / 16777216.0);
+        const double g = sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+        const float v = __double2float_rn(fabs(g) * (double)sigma / 127.0);
+        s[i] = __half2float(__float2half_rn(v));
     }
 }
 
@@ -980,5 +985,15 @@ int unet_tensor(const sdvk_unet* u, uint32_t i, sdvk_unet_tensor_info* out) {
 }
 
 uint32_t unet_tensor_count(const sdvk_unet* u) { return u ? (uint32_t)u->t.size() : 0; }
+
+int unet_tensor_layout(const sdvk_unet* u, uint32_t i, sdvk_unet_param_layout* out) {
+    if (!u || !out || i >= u->t.size()) return SDVK_E_ARG;
+    const U::Tensor& t = u->t[i];
+    out->q_off = t.kind == SDVK_UNET_Q8 ? t.q_off : 0;
+    out->s_off = t.kind == SDVK_UNET_Q8 ? t.s_off : 0;
+    out->f_off = t.kind == SDVK_UNET_F32 ? t.f_off : 0;
+    out->init = t.init;
+    return SDVK_OK;
+}
 
 }  // namespace sdvk

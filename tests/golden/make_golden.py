@@ -1,8 +1,8 @@
 """Regenerate the golden fixtures in tests/golden/ from the reference's own code.
 
-Run in the development container (it needs the reference sources and a C++ compiler):
+Run where the reference sources and a C++ compiler are (SDVK_REFERENCE names the checkout):
 
-    python tests/golden/make_golden.py
+    SDVK_REFERENCE=<sdvk checkout> python tests/golden/make_golden.py
 
 What it writes (all produced by reference code compiled from its sources, never hand-written):
   attn_ref_<i>.f32   the reference test's fp64 attention reference() (tests/fused_attn_test.cpp:25-61)
@@ -30,7 +30,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 from oracle import pyoracle  # noqa: E402
 
-REF = os.environ.get("SDVK_REFERENCE", "/root/reference")
+REF = os.environ.get("SDVK_REFERENCE", "")
 ATTN_SHAPES = [  # (Tq, Tk, C, heads, causal): tests/fused_attn_test.cpp:74-79
     (32, 32, 320, 5, True),
     (32, 77, 1280, 20, False),
@@ -54,6 +54,8 @@ def ref_gguf():
 
 
 def main() -> int:
+    if not REF or not os.path.isdir(REF):
+        sys.exit("set SDVK_REFERENCE to the reference checkout")
     pyoracle.build()
     manifest = {"generator": "tests/golden/make_golden.py", "attention": [], "gguf": {}}
 
