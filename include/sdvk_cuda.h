@@ -80,6 +80,8 @@ SDVK_API int sdvk_ctx_set_timeout_ms(sdvk_ctx* ctx, uint32_t ms);
 SDVK_API int sdvk_ctx_set_precision(sdvk_ctx* ctx, int precision);
 /* Human-readable device report (Engine::deviceReport, vk_engine.hpp:169). */
 SDVK_API int sdvk_device_report(sdvk_ctx* ctx, char* buf, size_t len);
+/* Free and total bytes of the context's device memory (Engine::deviceLocalMb, vk_engine.hpp:166). */
+SDVK_API int sdvk_device_memory(sdvk_ctx* ctx, uint64_t* free_bytes, uint64_t* total_bytes);
 /* Text of the last error on this context (empty when none). */
 SDVK_API const char* sdvk_last_error(sdvk_ctx* ctx);
 SDVK_API const char* sdvk_status_string(int status);
@@ -111,6 +113,12 @@ SDVK_API int sdvk_step_end(sdvk_ctx* ctx);
 SDVK_API int sdvk_step_wait(sdvk_ctx* ctx, uint32_t timeout_ms);
 /* Block until all queued work is done and report any device-side error (timeouts). */
 SDVK_API int sdvk_synchronize(sdvk_ctx* ctx);
+/* Failure-path self-test, no counterpart in the reference (whose waits are host fences,
+ * vk_engine.cpp:1279): queues one kernel whose bounded wait can never complete (an mbarrier that
+ * nothing arrives on), so the wait runs out after the context's timeout (sdvk_ctx_set_timeout_ms),
+ * the kernel records a timeout in the device error word and returns, and the next synchronisation
+ * reports SDVK_E_TIMEOUT.  No fault and no trap: the context stays usable afterwards. */
+SDVK_API int sdvk_selftest_wait(sdvk_ctx* ctx);
 
 /* ---- the reference's dispatch interface --------------------------------------------------- */
 /* Engine::dispatch(kernel, bufs, push, gx, gy, gz) (vk_engine.hpp:111-112, vk_engine.cpp:1143-1180)
@@ -123,10 +131,26 @@ SDVK_API int sdvk_synchronize(sdvk_ctx* ctx);
  *   "fused_attn", "fused_attn_tiled"    bufs {Q, K, V, O}         push FaPush (36 B)
  *   "layernorm_fwd"                     bufs {X, gamma, beta, Y}  push {rows, d, eps, affine} (16 B)
  *   "groupnorm"                         bufs {X, gamma, beta, Y}  push {C, P, G, eps, act} (20 B)
+ * and the rest of the table that the UNet walker, the generation loop and the unfused-attention
+ * fallback dispatch (sdvkgen.cpp:912-1206, 1226-1281), so that code runs unchanged on this back end:
+ *   "add2"          bufs {C, A, B}        push {n} (4 B)                     add2.comp
+ *   "ew2"           bufs {C, A, B}        push {n, d0..d3, as0..3, bs0..3, mode} (56 B)  ew2.comp
+ *   "copy_nd"       bufs {Dst, Src}       push Pnd (60 B)                    copy_nd.comp
+ *   "unary_fwd"     bufs {X, Y}           push {n, mode} (8 B)               unary_fwd.comp
+ *   "bias_add"      bufs {X, B}           push {C, P} (8 B)                  bias_add.comp
+ *   "upsample2x"    bufs {X, Y}           push {C, H, W} (12 B)              upsample2x.comp
+ *   "im2col"        bufs {X, Col}         push {C, H, W, row0, rows} (20 B)  im2col.comp
+ *   "im2col_s2"     bufs {X, Col}         push {C, H, W, OH, OW, off} (24 B) im2col_s2.comp
+ *   "gemm_nt", "gemm_nn"  bufs {A, B, C}  push Pg, fp32 operands, batch = gz  gemm_nt.comp, gemm_nn.comp
+ *   "softmax_fwd"   bufs {X, Y}           push {rows, cols} (8 B)            softmax_fwd.comp
+ *   "causal_mask"   bufs {S}              push {batch, rows, cols} (12 B)    causal_mask.comp
+ * add2, ew2, copy_nd, unary_fwd and softmax_fwd accept the in-place aliasing the walker uses.
  * Pg = {M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, pad} (sdvkgen.cpp:901-903);
+ * Pnd = {n, d0..d3, os0..3, ss0..3, mode, scale} (sdvkgen.cpp:904-907);
  * FaPush = {Tq, Tk, C, heads, hd, causal, pad0, pad1, scale} (fused_attn.cpp:15-26).
  * The grid (gx, gy, gz) the caller computed for the Vulkan tiling is accepted and ignored: each
- * kernel covers the whole shape in the push constants with its own B200 tiling.
+ * kernel covers the whole shape in the push constants with its own B200 tiling; for the fp32
+ * GEMMs and the Q8 GEMMs the batch count is gz, the shaders' z workgroup range.
  * Deviations: Q8 kernels require K % 32 == 0 (whole Q8_0 blocks); attention requires hd <= 64.
  * Numerics: the GEMM runs the tensor cores in tf32 on fp32 activations; attention on the fp32
  * buffers follows sdvk_ctx_set_precision (fp32 arithmetic by default). */
@@ -243,7 +267,8 @@ SDVK_API int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, 
  * image at C = 1280 fits; the batch-2 config does not).  The array is shared by every call on a
  * device: calls that can overlap in time on one device (other streams, threads or contexts) race on
  * it, and the caller must serialise them.  The array's address is looked up on the first call on
- * each device; make that first call before any stream capture begins.
+ * each device (and again after the device's CUDA context is recreated, e.g. by cudaDeviceReset);
+ * make that first call before any stream capture begins.
  * No counterpart in the reference (it dispatches the block kernel by kernel into its step arena). */
 #define SDVK_STATIC_SCRATCH_BYTES (64ull << 20)
 SDVK_API int sdvk_transformer_block_static(sdvk_ctx* ctx, const sdvk_block_desc* desc);
@@ -416,6 +441,19 @@ SDVK_API int sdvk_unet_init_random(sdvk_ctx* ctx, sdvk_unet* unet, uint64_t seed
 SDVK_API int sdvk_unet_prepare(sdvk_ctx* ctx, sdvk_unet* unet);
 SDVK_API uint32_t sdvk_unet_tensor_count(const sdvk_unet* unet);
 SDVK_API int sdvk_unet_tensor(const sdvk_unet* unet, uint32_t index, sdvk_unet_tensor_info* out);
+/* Where a tensor lives in the parameter arena (a plan has the same layout): byte offsets of its int8
+ * payload and fp32 scales (Q8) or of its values (F32), and how sdvk_unet_init_random fills it.
+ * The seeded values depend only on the seed and these offsets: payload byte i of the arena is
+ * int8 (mix64(seed ^ i * 0xD1B54A32D192ED03) % 255) - 127; scale j (counted from the first Q8
+ * tensor's scales) is binary16(|Box-Muller normal| * 0.02 / 127) from mix64((seed ^ 0x5CA1E) ^
+ * j * 0x8CB92BA72F3D8DD7); F32 tensor number t (init 2) holds 0.02 * (2 u - 1) from
+ * mix64((seed + 1000003 t) ^ e * 0xA24BAED4963EE407), with mix64 the SplitMix64 finaliser.  A host
+ * program can therefore rebuild the same parameters (a GGUF for another engine, for instance). */
+typedef struct sdvk_unet_param_layout {
+    uint64_t q_off, s_off, f_off;
+    int init; /* F32: 0 ones, 1 zeros, 2 uniform [-0.02, 0.02]; -1: filled through its group or a repack */
+} sdvk_unet_param_layout;
+SDVK_API int sdvk_unet_tensor_layout(const sdvk_unet* unet, uint32_t index, sdvk_unet_param_layout* out);
 /* Algorithmic FLOP of one pass (GEMMs, convolutions at their real input channels, attention). */
 SDVK_API uint64_t sdvk_unet_flops(const sdvk_unet* unet);
 SDVK_API uint64_t sdvk_unet_workspace_bytes(const sdvk_unet* unet);

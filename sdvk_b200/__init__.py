@@ -119,6 +119,14 @@ class UnetTensorInfo(ctypes.Structure):
 
 UNET_Q8, UNET_F32 = 0, 1
 
+
+class UnetTensorLayout(ctypes.Structure):
+    """sdvk_unet_param_layout: where a parameter lives in the arena and how the seeded init fills it."""
+
+    _fields_ = [("q_off", ctypes.c_uint64), ("s_off", ctypes.c_uint64), ("f_off", ctypes.c_uint64),
+                ("init", ctypes.c_int)]
+
+
 # name -> (restype, argtypes) for every symbol include/sdvk_cuda.h declares
 _P, _U32, _U64, _I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
 SIGNATURES = {
@@ -175,6 +183,8 @@ SIGNATURES = {
     "sdvk_transformer_block_workspace": (_U64, [ctypes.POINTER(BlockDesc)]),
     "sdvk_transformer_block": (_I, [_P, ctypes.POINTER(BlockDesc), _P, _U64]),
     "sdvk_transformer_block_static": (_I, [_P, ctypes.POINTER(BlockDesc)]),
+    "sdvk_device_memory": (_I, [_P, ctypes.POINTER(_U64), ctypes.POINTER(_U64)]),
+    "sdvk_selftest_wait": (_I, [_P]),
     "sdvk_unet_create": (_I, [_P, ctypes.POINTER(UnetDesc), ctypes.POINTER(_P)]),
     "sdvk_unet_plan": (_I, [ctypes.POINTER(UnetDesc), ctypes.POINTER(_P)]),
     "sdvk_unet_destroy": (_I, [_P]),
@@ -182,6 +192,7 @@ SIGNATURES = {
     "sdvk_unet_prepare": (_I, [_P, _P]),
     "sdvk_unet_tensor_count": (_U32, [_P]),
     "sdvk_unet_tensor": (_I, [_P, _U32, ctypes.POINTER(UnetTensorInfo)]),
+    "sdvk_unet_tensor_layout": (_I, [_P, _U32, ctypes.POINTER(UnetTensorLayout)]),
     "sdvk_unet_flops": (_U64, [_P]),
     "sdvk_unet_workspace_bytes": (_U64, [_P]),
     "sdvk_unet_launches": (_U64, [_P]),
@@ -295,6 +306,10 @@ class Context:
 
     def synchronize(self) -> None:
         self._check(lib().sdvk_synchronize(self._h), "synchronize")
+
+    def selftest_wait(self) -> None:
+        """Queue the failure-path self-test: a bounded wait that runs out (sdvk_selftest_wait)."""
+        self._check(lib().sdvk_selftest_wait(self._h), "selftest_wait")
 
     # -- step protocol (beginStep / endStep / waitStep) --------------------------------------
     def step_begin(self) -> None:

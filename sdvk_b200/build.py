@@ -22,7 +22,7 @@ OBJDIR = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libsdvk_b200.so")
 HOST = os.path.join(PKG, "host")
 ENGINE_LIB = os.path.join(PKG, "libsdvk_engine.so")  # C++ ofc::gpu::Engine mirror over the C ABI
-SOURCES = ["sdvk_abi.cu", "gemm_q8.cu", "attention.cu", "block.cu", "collective.cu", "no_alloc.cu", "ingest.cu", "conv.cu", "sampler.cu", "unet.cu"]
+SOURCES = ["sdvk_abi.cu", "gemm_q8.cu", "attention.cu", "block.cu", "collective.cu", "no_alloc.cu", "ingest.cu", "conv.cu", "sampler.cu", "unet.cu", "table.cu"]
 HEADERS = ["ptx.cuh", "gemm_q8.cuh", "gemm_q8_2sm.cuh", "attention.cuh", "attention_tc.cuh", "attention_fp32.cuh", "attention_tc_short.cuh", "backend.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -72,7 +72,8 @@ def build_engine(force: bool = False) -> str:
     """The C++ engine mirror (host/engine.cpp) as libsdvk_engine.so, linked against libsdvk_b200.so."""
     src = os.path.join(HOST, "engine.cpp")
     deps = [src, LIB, os.path.join(ROOT, "include", "sdvk_cuda.h"),
-            os.path.join(HOST, "Modules", "GPU", "vk_engine.hpp"), os.path.join(HOST, "Modules", "GPU", "fused_attn.hpp")]
+            os.path.join(HOST, "Modules", "GPU", "vk_engine.hpp"), os.path.join(HOST, "Modules", "GPU", "fused_attn.hpp"),
+            os.path.join(HOST, "Modules", "GPU", "gpu_ops.hpp")]
     if force or not os.path.exists(ENGINE_LIB) or os.path.getmtime(ENGINE_LIB) < _newest(deps):
         cxx = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else (shutil.which("g++") or "g++")
         subprocess.run([cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-I", os.path.join(ROOT, "include"), "-I", HOST,

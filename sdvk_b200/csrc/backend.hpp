@@ -114,6 +114,33 @@ uint64_t unet_workspace_bytes(const sdvk_unet* u);
 uint64_t unet_parameter_bytes(const sdvk_unet* u);
 int unet_tensor(const sdvk_unet* u, uint32_t i, sdvk_unet_tensor_info* out);
 uint32_t unet_tensor_count(const sdvk_unet* u);
+int unet_tensor_layout(const sdvk_unet* u, uint32_t i, sdvk_unet_param_layout* out);
+
+// table.cu: the rest of the reference's kernel table, with its push-constant blocks (sdvkgen.cpp:901-907
+// for Pg and Pnd, the ew2 block of mul2 :1003-1019).
+struct TablePg {
+    uint32_t M, N, K, mode, sA, sB, sC, batch, lda, ldb, ldc, pad;
+};
+struct TablePnd {
+    uint32_t n, d0, d1, d2, d3, os0, os1, os2, os3, ss0, ss1, ss2, ss3, mode;
+    float scale;
+};
+struct TablePew2 {
+    uint32_t n, d0, d1, d2, d3, as0, as1, as2, as3, bs0, bs1, bs2, bs3, mode;
+};
+int table_add2(float* c, const float* a, const float* b, uint32_t n, const LaunchEnv& env);
+int table_copy_nd(float* d, const float* s, const TablePnd& p, const LaunchEnv& env);
+int table_ew2(float* c, const float* a, const float* b, const TablePew2& p, const LaunchEnv& env);
+int table_unary(const float* x, float* y, uint32_t n, uint32_t mode, const LaunchEnv& env);
+int table_bias_add(float* x, const float* b, uint32_t C, uint32_t P, const LaunchEnv& env);
+int table_upsample2x(const float* x, float* y, uint32_t C, uint32_t H, uint32_t W, const LaunchEnv& env);
+// stride2 = false: im2col (a = row0, b = rows); true: im2col_s2 (a = OH, b = OW, off)
+int table_im2col(const float* x, float* col, uint32_t C, uint32_t H, uint32_t W, uint32_t a, uint32_t b, int off,
+                 bool stride2, const LaunchEnv& env);
+int table_gemm_fp32(bool nt, const float* A, const float* B, float* C, const TablePg& p, uint32_t batch,
+                    const LaunchEnv& env);
+int table_softmax(const float* x, float* y, uint32_t rows, uint32_t cols, const LaunchEnv& env);
+int table_causal_mask(float* s, uint32_t batch, uint32_t rows, uint32_t cols, const LaunchEnv& env);
 
 inline int dtype_size(int dt) { return dt == SDVK_F32 ? 4 : (dt == SDVK_F16 || dt == SDVK_BF16) ? 2 : 0; }
 

@@ -2,6 +2,7 @@
 // protocol, the reference-compatible name dispatch and the typed hot-path entry points.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -102,6 +103,131 @@ int collect_device_error(sdvk_ctx* ctx) {
 bool buf_holds(const sdvk_buf& b, uint64_t bytes) { return b.ptr && (b.size == 0 || bytes <= b.size); }
 const void* buf_ptr(const sdvk_buf& b) { return static_cast<const char*>(b.ptr) + b.offset; }
 void* buf_mptr(const sdvk_buf& b) { return static_cast<char*>(b.ptr) + b.offset; }
+const float* fptr(const sdvk_buf& b) { return static_cast<const float*>(buf_ptr(b)); }
+float* fmptr(const sdvk_buf& b) { return static_cast<float*>(buf_mptr(b)); }
+
+// Largest element index + 1 that a copy_nd / ew2 operand reaches for i < n, with i split over
+// d0..d2 (the rest in the last coordinate); 0 for a zero dimension.
+uint64_t nd_extent(uint32_t n, uint32_t d0, uint32_t d1, uint32_t d2, uint32_t s0, uint32_t s1, uint32_t s2,
+                   uint32_t s3) {
+    if (!n) return 0;
+    if (!d0 || !d1 || !d2) return UINT64_MAX;
+    const uint64_t last = n - 1ull;
+    const uint64_t c0 = std::min<uint64_t>(d0 - 1ull, last), c1 = std::min<uint64_t>(d1 - 1ull, last / d0);
+    const uint64_t c2 = std::min<uint64_t>(d2 - 1ull, last / ((uint64_t)d0 * d1));
+    const uint64_t c3 = last / ((uint64_t)d0 * d1 * d2);
+    return c0 * s0 + c1 * s1 + c2 * s2 + c3 * s3 + 1;
+}
+
+// The kernel-table entries around the hot path (table.cu): the walker's glue, in its binding orders
+// and push layouts (vk_engine.cpp:51-125).  Every operand is fp32; extents are checked against the
+// buffer sizes, and shapes whose indices would pass 2^32 (the shaders' uint arithmetic) are refused.
+int dispatch_table(sdvk_ctx* ctx, const std::string& name, const sdvk_buf* bufs, uint32_t nbufs, const void* push,
+                   uint32_t push_bytes, uint32_t batch) {
+    auto need = [&](uint32_t nb, uint32_t pb) -> int {
+        if (nbufs < nb || push_bytes < pb)
+            return set_err(ctx, SDVK_E_ARG, name + ": needs " + std::to_string(nb) + " buffers and a " +
+                                                std::to_string(pb) + "-byte push");
+        return SDVK_OK;
+    };
+    auto small = [&](uint32_t i, uint64_t elems) {
+        return elems > (1ull << 32) || !buf_holds(bufs[i], elems * 4);
+    };
+    auto too_small = [&]() { return set_err(ctx, SDVK_E_ARG, name + ": a buffer is smaller than the shape needs"); };
+    uint32_t u[6] = {};
+    std::memcpy(u, push, std::min<uint32_t>(push_bytes, sizeof u));
+    if (int rc = use_device(ctx)) return rc;
+    const sdvk::LaunchEnv env = env_of(ctx);
+    if (name == "add2") {
+        if (int rc = need(3, 4)) return rc;
+        if (small(0, u[0]) || small(1, u[0]) || small(2, u[0])) return too_small();
+        return sdvk::table_add2(fmptr(bufs[0]), fptr(bufs[1]), fptr(bufs[2]), u[0], env);
+    }
+    if (name == "copy_nd") {
+        if (int rc = need(2, sizeof(sdvk::TablePnd))) return rc;
+        sdvk::TablePnd p;
+        std::memcpy(&p, push, sizeof p);
+        if (small(0, nd_extent(p.n, p.d0, p.d1, p.d2, p.os0, p.os1, p.os2, p.os3)) ||
+            small(1, nd_extent(p.n, p.d0, p.d1, p.d2, p.ss0, p.ss1, p.ss2, p.ss3)))
+            return too_small();
+        return sdvk::table_copy_nd(fmptr(bufs[0]), fptr(bufs[1]), p, env);
+    }
+    if (name == "ew2") {
+        if (int rc = need(3, sizeof(sdvk::TablePew2))) return rc;
+        sdvk::TablePew2 p;
+        std::memcpy(&p, push, sizeof p);
+        if (small(0, p.n) || small(1, nd_extent(p.n, p.d0, p.d1, p.d2, p.as0, p.as1, p.as2, p.as3)) ||
+            small(2, nd_extent(p.n, p.d0, p.d1, p.d2, p.bs0, p.bs1, p.bs2, p.bs3)))
+            return too_small();
+        return sdvk::table_ew2(fmptr(bufs[0]), fptr(bufs[1]), fptr(bufs[2]), p, env);
+    }
+    if (name == "unary_fwd") {
+        if (int rc = need(2, 8)) return rc;
+        if (small(0, u[0]) || small(1, u[0])) return too_small();
+        return sdvk::table_unary(fptr(bufs[0]), fmptr(bufs[1]), u[0], u[1], env);
+    }
+    if (name == "bias_add") {
+        if (int rc = need(2, 8)) return rc;
+        if (small(0, (uint64_t)u[0] * u[1]) || small(1, u[1] ? u[0] : 0)) return too_small();
+        return sdvk::table_bias_add(fmptr(bufs[0]), fptr(bufs[1]), u[0], u[1], env);
+    }
+    if (name == "upsample2x") {
+        if (int rc = need(2, 12)) return rc;
+        const uint64_t in = (uint64_t)u[0] * u[1] * u[2];
+        if (small(0, in) || small(1, in * 4)) return too_small();
+        return sdvk::table_upsample2x(fptr(bufs[0]), fmptr(bufs[1]), u[0], u[1], u[2], env);
+    }
+    if (name == "im2col" || name == "im2col_s2") {
+        const bool s2 = name == "im2col_s2";
+        if (int rc = need(2, s2 ? 24 : 20)) return rc;
+        const uint64_t in = (uint64_t)u[0] * u[1] * u[2];
+        const uint64_t P = s2 ? (uint64_t)u[3] * u[4] : (uint64_t)u[4] * u[2];
+        if (small(0, in) || small(1, (uint64_t)u[0] * 9 * P)) return too_small();
+        if (!s2 && (uint64_t)u[3] + u[4] > u[1]) return set_err(ctx, SDVK_E_SHAPE, name + ": rows past the input");
+        return sdvk::table_im2col(fptr(bufs[0]), fmptr(bufs[1]), u[0], u[1], u[2], u[3], u[4], s2 ? (int)u[5] : -1, s2,
+                                  env);
+    }
+    if (name == "gemm_nt" || name == "gemm_nn") {
+        const bool nt = name == "gemm_nt";
+        if (int rc = need(3, sizeof(sdvk::TablePg))) return rc;
+        sdvk::TablePg p;
+        std::memcpy(&p, push, sizeof p);
+        if (!p.M || !p.N) return SDVK_OK;
+        const uint64_t lda = p.lda ? p.lda : p.K, ldb = nt ? p.K : (p.ldb ? p.ldb : p.N), ldc = p.ldc ? p.ldc : p.N;
+        const uint64_t z = batch - 1ull;
+        const uint64_t a_end = p.K ? z * p.sA + (p.M - 1ull) * lda + p.K : 0;
+        const uint64_t b_end = !p.K ? 0 : nt ? z * p.sB + (p.N - 1ull) * ldb + p.K : z * p.sB + (p.K - 1ull) * ldb + p.N;
+        const uint64_t c_end = z * p.sC + (p.M - 1ull) * ldc + p.N;
+        if (small(0, a_end) || small(1, b_end) || small(2, c_end)) return too_small();
+        return sdvk::table_gemm_fp32(nt, fptr(bufs[0]), fptr(bufs[1]), fmptr(bufs[2]), p, batch, env);
+    }
+    if (name == "softmax_fwd") {
+        if (int rc = need(2, 8)) return rc;
+        const uint64_t n = (uint64_t)u[0] * u[1];
+        if (small(0, n) || small(1, n)) return too_small();
+        return sdvk::table_softmax(fptr(bufs[0]), fmptr(bufs[1]), u[0], u[1], env);
+    }
+    if (name == "causal_mask") {
+        if (int rc = need(1, 12)) return rc;
+        if (small(0, (uint64_t)u[0] * u[1] * u[2])) return too_small();
+        return sdvk::table_causal_mask(fmptr(bufs[0]), u[0], u[1], u[2], env);
+    }
+    return set_err(ctx, SDVK_E_KERNEL, "unknown kernel " + name);
+}
+
+// One warp waits on phase 0 of an mbarrier that nothing arrives on, through the same bounded wait
+// every pipeline kernel uses (mbar_wait).  The wait runs out after timeout_ns of global time; the
+// warp then records kErrTimeout in the context's error word and the kernel returns normally.
+__global__ void __launch_bounds__(32) wait_selftest_kernel(uint32_t* err, uint64_t timeout_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        sdvk::mbar_init(&bar, 1);
+        sdvk::fence_mbar_init();
+    }
+    __syncwarp();
+    const bool done = sdvk::mbar_wait(&bar, 0, timeout_ns);
+    if (!done && threadIdx.x == 0) atomicOr(err, sdvk::kErrTimeout);
+}
 
 }  // namespace
 
@@ -211,6 +337,23 @@ int sdvk_device_report(sdvk_ctx* ctx, char* buf, size_t len) {
     std::snprintf(buf, len, "device|%d\nname|%s\nsms|%d\nmem_total_mb|%llu\nmem_free_mb|%llu\n", ctx->device,
                   ctx->device_name.c_str(), ctx->num_sms, (unsigned long long)(total_b >> 20),
                   (unsigned long long)(free_b >> 20));
+    return SDVK_OK;
+}
+
+int sdvk_selftest_wait(sdvk_ctx* ctx) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    wait_selftest_kernel<<<1, 32, 0, ctx->stream>>>(ctx->err_dev, ctx->timeout_ns);
+    return cuda_err(ctx, cudaGetLastError(), "sdvk_selftest_wait");
+}
+
+int sdvk_device_memory(sdvk_ctx* ctx, uint64_t* free_bytes, uint64_t* total_bytes) {
+    if (!ctx || !free_bytes || !total_bytes) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    size_t f = 0, t = 0;
+    if (int rc = cuda_err(ctx, cudaMemGetInfo(&f, &t), "cudaMemGetInfo")) return rc;
+    *free_bytes = f;
+    *total_bytes = t;
     return SDVK_OK;
 }
 
@@ -518,6 +661,11 @@ int sdvk_transformer_block(sdvk_ctx* ctx, const sdvk_block_desc* desc, void* wor
 int sdvk_transformer_block_static(sdvk_ctx* ctx, const sdvk_block_desc* desc) {
     if (!ctx || !desc) return SDVK_E_ARG;
     if (int rc = use_device(ctx)) return rc;
+    // the shape checks of the workspace entry point first, so a bad description gets its own error
+    if (!desc->x) return set_err(ctx, SDVK_E_ARG, "null pointer");
+    if (desc->batch && desc->T && (desc->heads == 0 || desc->C % desc->heads || desc->C / desc->heads > 64))
+        return set_err(ctx, SDVK_E_SHAPE, "heads must divide C with head dim <= 64");
+    if (desc->batch && desc->T && desc->Tctx && !desc->ctx) return set_err(ctx, SDVK_E_ARG, "null context");
     const uint64_t need = sdvk::block_workspace_bytes(*desc);
     if (need > SDVK_STATIC_SCRATCH_BYTES)
         return set_err(ctx, SDVK_E_SHAPE, "the block needs " + std::to_string(need) +
@@ -717,7 +865,7 @@ int sdvk_dispatch(sdvk_ctx* ctx, const char* kernel, const sdvk_buf* bufs, uint3
         d.causal = (int)pc.causal;
         return sdvk_attention(ctx, &d);
     }
-    return set_err(ctx, SDVK_E_KERNEL, "unknown kernel " + name);
+    return dispatch_table(ctx, name, bufs, nbufs, push, push_bytes, batch);
 }
 
 }  // extern "C"
@@ -753,6 +901,10 @@ uint32_t sdvk_unet_tensor_count(const sdvk_unet* unet) { return sdvk::unet_tenso
 
 int sdvk_unet_tensor(const sdvk_unet* unet, uint32_t index, sdvk_unet_tensor_info* out) {
     return sdvk::unet_tensor(unet, index, out);
+}
+
+int sdvk_unet_tensor_layout(const sdvk_unet* unet, uint32_t index, sdvk_unet_param_layout* out) {
+    return sdvk::unet_tensor_layout(unet, index, out);
 }
 
 uint64_t sdvk_unet_flops(const sdvk_unet* unet) { return sdvk::unet_flops(unet); }

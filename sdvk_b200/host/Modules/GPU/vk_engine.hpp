@@ -11,9 +11,16 @@
 //     VkDevice and VkPhysicalDevice are opaque pointer aliases; device()/physDevice() return the
 //     sdvk context, which Arena::init takes to allocate from.
 //   * Kernels are compiled into the library: loadKernels() checks the library is usable and
-//     ignores the SPIR-V directory.  dispatch() accepts the hot-path kernel names
-//     (gemm_nt_q8*, gemm_nn_q8*, fused_attn*); any other name throws std::runtime_error where the
-//     reference prints and exits (vk_engine.cpp:1147-1150).
+//     ignores the SPIR-V directory.  dispatch() accepts the hot-path kernel names (gemm_nt_q8*,
+//     gemm_nn_q8*, fused_attn*) and the rest of the table the UNet walker and generation loop use
+//     (layernorm_fwd, groupnorm, add2, ew2, copy_nd, unary_fwd, bias_add, upsample2x, im2col*,
+//     gemm_nt, gemm_nn, softmax_fwd, causal_mask); any other name throws std::runtime_error where
+//     the reference prints and exits (vk_engine.cpp:1147-1150).
+//   * beginUpload / stageUpload hand out pinned staging slots that stay valid until flushUploads()
+//     copies them all (the ring grows by a new pinned chunk instead of flushing under a caller that
+//     still holds an earlier slot).
+//   * profileDump() (OFC_KERNEL_PROFILE=1): dispatches are then synchronised one by one and their
+//     host-measured times aggregated per kernel name.
 //   * Work is stream-ordered on the context's CUDA stream, so barrier() has nothing to do; steps
 //     map to sdvk_step_begin/end/wait.
 //   * Arena::allocGrow cannot move a device allocation under live BufRefs (they hold the base
@@ -25,6 +32,8 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <unordered_map>
+#include <utility>
 #include <vector>
 
 #ifndef VK_NULL_HANDLE
@@ -99,22 +108,27 @@ public:
     void endStep();
     void waitStep();
 
+    void profileDump();
+
     void uploadNow(BufRef dst, const void* src, uint64_t bytes);
-    void stageUpload(BufRef dst, const void* src, uint64_t bytes) { uploadNow(dst, src, bytes); }
+    void stageUpload(BufRef dst, const void* src, uint64_t bytes);
     void* beginUpload(BufRef dst, uint64_t bytes);
-    void endUpload();
+    void endUpload() {}
     void releaseUploadStaging();
-    void flushUploads() {}
+    void flushUploads();
     void downloadNow(BufRef src, void* dst, uint64_t bytes);
     void downloadNow(BufRef src, void* dst, uint64_t bytes, uint64_t srcOff);
 
     void barrier() {}
+    // Moves [off, off + bytes) of the step arena down to dst in stream order; the ranges may overlap.
+    void compactStepArena(uint64_t dst, uint64_t off, uint64_t bytes);
 
     Arena& stepArena() { return stepArena_; }
     Arena& scratchArena() { return scratchArena_; }
     VkDevice device() const { return static_cast<VkDevice>(ctx_); }
     VkPhysicalDevice physDevice() const { return static_cast<VkPhysicalDevice>(ctx_); }
     const std::string& deviceName() const { return deviceName_; }
+    uint64_t deviceLocalMb() const;
     uint64_t lastStepMs() const { return lastStepMs_; }
     std::string deviceReport() const;
 
@@ -124,16 +138,26 @@ public:
     void check(int status, const char* what) const;
 
 private:
+    void* stagingSlot(uint64_t bytes);
     sdvk_ctx* ctx_ = nullptr;
     int devIndex_ = 0;
     std::string deviceName_;
     Arena stepArena_, scratchArena_;
     bool inStep_ = false;
     uint64_t stepStartNs_ = 0, lastStepMs_ = 0;
-    void* upHost_ = nullptr;  // beginUpload staging (pinned)
-    uint64_t upCap_ = 0;
-    BufRef upDst_{};
-    uint64_t upBytes_ = 0;
+    struct StagingChunk {  // pinned host memory the upload slots come from
+        void* host;
+        uint64_t cap, used;
+    };
+    struct PendingUpload {
+        BufRef dst;
+        const void* src;
+        uint64_t bytes;
+    };
+    std::vector<StagingChunk> staging_;
+    std::vector<PendingUpload> pending_;
+    int profile_ = -1;  // OFC_KERNEL_PROFILE, read once
+    std::unordered_map<std::string, std::pair<double, uint64_t>> prof_;  // kernel -> (seconds, calls)
 };
 
 }  // namespace gpu

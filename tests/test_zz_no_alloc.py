@@ -54,6 +54,7 @@ def test_static_block_matches_workspace_entry_point_twice(cuda_ok):
     ctxh.transformer_block_static(desc(warm))  # first call: looks the array up on this device
     ctxh.synchronize()
     torch.cuda.synchronize()
+    alloc0, reserved0 = torch.cuda.memory_allocated(), torch.cuda.memory_reserved()
     free0, _ = torch.cuda.mem_get_info()  # nothing below allocates until free1
     for i in range(2):  # two calls in a row, each against the workspace entry point
         ctxh.transformer_block_static(desc(xa))
@@ -63,11 +64,24 @@ def test_static_block_matches_workspace_entry_point_twice(cuda_ok):
     ctxh.synchronize()
     torch.cuda.synchronize()
     free1, _ = torch.cuda.mem_get_info()
+    # strict: neither this process's torch allocator nor the device (coarse: any process) saw memory
+    # taken between the two readings
+    assert torch.cuda.memory_allocated() == alloc0 and torch.cuda.memory_reserved() == reserved0
     assert free1 == free0
     for i in range(2):
         assert torch.isfinite(after[2 * i]).all()
         assert torch.equal(after[2 * i], after[2 * i + 1])
     assert not torch.equal(after[0], x0) and not torch.equal(after[2], after[0])
+
+
+def test_static_block_reports_shape_errors_before_size(cuda_ok):
+    """A bad head layout gets its own error, not the scratch-size one, even when it is also too big."""
+    x0, ctx, W, desc = _block(B=2)
+    d = desc(x0)
+    d.heads = 0
+    with pytest.raises(sdvk_b200.SdvkError) as e:
+        torch_ops.context().transformer_block_static(d)
+    assert e.value.status == sdvk_b200.E_SHAPE and "heads" in str(e.value)
 
 
 def test_static_block_rejects_oversize_shapes(cuda_ok):
