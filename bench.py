@@ -28,10 +28,21 @@ prints one JSON line.
 `e2e` is the same metric through the C ABI with pinned host buffers: each step uploads that step's
 inputs, runs the kernel and downloads the result, all inside the timed region.
 
---impl reference times the reference's own arithmetic for the workload (the C++ restatement of
-gemm_nt_q8_v.comp / fused_attn_tiled.comp / fused_attn.comp in oracle/, which is what the
-reference's Vulkan path computes; the Vulkan path itself needs a graphics stack this machine does
-not have) on the host cores.
+--impl reference times the reference's own CPU implementation on the host cores (all usable cores,
+whatever OMP_NUM_THREADS the launcher set).  For the UNet workloads that is the reference's own
+generation program -- src/Modules/Diffusion/main.cpp and sdvkgen.cpp compiled unchanged against the
+host stub engine (oracle/_ref/sdvkgen_host), whose kernels restate the reference's shaders in C++ --
+running its Euler / v-pred / CFG 5 loop on the same seeded UNet at a 16x16 latent, each of its steps
+scaled to the 128x128 latent by the UNet's FLOP ratio (the program runs the full size about 20 %
+slower per FLOP than the small one, so the scaled value flatters the reference).  For the kernel
+workloads it is the oracle's C++ restatement of gemm_nt_q8_v.comp / fused_attn_tiled.comp /
+fused_attn.comp.  The Vulkan path itself needs a graphics stack this machine does not have.
+
+The default `unet` line also carries `kernels` (config 0's GEMM and config 1's three attentions,
+CUDA-event timed in the same process, each with its roofline fraction) and, at N >= 2, `cfg_pair`:
+the CFG halves of each image on a GPU pair through the C ABI (sdvk_comm_create / sdvk_allgather
+inside the captured step graph), with the pair's all-gather time and a check that both ranks of
+every pair end with bit-identical latents.
 """
 from __future__ import annotations
 
@@ -875,15 +886,88 @@ WORKLOADS = {
 }
 
 
+def usable_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def oracle_threads() -> int:
+    """Every usable host core for the oracle's OpenMP loops, whatever OMP_NUM_THREADS says (torchrun
+    sets it to 1 per rank)."""
+    from oracle import pyoracle
+
+    n = usable_cores()
+    pyoracle.lib().orc_set_num_threads(n)
+    return n
+
+
+REF_PROGRAM = os.path.join(ROOT, "oracle", "_ref", "sdvkgen_host")
+REF_SEED = 3        # the UNet seed both arms use (UnetWorkload._ensure)
+REF_LATENT = 16     # the reference program's sample latent edge
+
+
+def ref_model_args(workdir: str):
+    """The seeded SDXL UNet as a GGUF file the reference's loader reads (cached between runs in the
+    temp directory: 2.7 GB) and seeded embeddings, as the reference program's CLI options."""
+    sys.path.insert(0, ROOT)
+    from oracle import pyoracle, unet_gguf
+
+    gguf = os.path.join(tempfile.gettempdir(), f"sdvk_bench_unet_seed{REF_SEED}.gguf")
+    if not (os.path.exists(gguf) and os.path.getsize(gguf) > 2_000_000_000):
+        tmp = gguf + f".{os.getpid()}.part"
+        unet_gguf.write_gguf(tmp, REF_SEED)
+        os.replace(tmp, gguf)
+    files = {}
+    ctx = pyoracle.normal_f32(11, 1, (2, 77, 2048))
+    pool = pyoracle.normal_f32(11, 2, (2, 1280))
+    for k, a in (("c", ctx[0]), ("u", ctx[1]), ("p", pool[0]), ("pu", pool[1])):
+        files[k] = os.path.join(workdir, k + ".f32")
+        np.ascontiguousarray(a, "<f4").tofile(files[k])
+    return ["--unet", gguf, "--te1", gguf, "--te2", gguf, "--vae", gguf, "--emb-cond", files["c"], "--emb-uncond",
+            files["u"], "--emb-pool", files["p"], "--emb-poolu", files["pu"]]
+
+
+def ref_unet_sample(warmup: int, steps: int):
+    """warmup + steps steps of the reference's own generation loop (Euler, v-pred, CFG 5: two UNet
+    passes, the host CFG combine and the update per step) at a REF_LATENT^2 latent, each step timed
+    by the wall clock between the program's step lines.  Returns the mean of the timed steps in
+    seconds, the FLOP scale to the 128^2 latent and the core count."""
+    sys.path.insert(0, ROOT)
+    from sdvk_b200.unet import plan
+
+    cores = usable_cores()
+    with tempfile.TemporaryDirectory() as td:
+        args = ref_model_args(td)
+        env = dict(os.environ, OMP_NUM_THREADS=str(cores))
+        cmd = [REF_PROGRAM, "x"] + args + ["--width", str(8 * REF_LATENT), "--height", str(8 * REF_LATENT), "--seed",
+                                           "1", "--no-vae", "--latent-out", os.path.join(td, "lat.bin"), "--sampler",
+                                           "euler", "--steps", str(warmup + steps), "--cfg", "5", "--vpred"]
+        p = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, env=env, cwd=td)
+        times, t_prev, tail = [], None, []
+        for line in p.stdout:
+            now = time.perf_counter()
+            tail = (tail + [line])[-20:]
+            if line.startswith("sampler "):
+                t_prev = now
+            elif line.startswith("step ") and t_prev is not None:
+                times.append(now - t_prev)
+                t_prev = now
+        rc = p.wait()
+    if rc != 0 or len(times) != warmup + steps:
+        raise RuntimeError("reference program failed:\n" + "".join(tail))
+    scale = plan(1, 128, 128)["flops"] / plan(1, REF_LATENT, REF_LATENT)["flops"]
+    return statistics.mean(times[warmup:]), scale, cores
+
+
 def cpu_sample(wl, budget_s, steps=None):
     """Time the reference arithmetic on a bounded sample of the workload.  With `steps` given (the
     reference arm), each step runs the same number of whole units (rows of X, query rows), sized
     from a probe so that the steps take about `budget_s` together.  Without it, whole workloads (or
     the largest unit count that fits) repeat until `budget_s` has passed.  Returns
     (FLOP per s, units per run, runs, seconds, threads)."""
-    from oracle import pyoracle
-
-    threads = pyoracle.num_threads()
+    threads = oracle_threads()
     inputs = wl.host_inputs()
     probe = min(wl.cpu_units, 64)
     t0 = time.perf_counter()
@@ -905,6 +989,8 @@ def cpu_sample(wl, budget_s, steps=None):
 def run_reference(args, rank, world, wl):
     if rank != 0:
         return 0
+    if isinstance(wl, UnetWorkload) and os.path.exists(REF_PROGRAM):
+        return run_reference_program(args, world, wl)
     budget = 60.0
     fps, units, _, dt, threads = cpu_sample(wl, budget, steps=args.steps)
     value = wl_cpu_value(wl, fps)
@@ -923,6 +1009,173 @@ def run_reference(args, rank, world, wl):
     return 0
 
 
+def run_reference_program(args, world, wl):
+    """The reference arm of the UNet workloads: the reference's own generation loop (ref_unet_sample)."""
+    s_sample, scale, cores = ref_unet_sample(args.warmup, args.steps)
+    s_step = s_sample * scale  # one CFG step (two batch-1 passes) at the 128^2 latent
+    value = 1.0 / (wl.steps_per_image * s_step)
+    sample = (f"{args.steps} timed steps (after {args.warmup}) of the reference's own generation loop "
+              f"(oracle/_ref/sdvkgen_host: main.cpp + sdvkgen.cpp unchanged, shaders restated in C++, "
+              f"{cores} OpenMP threads) at a {REF_LATENT}x{REF_LATENT} latent, Euler / v-pred / CFG 5, "
+              f"{s_sample * 1e3:.0f} ms per step, scaled to 128x128 by the UNet FLOP ratio {scale:.1f}")
+    line = {
+        "impl": "reference", "metric": wl.metric, "value": value, "unit": wl_unit(wl), "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": s_step * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": wl.describe, "sample_latent": REF_LATENT,
+                                        "flop_scale_to_full": scale},
+        "cpu_baseline": {"value": value, "unit": wl_unit(wl), "cores": cores, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": wl_unit(wl), "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's Vulkan engine is unavailable on this box (no graphics stack); its own UNet walker "
+                "and generation loop run on the host stub engine",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def kernel_lines(torch, torch_ops, device):
+    """Config 0's GEMM and config 1's attentions, CUDA-event timed over CUDA-graph replays in this
+    process (rotating inputs larger than L2), each against its roofline."""
+    pk, pk_kind = peaks()
+    cases = [("gemm_9216x1280x1280", GemmWorkload(), 2000),
+             ("attn_self_4096", AttnWorkload("attn-self-4096", 2, 4096, 4096, 10), 400),
+             ("attn_self_1024", AttnWorkload("attn-self-1024", 2, 1024, 1024, 20), 2000),
+             ("attn_cross_77", AttnWorkload("attn-cross-77", 2, 1024, 77, 20), 2000)]
+    out = {}
+    cap = torch.cuda.Stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clk:
+        for key, wl, steps in cases:
+            sets = [wl.make_set(torch, device, 77 + i) for i in range(wl.rotate)]
+            for i in range(2 * wl.rotate):
+                wl.step(torch_ops, sets[i % wl.rotate])
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for i in range(GRAPH_LEN):
+                    wl.step(torch_ops, sets[i % wl.rotate])
+            reps = max(1, steps // GRAPH_LEN)
+            g.replay()
+            torch.cuda.synchronize()
+            stream = torch.cuda.current_stream(device)
+            ev0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            us = ev0.elapsed_time(ev1) * 1e3 / (reps * GRAPH_LEN)
+            if wl.bound == "tensor":
+                ach, peak, unit = wl.flop / (us * 1e-6) / 1e12, pk["bf16_tflops"], "TFLOP/s"
+            else:
+                ach, peak, unit = wl.bytes / (us * 1e-6) / 1e9, pk["hbm_gbs"], "GB/s"
+            out[key] = {"us_per_launch": us, "achieved": ach, "unit": unit, "peak": peak, "frac": ach / peak,
+                        "bound": wl.bound, "flop": wl.flop, "bytes": wl.bytes, "traffic": profile_traffic(wl.name),
+                        "launches": reps * GRAPH_LEN}
+            del g, sets
+            torch.cuda.synchronize()
+    out["peak_kind"] = f"{pk_kind} (MEASURED_PEAKS.json: dense bf16 burst / HBM copy)"
+    out["clocks"] = clk.summary()
+    return out
+
+
+def cfg_pair_line(torch, dist, device, rank, world, steps, warmup):
+    """BASELINE config 4's second mode through the C ABI: rank 2p runs image p's conditional half and
+    rank 2p + 1 its unconditional half (batch-1 UNet passes); each step's captured CUDA graph is the
+    pass, sdvk_allgather of the two 4x128x128 fp32 predictions over the pair's NCCL communicator
+    (sdvk_comm_create), and the sampler step on the gathered [cond | uncond] -- so both ranks update
+    the same latent from the same bytes.  Every rank takes the same collective steps."""
+    import sdvk_b200
+    from sdvk_b200 import torch_ops
+    from sdvk_b200.unet import Unet
+
+    ctx = torch_ops.context(device)
+    pair, prank = rank // 2, rank % 2
+    uid = sdvk_b200.comm_unique_id() if prank == 0 else bytes(sdvk_b200.COMM_ID_BYTES)
+    ids = [None] * world
+    dist.all_gather_object(ids, uid)
+    comm = sdvk_b200.Comm(ctx, 2, prank, ids[2 * pair], timeout_ms=60000)
+    u = Unet(1, 128, 128, device=device.index)
+    u.init_random(REF_SEED)
+    n = 4 * 128 * 128
+    g = torch.Generator(device=device)
+    g.manual_seed(500 + pair)  # the same image on both ranks of the pair
+    lat = torch.randn((n,), generator=g, device=device) * 14.6
+    adm = torch.randn((1, 2816), generator=g, device=device)
+    ctxs = torch.randn((2, 77, 2048), generator=g, device=device).half()
+    cx = ctxs[prank:prank + 1].contiguous()  # this rank's half: cond or uncond
+    xin = (lat / math.sqrt(14.6 ** 2 + 1)).view(1, 4, 128, 128).contiguous()
+    ts = torch.full((1,), 999.0, device=device)
+    out = torch.empty_like(xin)
+    gathered = torch.empty((2, n), device=device)
+    x0 = torch.empty((n,), device=device)
+    d = sdvk_b200.SamplerStepDesc()
+    d.kind, d.phase, d.n = sdvk_b200.SAMPLER_EULER, 0, n
+    d.eps_c, d.eps_u, d.cfg, d.vpred = gathered.data_ptr(), gathered.data_ptr() + 4 * n, 5.0, 1
+    d.lat, d.x0, d.x_model = lat.data_ptr(), x0.data_ptr(), xin.data_ptr()
+    d.sigma, d.sigma_next = 14.6, 12.0
+    lib = sdvk_b200.lib()
+
+    def one_step():
+        ctx._check(lib.sdvk_unet_forward(ctx.handle, u._h, xin.data_ptr(), ts.data_ptr(), adm.data_ptr(),
+                                         cx.data_ptr(), 1, out.data_ptr()), "sdvk_unet_forward")
+        comm.allgather(out.data_ptr(), gathered.data_ptr(), n, sdvk_b200.F32)
+        ctx.sampler_step(d)
+
+    cur = torch.cuda.current_stream(device)
+    for _ in range(max(2, warmup)):
+        ctx.set_stream(cur.cuda_stream)
+        one_step()
+    comm.wait()
+    torch.cuda.synchronize()
+    cap = torch.cuda.Stream(device)
+    step_graph, ag_graph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    cap.wait_stream(cur)
+    with torch.cuda.graph(step_graph, stream=cap):
+        ctx.set_stream(cap.cuda_stream)
+        one_step()
+    with torch.cuda.graph(ag_graph, stream=cap):
+        ctx.set_stream(cap.cuda_stream)
+        for _ in range(20):
+            comm.allgather(out.data_ptr(), gathered.data_ptr(), n, sdvk_b200.F32)
+    cur.wait_stream(cap)
+    ctx.set_stream(cur.cuda_stream)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(graph, reps):
+        graph.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        ev0.record(cur)
+        for _ in range(reps):
+            graph.replay()
+        ev1.record(cur)
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1)], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with ClockSampler(device.index) as clk:
+        ms = timed(step_graph, steps) / steps
+    ag_us = timed(ag_graph, 5) * 1e3 / (5 * 20)
+    # both ranks of every pair must hold the same latent bytes
+    lats = [torch.empty_like(lat) for _ in range(world)]
+    dist.all_gather(lats, lat)
+    same = all(torch.equal(lats[2 * p], lats[2 * p + 1]) for p in range(world // 2))
+    del step_graph, ag_graph
+    torch.cuda.synchronize()
+    dist.barrier()
+    comm.close()
+    u.close()
+    pairs = world // 2
+    return {"pairs": pairs, "ms_per_step": ms, "images_per_s": pairs / (UnetWorkload.steps_per_image * ms * 1e-3),
+            "allgather_us": ag_us, "allgather_bytes_per_rank": 4 * n, "latents_bit_identical": bool(same),
+            "nccl_ranks_per_communicator": 2, "communicators": pairs, "steps": steps, "clocks": clk.summary(),
+            "path": "sdvk_unet_forward (batch 1) + sdvk_allgather (C ABI over NCCL) + sdvk_sampler_step, "
+                    "one CUDA graph per step, CUDA events, max over ranks"}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -931,6 +1184,8 @@ def main(argv=None):
     ap.add_argument("--impl", default="sdvk", choices=["sdvk", "reference"])
     ap.add_argument("--workload", default="unet", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernels", action="store_true", help="unet: leave out the GEMM/attention sub-line")
+    ap.add_argument("--no-cfg-pair", action="store_true", help="unet at N >= 2: leave out the CFG-pair sub-line")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
     wl = WORKLOADS[args.workload]()
@@ -1047,9 +1302,26 @@ def main(argv=None):
     # ---- CPU baseline (rank 0, N = 1 only): a bounded sample of the same workload
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        fps, units, runs, secs, threads = cpu_sample(wl, budget_s=15.0)
-        cpu = {"value": wl_cpu_value(wl, fps), "unit": wl_unit(wl), "cores": threads, "kind": "port",
-               "sample": f"{runs} x {units} of {wl.cpu_units} {wl.cpu_what}, {secs:.1f} s"}
+        if isinstance(wl, UnetWorkload) and os.path.exists(REF_PROGRAM):
+            s_sample, scale, cores = ref_unet_sample(1, 3)
+            cpu = {"value": 1.0 / (wl.steps_per_image * s_sample * scale), "unit": wl_unit(wl), "cores": cores,
+                   "kind": "reference",
+                   "sample": (f"3 steps (after 1) of the reference's own generation loop (oracle/_ref/sdvkgen_host, "
+                              f"main.cpp + sdvkgen.cpp unchanged on the host stub engine) at a {REF_LATENT}x"
+                              f"{REF_LATENT} latent, {s_sample * 1e3:.0f} ms per step, scaled to 128x128 by the "
+                              f"UNet FLOP ratio {scale:.1f}")}
+        else:
+            fps, units, runs, secs, threads = cpu_sample(wl, budget_s=15.0)
+            cpu = {"value": wl_cpu_value(wl, fps), "unit": wl_unit(wl), "cores": threads, "kind": "port",
+                   "sample": f"{runs} x {units} of {wl.cpu_units} {wl.cpu_what}, {secs:.1f} s"}
+
+    # ---- the metric's kernel half (config 0 GEMM, config 1 attention) and, at N >= 2, the CFG pair
+    kernels = None
+    if wl.name == "unet" and rank == 0 and not args.no_kernels:
+        kernels = kernel_lines(torch, torch_ops, device)
+    pair_line = None
+    if wl.name == "unet" and world >= 2 and world % 2 == 0 and not args.no_cfg_pair:
+        pair_line = cfg_pair_line(torch, dist, device, rank, world, min(args.steps, 20), args.warmup)
 
     pk, pk_kind = peaks()
     achieved_tf = wl.flop / (ms_per_step * 1e-3) / 1e12
@@ -1081,6 +1353,10 @@ def main(argv=None):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if kernels is not None:
+            line["kernels"] = kernels
+        if pair_line is not None:
+            line["cfg_pair"] = pair_line
         print(json.dumps(line), flush=True)
     for g in graphs.values():
         del g
