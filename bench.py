@@ -1131,10 +1131,11 @@ def cfg_pair_line(torch, dist, device, rank, world, steps, warmup):
     cap = torch.cuda.Stream(device)
     step_graph, ag_graph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     cap.wait_stream(cur)
-    with torch.cuda.graph(step_graph, stream=cap):
+    # thread-local capture: NCCL's own threads keep making CUDA calls while this thread captures
+    with torch.cuda.graph(step_graph, stream=cap, capture_error_mode="thread_local"):
         ctx.set_stream(cap.cuda_stream)
         one_step()
-    with torch.cuda.graph(ag_graph, stream=cap):
+    with torch.cuda.graph(ag_graph, stream=cap, capture_error_mode="thread_local"):
         ctx.set_stream(cap.cuda_stream)
         for _ in range(20):
             comm.allgather(out.data_ptr(), gathered.data_ptr(), n, sdvk_b200.F32)

@@ -44,8 +44,14 @@ struct Gemm2Config {
     static constexpr int kES = sizeof(TA);
     static constexpr int kBK = 128 / kES;
     static constexpr int kUmmaK = 32 / kES;
-    static constexpr int kS = 5;          // stages of (dequantised weight tile, activation tile)
-    static constexpr int kSW = 4;         // raw int8 weight stages
+#ifndef SDVK_GEMM2_STAGES
+#define SDVK_GEMM2_STAGES 5
+#endif
+#ifndef SDVK_GEMM2_RAW_STAGES
+#define SDVK_GEMM2_RAW_STAGES 4
+#endif
+    static constexpr int kS = SDVK_GEMM2_STAGES;       // stages of (dequantised weight tile, activation tile)
+    static constexpr int kSW = SDVK_GEMM2_RAW_STAGES;  // raw int8 weight stages
     static constexpr int kAcc = 2;
     static constexpr int kABytes = kBW * 128;
     static constexpr int kXBytes = kBXC * 128;
