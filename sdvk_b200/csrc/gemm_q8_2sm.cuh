@@ -68,7 +68,10 @@ struct Gemm2Config {
     static constexpr int kThreads = 512;
     // dequantiser groups (stages round-robin); bf16's dequantisation goes through fp32 and needs
     // the registers of a two-group split
-    static constexpr int kDqGroups = std::is_same<TA, __nv_bfloat16>::value ? 2 : 4;
+#ifndef SDVK_GEMM2_DQ_GROUPS
+#define SDVK_GEMM2_DQ_GROUPS 4
+#endif
+    static constexpr int kDqGroups = std::is_same<TA, __nv_bfloat16>::value ? 2 : SDVK_GEMM2_DQ_GROUPS;
     static constexpr int kDqWarps = 8 / kDqGroups;  // warps per group
     static constexpr int kConvThreads = 32 * kDqWarps;
     static constexpr int kChunksPerRow = kBK / 16;
