@@ -505,15 +505,18 @@ class ConvWorkload:
         self.B, self.cin, self.cout, self.H, self.W = B, cin, cout, H, W
         P, K = H * W, cin * 9
         self.flop = 2.0 * B * cout * P * K
-        self.bytes = B * (2.0 * cin * P + 4.0 * cout * P) + cout * K * (1 + 4 / 32)
+        self.bytes = B * (2.0 * cin * P + 4.0 * cout * P) + cout * K * 2
         self.bound = "tensor"
         self.metric = f"Q8_0 conv3x3 TFLOP/s @B{B} {cin}->{cout} {H}x{W}"
         self.describe = (f"3x3 convolution, Q8_0 weight [{cout}, {cin}*9] (config-0 distribution), {B} images of "
-                         f"{cin}x{H}x{W} fp16 ~N(0,1), fp32 out + bias, im2col + NN GEMM")
+                         f"{cin}x{H}x{W} fp16 ~N(0,1), fp32 out + bias; step: the implicit GEMM as the UNet runs it "
+                         f"(sdvk_conv3x3_nhwc: TMA im2col loads from the channels-last input its producer writes, "
+                         f"weights repacked to fp16 at load time); e2e: sdvk_conv3x3_q8 from channel-major x and "
+                         f"the Q8_0 weight, both conversions inside every call")
         self.rotate = max(2, -(-2 * L2_BYTES // int(self.bytes)))
         self.cpu_units = cout
         self.cpu_what = "output channels of image 0 (fp32 restatement of im2col.comp + gemm_nn_q8_v.comp)"
-        self.launches_per_step = 2 * B
+        self.launches_per_step = 1
 
     def make_set(self, torch, device, seed):
         g = torch.Generator(device=device)
@@ -528,28 +531,33 @@ class ConvWorkload:
 
         nbytes = sdvk_b200.Context.conv3x3_workspace(self.cin, self.H, self.W, 1, sdvk_b200.F16)
         ws = torch.empty((nbytes,), dtype=torch.uint8, device=device)
-        return x, q, s, bias, y, ws
+        from sdvk_b200 import torch_ops
 
-    def _call(self, ctx, st):
-        import sdvk_b200
-
-        x, q, s, bias, y, ws = st
-        ctx.conv3x3_q8(x.data_ptr(), sdvk_b200.F16, q.data_ptr(), s.data_ptr(), bias.data_ptr(), y.data_ptr(),
-                       sdvk_b200.F32, self.B, self.cin, self.cout, self.H, self.W, 1, -1, ws.data_ptr(), ws.numel())
+        xcl = x.permute(0, 2, 3, 1).contiguous()  # what the producer (GroupNorm+SiLU) writes in the UNet
+        w16 = torch_ops.conv3x3_weights_f16(q, s)  # the load-time repack
+        return x, q, s, bias, y, ws, xcl, w16
 
     def step(self, torch_ops, st):
-        self._call(torch_ops.context(st[0].device), st)
+        import sdvk_b200
+
+        x, q, s, bias, y, ws, xcl, w16 = st
+        torch_ops.context(x.device).conv3x3_nhwc(xcl.data_ptr(), w16.data_ptr(), bias.data_ptr(), 0, False,
+                                                 y.data_ptr(), sdvk_b200.F32, self.B, self.cin, self.cout, self.H,
+                                                 self.W, 1, -1)
 
     def e2e(self, sdvk_b200, ctx, torch, st):
-        """Per step: pinned x -> device, convolution, device y -> pinned host."""
-        x, y = st[0], st[4]
+        """Per step: pinned x -> device, sdvk_conv3x3_q8 (channels-last copy, weight repack, implicit GEMM),
+        device y -> pinned host."""
+        x, q, s, bias, y, ws = st[:6]
         xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
         xh.copy_(x.cpu())
         yh = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
 
         def run():
             ctx.upload_async(x.data_ptr(), xh.data_ptr(), xh.numel() * 2)
-            self._call(ctx, st)
+            ctx.conv3x3_q8(x.data_ptr(), sdvk_b200.F16, q.data_ptr(), s.data_ptr(), bias.data_ptr(), y.data_ptr(),
+                           sdvk_b200.F32, self.B, self.cin, self.cout, self.H, self.W, 1, -1, ws.data_ptr(),
+                           ws.numel())
             ctx.download_async(yh.data_ptr(), y.data_ptr(), yh.numel() * 4)
 
         return run, xh.numel() * 2, yh.numel() * 4, "sdvk_upload_async + sdvk_conv3x3_q8 + sdvk_download_async"

@@ -350,11 +350,6 @@ SDVK_API int sdvk_sampler_scale(sdvk_ctx* ctx, const float* x, float* out, uint6
  * module: it replaces the host-side split when the raw blocks are uploaded as they are. */
 SDVK_API int sdvk_q8_0_ingest(sdvk_ctx* ctx, const void* blocks, uint64_t rows, uint64_t cols, int8_t* q,
                               uint64_t ldq, float* scales);
-/* GroupNorm over x[batch][C][P] (channel-major, P = H*W) with G groups of C/G channels
- * (groupnorm.comp, gnInto sdvkgen.cpp:1105-1113; the reference runs batch 1): per (image, group)
- * mean and population variance, y = (x - mean)/sqrt(var + eps)*gamma[c] + beta[c], then
- * y/(1 + e^-y) when silu != 0.  fp32 in and out; y may alias x.  workspace: device memory of at
- * least sdvk_groupnorm_workspace(batch, C, P, G) bytes, 16-byte aligned. */
 /* 3x3 convolution with a Q8_0 weight (conv3RawInto / conv3s2, sdvkgen.cpp:1133-1175: im2col.comp or
  * im2col_s2.comp, then gemmNnQ8 with ldc = P, then biasAddCh).  x: x_dtype (F16, BF16 or F32)
  * [batch][cin][H][W]; q: int8 [cout][cin*9] (k = c*9 + ky*3 + kx; cin*9 % 32 == 0) with fp32 scales
@@ -367,10 +362,40 @@ SDVK_API uint64_t sdvk_conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, i
 SDVK_API int sdvk_conv3x3_q8(sdvk_ctx* ctx, const void* x, int x_dtype, const int8_t* q, const float* s,
                              const float* bias, void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout,
                              uint32_t H, uint32_t W, int stride, int pad_off, void* workspace, uint64_t workspace_bytes);
+/* The same convolution as an implicit GEMM, without the column matrix: TMA im2col-mode loads read the
+ * input windows from a channels-last fp16 x [batch][H][W][cin] (replacing im2col.comp + gemmNnQ8 in
+ * conv3RawInto / conv3s2, sdvkgen.cpp:1133-1175).  sdvk_conv3x3_q8 takes this form by itself for an F16
+ * input when sdvk_conv3x3_implicit_ok holds and its workspace holds x channels-last and the repacked
+ * weights: batch*cin*H*W*2 bytes rounded up to 256, then cout*cin*9*2 (the im2col size of one image
+ * holds both for the UNet's shapes).  Results agree with the im2col form up to fp32 summation order.
+ * sdvk_conv3x3_implicit_ok: 1 when cin % 64 == 0, OH*OW % 128 == 0, stride is 1 or 2, the input has at
+ *   least 128 KB and the environment variable SDVK_CONV_IMPLICIT is not "0"; else 0.
+ * sdvk_conv3x3_weights_f16: w16, fp16 [cout][cin*9], 16-byte aligned, gets
+ *   w16[o][(cb*9 + tap)*64 + j] = q[o][(cb*64 + j)*9 + tap] * scale rounded to fp16 (the value the Q8_0
+ *   GEMMs' dequantiser produces; 64-channel blocks cb, tap = ky*3 + kx).  cin % 64 == 0.
+ * sdvk_conv3x3_nhwc: y (y_dtype F32 or F16, [batch][cout][OH][OW] channel-major, 16-byte aligned) =
+ *   conv(x, w16) + bias[b*bias_stride + o] (bias fp32 or NULL), or += with accumulate (F32 y only).
+ *   SDVK_E_SHAPE when sdvk_conv3x3_implicit_ok does not hold. */
+SDVK_API int sdvk_conv3x3_implicit_ok(uint32_t batch, uint32_t cin, uint32_t H, uint32_t W, int stride);
+SDVK_API int sdvk_conv3x3_weights_f16(sdvk_ctx* ctx, const int8_t* q, const float* s, uint32_t cout, uint32_t cin,
+                                      void* w16);
+SDVK_API int sdvk_conv3x3_nhwc(sdvk_ctx* ctx, const void* x, const void* w16, const float* bias, uint64_t bias_stride,
+                               int accumulate, void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout,
+                               uint32_t H, uint32_t W, int stride, int pad_off);
+/* GroupNorm over x[batch][C][P] (channel-major, P = H*W) with G groups of C/G channels
+ * (groupnorm.comp, gnInto sdvkgen.cpp:1105-1113; the reference runs batch 1): per (image, group)
+ * mean and population variance, y = (x - mean)/sqrt(var + eps)*gamma[c] + beta[c], then
+ * y/(1 + e^-y) when silu != 0.  fp32 in and out; y may alias x.  workspace: device memory of at
+ * least sdvk_groupnorm_workspace(batch, C, P, G) bytes, 16-byte aligned.
+ * sdvk_groupnorm_cl: the same values as fp16, channels-last y[batch][P][C] (C % 32 == 0; y must not
+ * alias x): the layout sdvk_conv3x3_nhwc reads. */
 SDVK_API uint64_t sdvk_groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G);
 SDVK_API int sdvk_groupnorm(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, float* y,
                             uint32_t batch, uint32_t C, uint32_t P, uint32_t G, float eps, int silu, void* workspace,
                             uint64_t workspace_bytes);
+SDVK_API int sdvk_groupnorm_cl(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, void* y,
+                               uint32_t batch, uint32_t C, uint32_t P, uint32_t G, float eps, int silu, void* workspace,
+                               uint64_t workspace_bytes);
 
 /* An NCCL communicator for the context's device.  The reference runs both CFG passes on one device
  * (runPass twice, sdvkgen.cpp:3812-3813); with a GPU pair each rank runs one pass and the halves

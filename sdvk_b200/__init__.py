@@ -169,7 +169,11 @@ SIGNATURES = {
     "sdvk_conv3x3_workspace": (_U64, [_U32, _U32, _U32, _I, _I]),
     "sdvk_conv3x3_q8": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _U32, _U32, _U32, _U32, _U32, _I, _I, _P, _U64]),
     "sdvk_groupnorm_workspace": (_U64, [_U32, _U32, _U32, _U32]),
+    "sdvk_conv3x3_implicit_ok": (_I, [_U32, _U32, _U32, _U32, _I]),
+    "sdvk_conv3x3_weights_f16": (_I, [_P, _P, _P, _U32, _U32, _P]),
+    "sdvk_conv3x3_nhwc": (_I, [_P, _P, _P, _P, _U64, _I, _P, _I, _U32, _U32, _U32, _U32, _U32, _I, _I]),
     "sdvk_groupnorm": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, ctypes.c_float, _I, _P, _U64]),
+    "sdvk_groupnorm_cl": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, ctypes.c_float, _I, _P, _U64]),
     "sdvk_comm_unique_id": (_I, [_P]),
     "sdvk_comm_create": (_I, [_P, _I, _I, _P, _U32, ctypes.POINTER(_P)]),
     "sdvk_comm_destroy": (_I, [_P]),
@@ -396,6 +400,18 @@ class Context:
                                           stride, pad_off, workspace or None, workspace_bytes), "conv3x3_q8")
 
     @staticmethod
+    def conv3x3_implicit_ok(batch: int, cin: int, H: int, W: int, stride: int) -> bool:
+        return bool(lib().sdvk_conv3x3_implicit_ok(batch, cin, H, W, stride))
+
+    def conv3x3_weights_f16(self, q: int, s: int, cout: int, cin: int, w16: int) -> None:
+        self._check(lib().sdvk_conv3x3_weights_f16(self._h, q, s, cout, cin, w16), "conv3x3_weights_f16")
+
+    def conv3x3_nhwc(self, x: int, w16: int, bias: Optional[int], bias_stride: int, accumulate: bool, y: int,
+                     y_dtype: int, batch: int, cin: int, cout: int, H: int, W: int, stride: int, pad_off: int) -> None:
+        self._check(lib().sdvk_conv3x3_nhwc(self._h, x, w16, bias or None, bias_stride, int(accumulate), y, y_dtype,
+                                            batch, cin, cout, H, W, stride, pad_off), "conv3x3_nhwc")
+
+    @staticmethod
     def groupnorm_workspace(batch: int, C: int, P: int, G: int) -> int:
         return lib().sdvk_groupnorm_workspace(batch, C, P, G)
 
@@ -403,6 +419,11 @@ class Context:
                   silu: bool, workspace: int, workspace_bytes: int) -> None:
         self._check(lib().sdvk_groupnorm(self._h, x, gamma, beta, y, batch, C, P, G, eps, int(silu), workspace or None,
                                          workspace_bytes), "groupnorm")
+
+    def groupnorm_cl(self, x: int, gamma: int, beta: int, y: int, batch: int, C: int, P: int, G: int, eps: float,
+                     silu: bool, workspace: int, workspace_bytes: int) -> None:
+        self._check(lib().sdvk_groupnorm_cl(self._h, x, gamma, beta, y, batch, C, P, G, eps, int(silu),
+                                            workspace or None, workspace_bytes), "groupnorm_cl")
 
     def sampler_step(self, desc: SamplerStepDesc) -> None:
         """sdvk_sampler_step: guidance, x0 and the sampler update of one model evaluation."""

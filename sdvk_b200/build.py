@@ -23,7 +23,7 @@ LIB = os.path.join(PKG, "libsdvk_b200.so")
 HOST = os.path.join(PKG, "host")
 ENGINE_LIB = os.path.join(PKG, "libsdvk_engine.so")  # C++ ofc::gpu::Engine mirror over the C ABI
 SOURCES = ["sdvk_abi.cu", "gemm_q8.cu", "attention.cu", "block.cu", "collective.cu", "no_alloc.cu", "ingest.cu", "conv.cu", "sampler.cu", "unet.cu", "table.cu"]
-HEADERS = ["ptx.cuh", "gemm_q8.cuh", "gemm_q8_2sm.cuh", "attention.cuh", "attention_tc.cuh", "attention_fp32.cuh", "attention_tc_short.cuh", "backend.hpp"]
+HEADERS = ["ptx.cuh", "gemm_q8.cuh", "gemm_q8_2sm.cuh", "attention.cuh", "attention_tc.cuh", "attention_fp32.cuh", "attention_tc_short.cuh", "conv_tc2.cuh", "backend.hpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -54,6 +54,12 @@ int geglu_interleave(const int8_t* q, const float* s, const float* bias, uint32_
 // shared-memory opt-in for a kernel (done once per kernel and device).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 bool kernel_smem_attr(const void* kern, int bytes, int device);
+// 3-D tiled tensor map {d0 (contiguous), d1, d2} with byte strides s1, s2 and box {b0, b1, 1}
+// (SDVK_E_SHAPE if the driver rejects it), and the TMA element type of an SDVK dtype.
+int tiled_map_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw, const LaunchEnv& env,
+                 const char* what);
+CUtensorMapDataType tma_dtype(int dt);
 int attention(const sdvk_attn_desc& d, const LaunchEnv& env);
 int layernorm(const float* x, const float* gamma, const float* beta, void* y, int y_dtype, uint32_t rows, uint32_t d,
               uint64_t ldx, uint64_t ldy, float eps, const LaunchEnv& env);
@@ -93,12 +99,35 @@ int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, cons
 int conv3x3_q8_ex(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, uint64_t bias_stride,
                   bool accumulate, void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H,
                   uint32_t W, uint32_t stride, int off, void* workspace, uint64_t ws_bytes, const LaunchEnv& env);
+// The implicit-GEMM form (conv_tc2.cuh): x channels-last fp16 [batch][H][W][cin], w16 the weights
+// repacked by conv_weights_f16, y channel-major [batch][cout][OH][OW] in F16 or F32 (F32 to
+// accumulate), image b's bias at bias + b * sbias.
+struct ConvImplicitDesc {
+    const __half* x;
+    const __half* w16;
+    const float* bias;
+    uint64_t sbias;
+    bool accumulate;
+    void* y;
+    int y_dtype;
+    uint32_t batch, cin, cout, H, W, stride;
+    int off;
+};
+// Whether conv3x3_implicit takes this shape: cin % 64 == 0, OH*OW % 128 == 0, stride 1 or 2, an input of
+// at least 128 KB, and SDVK_CONV_IMPLICIT is not 0.
+bool conv_implicit_ok(uint32_t batch, uint32_t cin, uint32_t H, uint32_t W, uint32_t stride);
+// w16[o][(cb*9 + tap)*64 + j] = fp16(q[o][(cb*64 + j)*9 + tap] * scale), [cout][cin*9]
+int conv_weights_f16(const int8_t* q, const float* s, uint32_t cout, uint32_t cin, __half* w16, const LaunchEnv& env);
+int conv3x3_implicit(const ConvImplicitDesc& d, const LaunchEnv& env);
+// [batch][C][P] fp16 -> [batch][P][C] fp16
+int to_channels_last_f16(const __half* x, __half* y, uint32_t batch, uint32_t C, uint32_t P, const LaunchEnv& env);
 int groupnorm(const float* x, const float* gamma, const float* beta, float* y, uint32_t batch, uint32_t C, uint32_t P,
               uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes, const LaunchEnv& env);
-// The same GroupNorm with y in F32 or F16 (the UNet feeds the F16 form to its convolutions).
+// The same GroupNorm with y in F32 or F16 (the UNet feeds the F16 form to its convolutions); with
+// channels_last, y is F16 [batch][P][C] (C % 32 == 0) holding the same values.
 int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y, int y_dtype, uint32_t batch,
                  uint32_t C, uint32_t P, uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes,
-                 const LaunchEnv& env);
+                 const LaunchEnv& env, bool channels_last = false);
 
 // unet.cu: the SDXL UNet pass over the kernels above.
 int unet_plan(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env);

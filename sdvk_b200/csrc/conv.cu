@@ -8,10 +8,18 @@
 // (off = 0, the VAE encoder's Downsample2D).  The column matrix col[k][p] (p over a band of output rows)
 // goes to a caller-provided workspace in the GEMM's activation type, in bands of output rows that fit
 // it; the GEMM writes the band's output columns with the row stride OH*OW and adds the bias in its
-// epilogue.  An implicit-GEMM form that never materialises col (TMA im2col loads) is the next step.
+// epilogue.
+//
+// The implicit-GEMM form (conv_tc2.cuh) never materialises col: TMA im2col loads read the input
+// windows from a channels-last fp16 copy of x, and the weights are a tap-major fp16 repack of the
+// Q8_0 payload.  sdvk_conv3x3_q8 takes it for fp16 inputs whose shape it handles when the workspace
+// holds the two (x channels-last, then the repacked weights); the UNet keeps both resident.
 #include <algorithm>
+#include <cstdlib>
+#include <mutex>
 
 #include "backend.hpp"
+#include "conv_tc2.cuh"
 #include "ptx.cuh"
 
 namespace sdvk {
@@ -175,7 +183,210 @@ int im2col_any(const void* x, int x_dtype, void* col, uint32_t cin, uint32_t H, 
                          nrows, ld, stride, off, images, xbs, cbs, env);
 }
 
+// ---------------------------------------------------------------- the implicit-GEMM form
+
+PFN_cuTensorMapEncodeIm2col_v12000 im2col_encode_fn() {
+    static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+    });
+    return fn;
+}
+
+// w16[o][(cb*9 + t)*64 + j] = q[o][(cb*64 + j)*9 + t] * scale, both factors as fp16 and one rounded fp16
+// multiply: the value the GEMM's dequantiser writes for the same weight (dequant16<__half>).
+__global__ void conv_weights_f16_kernel(const int8_t* __restrict__ q, const float* __restrict__ s,
+                                        __half* __restrict__ w16, uint32_t cout, uint32_t cin) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    const uint32_t K = cin * 9;
+    const uint64_t n = (uint64_t)cout * K;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t o = (uint32_t)(i / K), kp = (uint32_t)(i % K), ks = kp / 64, j = kp % 64, cb = ks / 9,
+                       t = ks - cb * 9;
+        const uint64_t src = (uint64_t)o * K + (uint64_t)(cb * 64 + j) * 9 + t;
+        w16[i] = __hmul(__float2half_rn((float)q[src]), __float2half_rn(s[src >> 5]));
+    }
+}
+
+// out[b][p][c] = in[b][c][p]: 32 x 32 tiles through shared memory; grid (ceil(P/32), ceil(C/32), B),
+// block (32, 8).
+__global__ void __launch_bounds__(256) channels_last_kernel(const __half* __restrict__ in, __half* __restrict__ out,
+                                                            uint32_t C, uint32_t P) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    __shared__ __half tile[32][34];
+    const uint32_t b = blockIdx.z, c0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
+    const __half* src = in + (uint64_t)b * C * P;
+    __half* dst = out + (uint64_t)b * C * P;
+    for (uint32_t r = threadIdx.y; r < 32; r += 8) {
+        const uint32_t c = c0 + r, pp = p0 + threadIdx.x;
+        if (c < C && pp < P) tile[r][threadIdx.x] = src[(uint64_t)c * P + pp];
+    }
+    __syncthreads();
+    for (uint32_t r = threadIdx.y; r < 32; r += 8) {
+        const uint32_t pp = p0 + r, c = c0 + threadIdx.x;
+        if (c < C && pp < P) dst[(uint64_t)pp * C + c] = tile[threadIdx.x][r];
+    }
+}
+
+// Pair-tile width (tensor-core N = output channels): the candidate with the fewest waves x per-stage
+// cycles, where a stage costs the tensor core's 2*BN cycles or the L2 reads of its operands (16 KB of
+// windows and BN*64 bytes of weights per CTA, at about 60 bytes per cycle per SM), whichever is longer.
+int pick_conv_bn(uint64_t positions, uint32_t cout, int num_sms) {
+    if (const char* e = getenv("SDVK_CONV_BN")) return atoi(e);
+    const uint64_t clusters = (uint64_t)std::max(1, num_sms / 2), mt = (positions + 255) / 256;
+    int best = 256;
+    double best_cost = 1e300;
+    for (int bn : {256, 192, 160, 128, 64, 32}) {
+        const uint64_t tiles = mt * ((cout + bn - 1) / bn), waves = (tiles + clusters - 1) / clusters;
+        const double cost = (double)waves * std::max(2.0 * bn, (16384.0 + 64.0 * bn) / 60.0);
+        if (cost < best_cost) best_cost = cost, best = bn;
+    }
+    return best;
+}
+
+template <int BN, class TC>
+int launch_conv_tc2(const ConvImplicitDesc& d, const LaunchEnv& env) {
+    using Cfg = ConvCfg<BN>;
+    const uint32_t S = d.stride, OH = S == 1 ? d.H : d.H / 2, OW = S == 1 ? d.W : d.W / 2, P = OH * OW;
+    const int lower = S == 1 ? -1 : d.off;
+    auto enc = im2col_encode_fn();
+    if (!enc) return fail(env, SDVK_E_CUDA, "cuTensorMapEncodeIm2col unavailable");
+    // The pixel box holds the window corners of the output positions, (lower + S*o) for o < OW (OH),
+    // walked with traversal stride S; the load's offsets pick the tap.
+    CUtensorMap tmX, tmW, tmC;
+    const cuuint64_t dims[4] = {d.cin, d.W, d.H, d.batch};
+    const cuuint64_t strides[3] = {(uint64_t)d.cin * 2, (uint64_t)d.W * d.cin * 2, (uint64_t)d.H * d.W * d.cin * 2};
+    const int lo[2] = {lower, lower};
+    const int hi[2] = {(int)((OW - 1) * S) + lower - (int)d.W + 1, (int)((OH - 1) * S) + lower - (int)d.H + 1};
+    const cuuint32_t estr[4] = {1, S, S, 1};
+    CUresult r = enc(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(d.x), dims, strides, lo, hi, 64,
+                     128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(env, SDVK_E_SHAPE, "tensor map rejected: conv input windows (im2col)");
+    const uint64_t K = 9ull * d.cin;
+    int rc = tiled_map_3d(&tmW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, d.w16, K, d.cout, 1, K * 2, 0, 64, BN / 2,
+                          CU_TENSOR_MAP_SWIZZLE_128B, env, "conv weights");
+    if (rc) return rc;
+    const uint64_t ces = sizeof(TC);
+    rc = tiled_map_3d(&tmC, tma_dtype(d.y_dtype), d.y, P, d.cout, d.batch, P * ces, (uint64_t)d.cout * P * ces, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, env, "conv output");
+    if (rc) return rc;
+    ConvParams p{};
+    p.bias = d.bias;
+    p.sbias = d.bias ? d.sbias : 0;
+    p.P = P;
+    p.OW = OW;
+    p.batch = d.batch;
+    p.cout = d.cout;
+    p.stride = (int)S;
+    p.lower = lower;
+    p.k_stages = 9 * d.cin / 64;
+    p.tiles_n = (d.cout + BN - 1) / BN;
+    const uint64_t tiles = ((uint64_t)d.batch * P + 255) / 256 * p.tiles_n;
+    if (tiles > 0x7FFFFFFFull) return fail(env, SDVK_E_SHAPE, "convolution too large");
+    p.num_tiles = (uint32_t)tiles;
+    p.accumulate = d.accumulate ? 1u : 0u;
+    p.err = env.err_dev;
+    p.timeout_ns = env.timeout_ns;
+    auto kern = conv3x3_tc2_kernel<BN, TC>;
+    if (!kernel_smem_attr(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, env.device))
+        return fail(env, SDVK_E_CUDA, "cudaFuncSetAttribute(max dynamic smem) failed");
+    const uint32_t clusters = std::min<uint32_t>(p.num_tiles, (uint32_t)env.num_sms / 2);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = env.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_check(env, cudaLaunchKernelEx(&cfg, kern, tmX, tmW, tmC, p), "conv3x3_tc2_kernel launch");
+}
+
+template <class TC>
+int launch_conv_bn(const ConvImplicitDesc& d, int bn, const LaunchEnv& env) {
+    switch (bn) {
+        case 32: return launch_conv_tc2<32, TC>(d, env);
+        case 64: return launch_conv_tc2<64, TC>(d, env);
+        case 128: return launch_conv_tc2<128, TC>(d, env);
+        case 160: return launch_conv_tc2<160, TC>(d, env);
+        case 192: return launch_conv_tc2<192, TC>(d, env);
+        case 256: return launch_conv_tc2<256, TC>(d, env);
+        default: return fail(env, SDVK_E_ARG, "conv tile width must be 32, 64, 128, 160, 192 or 256");
+    }
+}
+
+// Shared argument checks of both forms (the explicit one's order: pointers, dtypes, stride, padding).
+int check_conv(const void* x, int x_dtype, const void* w, const void* y, int y_dtype, bool accumulate, uint32_t stride,
+               int& off, const LaunchEnv& env) {
+    if (!x || !w || !y) return fail(env, SDVK_E_ARG, "null pointer");
+    if (accumulate && y_dtype != SDVK_F32) return fail(env, SDVK_E_ARG, "an accumulating conv needs an F32 output");
+    if (x_dtype != SDVK_F16 && x_dtype != SDVK_BF16 && x_dtype != SDVK_F32)
+        return fail(env, SDVK_E_ARG, "conv input must be F16, BF16 or F32");
+    if (y_dtype != SDVK_F16 && y_dtype != SDVK_F32) return fail(env, SDVK_E_ARG, "conv output must be F16 or F32");
+    if (stride != 1 && stride != 2) return fail(env, SDVK_E_SHAPE, "conv stride must be 1 or 2");
+    if (stride == 1) off = -1;
+    if (off != -1 && off != 0) return fail(env, SDVK_E_SHAPE, "conv padding offset must be -1 or 0");
+    return SDVK_OK;
+}
+
 }  // namespace
+
+bool conv_implicit_ok(uint32_t batch, uint32_t cin, uint32_t H, uint32_t W, uint32_t stride) {
+    if (const char* e = getenv("SDVK_CONV_IMPLICIT"))
+        if (e[0] == '0') return false;
+    if ((stride != 1 && stride != 2) || batch == 0 || cin == 0 || cin % 64 || H == 0 || W == 0) return false;
+    const uint64_t OH = stride == 1 ? H : H / 2, OW = stride == 1 ? W : W / 2, P = OH * OW;
+    if (P == 0 || P % 128 || P > 0xFFFFFFFFull || H > 0x7FFFFFFF || W > 0x7FFFFFFF) return false;
+    // Inputs under 128 KB go the explicit way: CUTLASS adjusts im2col tensor maps of such small
+    // tensors on drivers up to 13.1, and nothing here needs the implicit form at that size.
+    return (uint64_t)batch * cin * H * W * 2 >= (128u << 10);
+}
+
+int conv_weights_f16(const int8_t* q, const float* s, uint32_t cout, uint32_t cin, __half* w16, const LaunchEnv& env) {
+    if (!q || !s || !w16) return fail(env, SDVK_E_ARG, "null pointer");
+    if (cin % 64) return fail(env, SDVK_E_SHAPE, "the repacked conv weights need cin % 64 == 0");
+    const uint64_t n = (uint64_t)cout * cin * 9;
+    if (n == 0) return SDVK_OK;
+    return launch_pdl(conv_weights_f16_kernel, dim3((uint32_t)std::min<uint64_t>((n + 255) / 256, 148ull * 16)),
+                      dim3(256), 0, env, "conv_weights_f16_kernel launch", q, s, w16, cout, cin);
+}
+
+int to_channels_last_f16(const __half* x, __half* y, uint32_t batch, uint32_t C, uint32_t P, const LaunchEnv& env) {
+    if (!x || !y) return fail(env, SDVK_E_ARG, "null pointer");
+    if (batch == 0 || C == 0 || P == 0) return SDVK_OK;
+    if (batch > 65535 || (C + 31) / 32 > 65535) return fail(env, SDVK_E_SHAPE, "too many images or channels");
+    return launch_pdl(channels_last_kernel, dim3((P + 31) / 32, (C + 31) / 32, batch), dim3(32, 8), 0, env,
+                      "channels_last_kernel launch", x, y, C, P);
+}
+
+int conv3x3_implicit(const ConvImplicitDesc& d, const LaunchEnv& env) {
+    int off = d.off;
+    if (int rc = check_conv(d.x, SDVK_F16, d.w16, d.y, d.y_dtype, d.accumulate, d.stride, off, env)) return rc;
+    if (d.batch == 0 || d.cout == 0 || d.H == 0 || d.W == 0) return SDVK_OK;
+    if (d.batch > 0x7FFFFFFFu || d.cout > 0xFFFFu * 256)
+        return fail(env, SDVK_E_SHAPE, "too many images or output channels");
+    if (!conv_implicit_ok(d.batch, d.cin, d.H, d.W, d.stride))
+        return fail(env, SDVK_E_SHAPE,
+                    "the implicit conv needs cin % 64 == 0, OH*OW % 128 == 0 and an input of at least 128 KB");
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (!a16(d.x) || !a16(d.w16) || !a16(d.y)) return fail(env, SDVK_E_SHAPE, "operands must be 16-byte aligned");
+    ConvImplicitDesc e = d;
+    e.off = off;
+    const uint32_t OH = d.stride == 1 ? d.H : d.H / 2, OW = d.stride == 1 ? d.W : d.W / 2;
+    const int bn = pick_conv_bn((uint64_t)d.batch * OH * OW, d.cout, env.num_sms);
+    if (d.y_dtype == SDVK_F32) return launch_conv_bn<float>(e, bn, env);
+    return launch_conv_bn<__half>(e, bn, env);
+}
 
 uint64_t conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, uint32_t stride, int dtype) {
     if (stride != 1 && stride != 2) return 0;
@@ -186,6 +397,21 @@ uint64_t conv3x3_workspace(uint32_t cin, uint32_t H, uint32_t W, uint32_t stride
 int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, void* y, int y_dtype,
                uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W, uint32_t stride, int off,
                void* workspace, uint64_t ws_bytes, const LaunchEnv& env) {
+    if (int rc = check_conv(x, x_dtype, q, y, y_dtype, false, stride, off, env)) return rc;
+    if (!s) return fail(env, SDVK_E_ARG, "null pointer");
+    // The implicit form when the input is fp16, the shape is one it takes and the workspace holds x
+    // channels-last and the repacked weights; the explicit form otherwise.
+    const uint64_t xb = ((uint64_t)batch * cin * H * W * 2 + 255) & ~uint64_t(255), wb = (uint64_t)cout * cin * 9 * 2;
+    if (x_dtype == SDVK_F16 && cout > 0 && conv_implicit_ok(batch, cin, H, W, stride) && workspace &&
+        (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 && ws_bytes >= xb + wb &&
+        (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0) {
+        __half* xcl = static_cast<__half*>(workspace);
+        __half* w16 = reinterpret_cast<__half*>(static_cast<uint8_t*>(workspace) + xb);
+        if (int rc = to_channels_last_f16(static_cast<const __half*>(x), xcl, batch, cin, H * W, env)) return rc;
+        if (int rc = conv_weights_f16(q, s, cout, cin, w16, env)) return rc;
+        ConvImplicitDesc d{xcl, w16, bias, 0, false, y, y_dtype, batch, cin, cout, H, W, stride, off};
+        return conv3x3_implicit(d, env);
+    }
     return conv3x3_q8_ex(x, x_dtype, q, s, bias, 0, false, y, y_dtype, batch, cin, cout, H, W, stride, off, workspace,
                          ws_bytes, env);
 }
@@ -193,14 +419,8 @@ int conv3x3_q8(const void* x, int x_dtype, const int8_t* q, const float* s, cons
 int conv3x3_q8_ex(const void* x, int x_dtype, const int8_t* q, const float* s, const float* bias, uint64_t bias_stride,
                   bool accumulate, void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H,
                   uint32_t W, uint32_t stride, int off, void* workspace, uint64_t ws_bytes, const LaunchEnv& env) {
-    if (!x || !q || !s || !y) return fail(env, SDVK_E_ARG, "null pointer");
-    if (accumulate && y_dtype != SDVK_F32) return fail(env, SDVK_E_ARG, "an accumulating conv needs an F32 output");
-    if (x_dtype != SDVK_F16 && x_dtype != SDVK_BF16 && x_dtype != SDVK_F32)
-        return fail(env, SDVK_E_ARG, "conv input must be F16, BF16 or F32");
-    if (y_dtype != SDVK_F16 && y_dtype != SDVK_F32) return fail(env, SDVK_E_ARG, "conv output must be F16 or F32");
-    if (stride != 1 && stride != 2) return fail(env, SDVK_E_SHAPE, "conv stride must be 1 or 2");
-    if (stride == 1) off = -1;
-    if (off != -1 && off != 0) return fail(env, SDVK_E_SHAPE, "conv padding offset must be -1 or 0");
+    if (int rc = check_conv(x, x_dtype, q, y, y_dtype, accumulate, stride, off, env)) return rc;
+    if (!s) return fail(env, SDVK_E_ARG, "null pointer");
     if (batch == 0 || cout == 0 || H == 0 || W == 0) return SDVK_OK;
     const uint32_t K = cin * 9;
     if (cin == 0 || K % 32) return fail(env, SDVK_E_SHAPE, "conv needs cin*9 % 32 == 0 (whole Q8_0 blocks)");

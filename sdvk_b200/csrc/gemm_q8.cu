@@ -320,6 +320,12 @@ int geglu_interleave(const int8_t* q, const float* s, const float* bias, uint32_
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
+int tiled_map_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw, const LaunchEnv& env,
+                 const char* what) {
+    return make_map(m, dt, base, d0, d1, d2, s1, s2, b0, b1, sw, env, what);
+}
+CUtensorMapDataType tma_dtype(int dt) { return tma_type(dt); }
 bool kernel_smem_attr(const void* kern, int bytes, int device) { return set_smem_attr(kern, bytes, device); }
 
 int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env) {

@@ -140,6 +140,44 @@ __global__ void __launch_bounds__(kGnThreads) gn_stats_kernel(const float* __res
     if (threadIdx.x == 0) stats[((uint64_t)b * G + g) * chunks + blockIdx.x] = GnStat{n, mean, m2};
 }
 
+// One warp: (mean, 1/sqrt(var + eps)) of a group from its chunk statistics.  Lane l merges chunks l,
+// l+32, ... in order (Chan et al.'s pairwise update of count, mean and M2), then a fixed butterfly over
+// the lanes in which both partners merge the pair in the same order (lower lane first), so every lane,
+// and every CTA that merges the same group, gets the same result.
+__device__ __forceinline__ float2 gn_group_norm(const GnStat* __restrict__ st, uint32_t chunks, float eps) {
+    const uint32_t lane = threadIdx.x & 31;
+    float n = 0.0f, m = 0.0f, m2 = 0.0f;
+    auto merge = [](float& n, float& m, float& m2, float on, float om, float om2) {
+        if (on == 0.0f) return;
+        const float nn = n + on, d = om - m;
+        m += d * (on / nn);
+        m2 += om2 + d * d * (n * on / nn);
+        n = nn;
+    };
+    for (uint32_t k = lane; k < chunks; k += 32) merge(n, m, m2, st[k].n, st[k].mean, st[k].m2);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float on = __shfl_xor_sync(0xffffffffu, n, o), om = __shfl_xor_sync(0xffffffffu, m, o),
+                    om2 = __shfl_xor_sync(0xffffffffu, m2, o);
+        if ((lane & o) == 0) {
+            merge(n, m, m2, on, om, om2);
+        } else {
+            float pn = on, pm = om, pm2 = om2;
+            merge(pn, pm, pm2, n, m, m2);
+            n = pn, m = pm, m2 = pm2;
+        }
+    }
+    return make_float2(m, 1.0f / sqrtf(m2 / n + eps));
+}
+
+// GroupNorm's output value (x - mean) * sc + sh, then SiLU v / (1 + e^-v) with the fast exponential and a
+// correctly rounded reciprocal (a few ulp, against a full division and expf that made the apply pass
+// issue-bound rather than HBM-bound).
+__device__ __forceinline__ float gn_out(float v, float mean, float sc, float sh, uint32_t act) {
+    v = (v - mean) * sc + sh;
+    return act ? v * __frcp_rn(1.0f + __expf(-v)) : v;
+}
+
 // grid (C, B): one channel row of one image per CTA.  Warp 0 merges the channel's group statistics
 // (Chan et al.'s pairwise update of count, mean and M2, in a fixed order) into (mean,
 // 1/sqrt(var + eps)), then the CTA writes y = (x - mean) * rstd * gamma[c] + beta[c] (+ SiLU
@@ -155,44 +193,15 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(const float* __res
     __shared__ float2 norm;
     const uint32_t c = blockIdx.x, b = blockIdx.y, g = c / (C / G);
     if (threadIdx.x < 32) {
-        // Warp 0: lane l merges chunks l, l+32, ... in order, then a fixed butterfly over the lanes
-        // (every CTA of the group computes the same result in the same order).
-        const GnStat* st = stats + ((uint64_t)b * G + g) * chunks;
-        float n = 0.0f, m = 0.0f, m2 = 0.0f;
-        auto merge = [](float& n, float& m, float& m2, float on, float om, float om2) {
-            if (on == 0.0f) return;
-            const float nn = n + on, d = om - m;
-            m += d * (on / nn);
-            m2 += om2 + d * d * (n * on / nn);
-            n = nn;
-        };
-        for (uint32_t k = threadIdx.x; k < chunks; k += 32) merge(n, m, m2, st[k].n, st[k].mean, st[k].m2);
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float on = __shfl_xor_sync(0xffffffffu, n, o), om = __shfl_xor_sync(0xffffffffu, m, o),
-                        om2 = __shfl_xor_sync(0xffffffffu, m2, o);
-            // both partners merge the pair in the same order (lower lane first), so they agree
-            if ((threadIdx.x & o) == 0) {
-                merge(n, m, m2, on, om, om2);
-            } else {
-                float pn = on, pm = om, pm2 = om2;
-                merge(pn, pm, pm2, n, m, m2);
-                n = pn, m = pm, m2 = pm2;
-            }
-        }
-        if (threadIdx.x == 0) norm = make_float2(m, 1.0f / sqrtf(m2 / n + eps));
+        const float2 r = gn_group_norm(stats + ((uint64_t)b * G + g) * chunks, chunks, eps);
+        if (threadIdx.x == 0) norm = r;
     }
     __syncthreads();
     const float mean = norm.x, sc = norm.y * gamma[c], sh = beta[c];
     const uint64_t off = ((uint64_t)b * C + c) * P;
     const float* xr = x + off;
     TY* yr = y + off;
-    // SiLU with the fast exponential and a correctly rounded reciprocal (a few ulp, against a full
-    // division and expf that made the apply pass issue-bound rather than HBM-bound)
-    auto f = [&](float v) {
-        v = (v - mean) * sc + sh;
-        return act ? v * __frcp_rn(1.0f + __expf(-v)) : v;
-    };
+    auto f = [&](float v) { return gn_out(v, mean, sc, sh, act); };
     if (vec) {
 #pragma unroll 4
         for (uint32_t i = 4 * threadIdx.x; i < P; i += 4 * kGnThreads) {
@@ -207,6 +216,54 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(const float* __res
         }
     } else {
         for (uint32_t i = threadIdx.x; i < P; i += kGnThreads) yr[i] = TY(f(xr[i]));
+    }
+}
+
+// The same values written channels-last, y[b][p][c] fp16 (the implicit convolution's input and the
+// spatial transformer's token layout).  grid (ceil(P / 128), C / 32, B), block (32, 8): 32 channels x
+// 128 positions per CTA, through 32 x 32 shared-memory tiles; the warps first merge the statistics of
+// the tile's groups (gn_group_norm, so the values equal gn_apply_kernel's bit for bit).  C % 32 == 0.
+__global__ void __launch_bounds__(kGnThreads) gn_apply_cl_kernel(const float* __restrict__ x,
+                                                                 const float* __restrict__ gamma,
+                                                                 const float* __restrict__ beta, __half* __restrict__ y,
+                                                                 uint32_t C, uint32_t P, uint32_t G, float eps,
+                                                                 uint32_t act, const GnStat* __restrict__ stats,
+                                                                 uint32_t chunks) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    __shared__ float2 gnorm[32];
+    __shared__ float cm[32], csc[32], csh[32];
+    __shared__ float tile[32][33];
+    const uint32_t b = blockIdx.z, c0 = blockIdx.y * 32, p0 = blockIdx.x * 128;
+    const uint32_t tx = threadIdx.x, ty = threadIdx.y, cpg = C / G;
+    const uint32_t g_lo = c0 / cpg, g_hi = (c0 + 31) / cpg;
+    for (uint32_t g = g_lo + ty; g <= g_hi; g += 8) {
+        const float2 r = gn_group_norm(stats + ((uint64_t)b * G + g) * chunks, chunks, eps);
+        if (tx == 0) gnorm[g - g_lo] = r;
+    }
+    __syncthreads();
+    if (ty == 0) {
+        const uint32_t c = c0 + tx;
+        const float2 r = gnorm[c / cpg - g_lo];
+        cm[tx] = r.x, csc[tx] = r.y * gamma[c], csh[tx] = beta[c];
+    }
+    __syncthreads();
+    const float* xb = x + ((uint64_t)b * C + c0) * P;
+    __half* yb = y + (uint64_t)b * P * C + c0;
+#pragma unroll 1
+    for (uint32_t sub = 0; sub < 128; sub += 32) {
+        const uint32_t ps = p0 + sub;
+        if (ps >= P) break;
+        for (uint32_t r = ty; r < 32; r += 8) {
+            const uint32_t pp = ps + tx;
+            if (pp < P) tile[r][tx] = gn_out(__ldcs(xb + (uint64_t)r * P + pp), cm[r], csc[r], csh[r], act);
+        }
+        __syncthreads();
+        for (uint32_t r = ty; r < 32; r += 8) {
+            const uint32_t pp = ps + r;
+            if (pp < P) yb[(uint64_t)pp * C + tx] = __float2half_rn(tile[tx][r]);
+        }
+        __syncthreads();
     }
 }
 
@@ -243,9 +300,11 @@ int groupnorm(const float* x, const float* gamma, const float* beta, float* y, u
 
 int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y, int y_dtype, uint32_t batch,
                  uint32_t C, uint32_t P, uint32_t G, float eps, uint32_t act, void* workspace, uint64_t ws_bytes,
-                 const LaunchEnv& env) {
+                 const LaunchEnv& env, bool channels_last) {
     if (!x || !gamma || !beta || !y) return fail(env, SDVK_E_ARG, "null pointer");
     if (y_dtype != SDVK_F32 && y_dtype != SDVK_F16) return fail(env, SDVK_E_ARG, "GroupNorm output must be F32 or F16");
+    if (channels_last && (y_dtype != SDVK_F16 || C % 32 || (C / 32) > 65535 || batch > 65535))
+        return fail(env, SDVK_E_SHAPE, "the channels-last GroupNorm writes F16 and needs C % 32 == 0");
     if (batch == 0 || C == 0 || P == 0) return SDVK_OK;
     if (G == 0 || C % G || G > 65535 || batch > 65535)
         return fail(env, SDVK_E_SHAPE, "GroupNorm needs C % G == 0 and at most 65535 groups and images");
@@ -260,6 +319,10 @@ int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y,
     if (int rc = launch_pdl(gn_stats_kernel, dim3(chunks, G, batch), dim3(kGnThreads), 0, env, "gn_stats_kernel launch",
                             x, C, P, G, vec, st))
         return rc;
+    if (channels_last)
+        return launch_pdl(gn_apply_cl_kernel, dim3((P + 127) / 128, C / 32, batch), dim3(32, 8), 0, env,
+                          "gn_apply_cl_kernel launch", x, gamma, beta, static_cast<__half*>(y), C, P, G, eps, act,
+                          (const GnStat*)st, chunks);
     if (y_dtype == SDVK_F16)
         return launch_pdl(gn_apply_kernel<__half>, dim3(C, batch), dim3(kGnThreads), 0, env, "gn_apply_kernel launch",
                           x, gamma, beta, static_cast<__half*>(y), C, P, G, eps, act, (const GnStat*)st, chunks,

@@ -366,6 +366,18 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
 }
+// TMA im2col-mode load of a 4-D channels-last tensor {c, w, h, n} into this CTA's shared memory,
+// counted on an mbarrier that may live in the peer CTA: the tensor map's pixelsPerColumn pixels,
+// walked through its pixel box from the window corner (w, h) of image n, each read at the offset
+// (dw, dh) from its corner, channelsPerPixel channels from channel c each (zero outside the tensor).
+__device__ __forceinline__ void tma_load_im2col_4d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
+                                                        int c, int w, int h, int n, uint16_t dw, uint16_t dh) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.im2col.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c), "r"(w), "r"(h), "r"(n), "h"(dw), "h"(dh)
+        : "memory");
+}
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                  "r"(ncols)

@@ -705,6 +705,29 @@ int sdvk_conv3x3_q8(sdvk_ctx* ctx, const void* x, int x_dtype, const int8_t* q, 
                             stride > 0 ? (uint32_t)stride : 0u, pad_off, workspace, workspace_bytes, env_of(ctx));
 }
 
+int sdvk_conv3x3_implicit_ok(uint32_t batch, uint32_t cin, uint32_t H, uint32_t W, int stride) {
+    return stride > 0 && sdvk::conv_implicit_ok(batch, cin, H, W, (uint32_t)stride) ? 1 : 0;
+}
+
+int sdvk_conv3x3_weights_f16(sdvk_ctx* ctx, const int8_t* q, const float* s, uint32_t cout, uint32_t cin, void* w16) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    if (w16 && (reinterpret_cast<uintptr_t>(w16) & 15u))
+        return sdvk::fail(env_of(ctx), SDVK_E_SHAPE, "w16 must be 16-byte aligned");
+    return sdvk::conv_weights_f16(q, s, cout, cin, static_cast<__half*>(w16), env_of(ctx));
+}
+
+int sdvk_conv3x3_nhwc(sdvk_ctx* ctx, const void* x, const void* w16, const float* bias, uint64_t bias_stride,
+                      int accumulate, void* y, int y_dtype, uint32_t batch, uint32_t cin, uint32_t cout, uint32_t H,
+                      uint32_t W, int stride, int pad_off) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    sdvk::ConvImplicitDesc d{static_cast<const __half*>(x), static_cast<const __half*>(w16), bias, bias_stride,
+                             accumulate != 0, y, y_dtype, batch, cin, cout, H, W,
+                             stride > 0 ? (uint32_t)stride : 0u, pad_off};
+    return sdvk::conv3x3_implicit(d, env_of(ctx));
+}
+
 uint64_t sdvk_groupnorm_workspace(uint32_t batch, uint32_t C, uint32_t P, uint32_t G) {
     return sdvk::groupnorm_workspace(batch, C, P, G);
 }
@@ -715,6 +738,15 @@ int sdvk_groupnorm(sdvk_ctx* ctx, const float* x, const float* gamma, const floa
     if (int rc = use_device(ctx)) return rc;
     return sdvk::groupnorm(x, gamma, beta, y, batch, C, P, G, eps, silu ? 1u : 0u, workspace, workspace_bytes,
                            env_of(ctx));
+}
+
+int sdvk_groupnorm_cl(sdvk_ctx* ctx, const float* x, const float* gamma, const float* beta, void* y, uint32_t batch,
+                      uint32_t C, uint32_t P, uint32_t G, float eps, int silu, void* workspace,
+                      uint64_t workspace_bytes) {
+    if (!ctx) return SDVK_E_ARG;
+    if (int rc = use_device(ctx)) return rc;
+    return sdvk::groupnorm_ex(x, gamma, beta, y, SDVK_F16, batch, C, P, G, eps, silu ? 1u : 0u, workspace,
+                              workspace_bytes, env_of(ctx), true);
 }
 
 int sdvk_comm_unique_id(void* id) { return sdvk::comm_unique_id(id); }

@@ -5,11 +5,13 @@
 //
 // Activations between modules are fp32 channel-major [B][C][H][W], as in the reference.  Per module:
 //   ResBlock     h = conv1(GN+SiLU(x)) + (b1 + emb_proj[b]);  out = skip(x) + conv2(GN+SiLU(h))
-//                GN writes fp16, the convolutions are im2col + the Q8_0 NN GEMM; the per-image bias of
+//                GN writes fp16 channels-last for the implicit-GEMM convolutions (conv_tc2.cuh, fp16
+//                weights repacked from the Q8_0 payload at prepare time); shapes the implicit form does
+//                not take keep channel-major fp16, im2col and the Q8_0 NN GEMM.  The per-image bias of
 //                conv1 is one accumulating GEMM for every ResBlock of the pass (all emb_layers weights
 //                lie back to back), and conv2 reduce-adds into the skip path's output.
-//   Transformer  g = GN(x) (fp16) -> tokens-major -> t = proj_in(g) (fp32 [B*P][C]) -> N blocks in place
-//                -> fp16 channel-major -> x += proj_out(.) (an accumulating NN GEMM)
+//   Transformer  g = GN(x) (fp16, written tokens-major) -> t = proj_in(g) (fp32 [B*P][C]) -> N blocks in
+//                place -> fp16 channel-major -> x += proj_out(.) (an accumulating NN GEMM)
 //   Down / up    stride-2 conv; nearest 2x upsample fused into the fp32 -> fp16 conversion, then conv
 //   conv_in      the 4 latent channels are zero-padded to 32 (cin*9 must hold whole Q8_0 blocks); the
 //                weight's padded columns are zero, so the result is the 4-channel convolution.
@@ -89,6 +91,30 @@ __global__ void to_f16_kernel(const float* __restrict__ x, __half* __restrict__ 
         const uint32_t c = (uint32_t)(r % Cout), b = (uint32_t)(r / Cout);
         const float v = c < Cin ? x[(((uint64_t)b * Cin + c) * H + (oh >> up)) * W + (ow >> up)] : 0.0f;
         y[i] = __float2half_rn(v);
+    }
+}
+
+// The same conversion written channels-last, y[b][oh][ow][c] = x[b][c][oh >> up][ow >> up]: 32 channels x
+// 32 output positions per tile through shared memory, coalesced on both sides.
+// grid (ceil(OH*OW / 32), ceil(C / 32), B), block (32, 8).
+__global__ void __launch_bounds__(256) to_f16_cl_kernel(const float* __restrict__ x, __half* __restrict__ y, uint32_t C,
+                                                        uint32_t H, uint32_t W, uint32_t up) {
+    grid_dependency_wait();
+    grid_launch_dependents();
+    __shared__ float tile[32][33];
+    const uint32_t OW = W << up, OP = (H << up) * OW;
+    const uint32_t b = blockIdx.z, c0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
+    for (uint32_t r = threadIdx.y; r < 32; r += 8) {
+        const uint32_t c = c0 + r, pp = p0 + threadIdx.x;
+        if (c < C && pp < OP) {
+            const uint32_t oh = pp / OW, ow = pp - oh * OW;
+            tile[r][threadIdx.x] = x[(((uint64_t)b * C + c) * H + (oh >> up)) * W + (ow >> up)];
+        }
+    }
+    __syncthreads();
+    for (uint32_t r = threadIdx.y; r < 32; r += 8) {
+        const uint32_t pp = p0 + r, c = c0 + threadIdx.x;
+        if (c < C && pp < OP) y[((uint64_t)b * OP + pp) * C + c] = __float2half_rn(tile[threadIdx.x][r]);
     }
 }
 
@@ -227,6 +253,8 @@ struct sdvk_unet {
     };
     struct Lin {  // a Q8 weight, its optional bias, by tensor index
         int w = -1, b = -1;
+        int64_t h = -1;  // 3x3 convs with cin % 64 == 0: byte offset of the weight's fp16 repack (conv_weights_f16)
+                         // in the arena's fp16 section
     };
     struct Res {
         uint32_t cin, cout, emb_off;  // emb_off: row of this block's emb_layers weight in the emb group
@@ -248,7 +276,7 @@ struct sdvk_unet {
     sdvk_unet_desc d{};
     int device = 0;
     std::vector<Tensor> t;
-    uint64_t q_bytes = 0, s_bytes = 0, f_bytes = 0;
+    uint64_t q_bytes = 0, s_bytes = 0, f_bytes = 0, h_bytes = 0, h_base = 0;
     uint8_t* arena = nullptr;
     uint8_t* ws = nullptr;
     uint64_t ws_bytes = 0;
@@ -268,6 +296,16 @@ struct sdvk_unet {
     int8_t* q(int i) const { return reinterpret_cast<int8_t*>(arena + t[i].q_off); }
     float* s(int i) const { return reinterpret_cast<float*>(arena + t[i].s_off); }
     float* f(int i) const { return i < 0 ? nullptr : reinterpret_cast<float*>(arena + t[i].f_off); }
+    __half* h16(const Lin& l) const { return reinterpret_cast<__half*>(arena + h_base + l.h); }
+    // every conv with an fp16 repack, for sdvk_unet_prepare
+    template <class F>
+    void for_each_repacked(F&& f) const {
+        auto one = [&](const Lin& l) {
+            if (l.h >= 0) f(l);
+        };
+        for (const Res& r : res) one(r.conv1), one(r.conv2);
+        one(down[0]), one(down[1]), one(up[0]), one(up[1]), one(conv_out);
+    }
 };
 
 namespace sdvk {
@@ -305,6 +343,12 @@ struct Registry {
         x.init = -1;  // filled through its parent
         u.t.push_back(x);
         return (int)u.t.size() - 1;
+    }
+    // the fp16 repack of a [cout][cin * 9] conv weight, when the implicit convolution can use it
+    void repack(U::Lin& l, uint32_t cout, uint32_t cin) {
+        if (cin % 64) return;
+        l.h = (int64_t)u.h_bytes;
+        u.h_bytes = a256(u.h_bytes + (uint64_t)cout * cin * 9 * 2);
     }
     U::Lin lin(const std::string& p, uint32_t rows, uint32_t cols, bool bias = true) {
         U::Lin l;
@@ -380,6 +424,8 @@ void build(U& u) {
         R.norm(p + ".out_layers.0", s.cout, r.gn2w, r.gn2b);
         r.conv2 = R.lin(p + ".out_layers.3", s.cout, s.cout * 9);
         if (s.cin != s.cout) r.skip = R.lin(p + ".skip_connection", s.cout, s.cin);
+        R.repack(r.conv1, s.cout, s.cin);
+        R.repack(r.conv2, s.cout, s.cout);
         off += s.cout;
         u.res.push_back(r);
     }
@@ -434,6 +480,11 @@ void build(U& u) {
     u.up[1] = R.lin(d.depth[1] ? "output_blocks.5.2.conv" : "output_blocks.5.1.conv", ch[1], ch[1] * 9);
     R.norm("out.0", ch[0], u.out_gnw, u.out_gnb);
     u.conv_out = R.lin("out.2", kOutCh, ch[0] * 9);
+    R.repack(u.down[0], ch[0], ch[0]);
+    R.repack(u.down[1], ch[1], ch[1]);
+    R.repack(u.up[0], ch[2], ch[2]);
+    R.repack(u.up[1], ch[1], ch[1]);
+    R.repack(u.conv_out, kOutCh, ch[0]);
 }
 
 // the spatial transformer of a module, by its name's prefix (null if the module has none)
@@ -476,29 +527,44 @@ struct Pass {
     }
     static uint32_t grid_for(uint64_t n) { return (uint32_t)std::min<uint64_t>((n + 255) / 256, 148ull * 8); }
 
-    // GroupNorm (+SiLU) to fp16
-    __half* gn16(const float* x, int w, int b, uint32_t C, uint32_t P, float eps, bool silu) {
+    // GroupNorm (+SiLU) to fp16, channel-major [B][C][P] or channels-last [B][P][C]
+    __half* gn16(const float* x, int w, int b, uint32_t C, uint32_t P, float eps, bool silu, bool cl = false) {
         const uint32_t B = u.d.batch;
         __half* y = scratch<__half>(need_h16, o_h16, (uint64_t)B * C * P * 2);
         void* ws = scratch<void>(need_gn, o_gn, groupnorm_workspace(B, C, P, kGroups));
         launches += 2;
         if (!dry && ok())
             run(groupnorm_ex(x, u.f(w), u.f(b), y, SDVK_F16, B, C, P, kGroups, eps, silu ? 1u : 0u, ws,
-                             groupnorm_workspace(B, C, P, kGroups), env));
+                             groupnorm_workspace(B, C, P, kGroups), env, cl));
         return y;
     }
-    // 3x3 convolution of fp16 x [B][cin][H][W] (cin_real channels count toward the FLOPs)
+    // whether conv() runs this 3x3 convolution as the implicit GEMM, whose input is channels-last
+    bool implicit(const U::Lin& l, uint32_t cin, uint32_t H, uint32_t W, uint32_t stride) const {
+        return l.h >= 0 && conv_implicit_ok(u.d.batch, cin, H, W, stride);
+    }
+    // 3x3 convolution of fp16 x: channels-last [B][H][W][cin] when implicit(l, ...) holds (one launch),
+    // else channel-major [B][cin][H][W] through im2col and the Q8_0 NN GEMM (cin_real channels count
+    // toward the FLOPs)
     void conv(const __half* x, const U::Lin& l, uint32_t cin, uint32_t cout, uint32_t H, uint32_t W, uint32_t stride,
               float* y, const float* bias, uint64_t bias_stride, bool acc, uint32_t cin_real = 0) {
         const uint32_t B = u.d.batch;
-        const uint64_t wsb = conv3x3_workspace(cin, H, W, stride, SDVK_F16) * B;  // every image's columns: one GEMM
-        void* col = scratch<void>(need_col, o_col, wsb);
         const uint32_t OH = stride == 1 ? H : H / 2, OW = stride == 1 ? W : W / 2;
         flops += 2ull * B * OH * OW * cout * (cin_real ? cin_real : cin) * 9;
+        const float* b = bias ? bias : u.f(l.b);
+        if (implicit(l, cin, H, W, stride)) {
+            ++launches;
+            if (!dry && ok())
+                run(conv3x3_implicit(ConvImplicitDesc{x, u.h16(l), b, bias ? bias_stride : 0, acc, y, SDVK_F32, B, cin,
+                                                      cout, H, W, stride, -1},
+                                     env));
+            return;
+        }
+        const uint64_t wsb = conv3x3_workspace(cin, H, W, stride, SDVK_F16) * B;  // every image's columns: one GEMM
+        void* col = scratch<void>(need_col, o_col, wsb);
         launches += 2;  // im2col and GEMM, each over all images (the workspace holds every column matrix)
         if (!dry && ok())
-            run(conv3x3_q8_ex(x, SDVK_F16, u.q(l.w), u.s(l.w), bias ? bias : u.f(l.b), bias ? bias_stride : 0, acc, y,
-                              SDVK_F32, B, cin, cout, H, W, stride, -1, col, wsb, env));
+            run(conv3x3_q8_ex(x, SDVK_F16, u.q(l.w), u.s(l.w), b, bias ? bias_stride : 0, acc, y, SDVK_F32, B, cin, cout,
+                              H, W, stride, -1, col, wsb, env));
     }
     void copy(float* dst, const float* src, uint64_t floats, const LaunchEnv* on = nullptr) {
         const LaunchEnv& e = on ? *on : env;
@@ -510,6 +576,14 @@ struct Pass {
         if (!dry && ok())
             run(launch_pdl(to_f16_kernel, dim3(grid_for(n)), dim3(256), 0, env, "to_f16_kernel launch", x, y, u.d.batch,
                            Cin, Cout, H, W, up));
+    }
+    // the same conversion (C channels) written channels-last, for an implicit convolution
+    void to_f16_cl(const float* x, __half* y, uint32_t C, uint32_t H, uint32_t W, uint32_t up) {
+        const uint64_t OP = (uint64_t)(H << up) * (W << up);
+        ++launches;
+        if (!dry && ok())
+            run(launch_pdl(to_f16_cl_kernel, dim3((uint32_t)((OP + 31) / 32), (C + 31) / 32, u.d.batch), dim3(32, 8), 0,
+                           env, "to_f16_cl_kernel launch", x, y, C, H, W, up));
     }
     template <class TI>
     void transpose(const TI* in, __half* out, uint32_t R, uint32_t Cc) {
@@ -604,11 +678,11 @@ struct Pass {
         if (r.cin == r.cout) copy(out, x, (uint64_t)B * r.cout * P, fork ? &side : nullptr);
         else conv1x1(x, SDVK_F32, r.skip, r.cin, r.cout, P, out, false, fork ? &side : nullptr);
         if (fork) run(cuda_check(env, cudaEventRecord(env.join, env.side), "join"));
-        __half* h16 = gn16(x, r.gn1w, r.gn1b, r.cin, P, 1e-5f, true);
+        __half* h16 = gn16(x, r.gn1w, r.gn1b, r.cin, P, 1e-5f, true, implicit(r.conv1, r.cin, H, W, 1));
         float* h = scratch<float>(need_h32, o_h32, (uint64_t)B * r.cout * P * 4);
         conv(h16, r.conv1, r.cin, r.cout, H, W, 1, h, dry ? nullptr : ebias + r.emb_off, u.emb_rows, false);
         flops += 2ull * B * r.cout * u.d.temb_dim;  // its share of the emb GEMM
-        __half* g16 = gn16(h, r.gn2w, r.gn2b, r.cout, P, 1e-5f, true);
+        __half* g16 = gn16(h, r.gn2w, r.gn2b, r.cout, P, 1e-5f, true, implicit(r.conv2, r.cout, H, W, 1));
         if (fork) run(cuda_check(env, cudaStreamWaitEvent(env.stream, env.join, 0), "join"));
         conv(g16, r.conv2, r.cout, r.cout, H, W, 1, out, nullptr, 0, true);
         return out;
@@ -617,9 +691,7 @@ struct Pass {
     // spatialTransformer (sdvkgen.cpp:1722-1777), x updated in place
     void transformer(float* x, const U::St& s, uint32_t H, uint32_t W, const void* ctx, int ctx_dtype) {
         const uint32_t B = u.d.batch, P = H * W, C = s.C;
-        __half* g16 = gn16(x, s.gnw, s.gnb, C, P, 1e-6f, false);
-        __half* a16 = scratch<__half>(need_tok, o_tok, (uint64_t)B * P * C * 2);
-        transpose(g16, a16, C, P);  // [B][C][P] -> [B][P][C]
+        __half* a16 = gn16(x, s.gnw, s.gnb, C, P, 1e-6f, false, true);  // tokens [B][P][C]
         float* t = scratch<float>(need_h32, o_h32, (uint64_t)B * P * C * 4);
         linear(a16, SDVK_F16, B * P, C, s.proj_in, t, C, false);
         // every block's cross-attention K|V from the context at once (the context is the same for all):
@@ -747,7 +819,8 @@ struct Pass {
             }
             if (lv < 2) {  // conv3s2 (sdvkgen.cpp:1162-1178)
                 __half* x16 = scratch<__half>(need_h16, o_h16, (uint64_t)B * ch * H * W * 2);
-                to_f16(x, x16, ch, ch, H, W, 0);
+                if (implicit(u.down[lv], ch, H, W, 2)) to_f16_cl(x, x16, ch, H, W, 0);
+                else to_f16(x, x16, ch, ch, H, W, 0);
                 float* y = out_buf((uint64_t)B * ch * (H / 2) * (W / 2));
                 conv(x16, u.down[lv], ch, ch, H, W, 2, y, nullptr, 0, false);
                 x = y;
@@ -783,7 +856,8 @@ struct Pass {
             module("output_blocks." + std::to_string(j));
             if (j == 2 || j == 5) {  // up2 + conv3Raw
                 __half* x16 = scratch<__half>(need_h16, o_h16, (uint64_t)B * ch * H * W * 4 * 2);
-                to_f16(x, x16, ch, ch, H, W, 1);
+                if (implicit(u.up[j == 2 ? 0 : 1], ch, 2 * H, 2 * W, 1)) to_f16_cl(x, x16, ch, H, W, 1);
+                else to_f16(x, x16, ch, ch, H, W, 1);
                 H *= 2, W *= 2;
                 float* y = out_buf((uint64_t)B * ch * H * W);
                 conv(x16, u.up[j == 2 ? 0 : 1], ch, ch, H, W, 1, y, nullptr, 0, false);
@@ -791,7 +865,7 @@ struct Pass {
             }
         }
         // ---- out: GN + SiLU, conv 3x3 to the 4 latent channels
-        __half* h16 = gn16(x, u.out_gnw, u.out_gnb, ch, H * W, 1e-5f, true);
+        __half* h16 = gn16(x, u.out_gnw, u.out_gnb, ch, H * W, 1e-5f, true, implicit(u.conv_out, ch, H, W, 1));
         conv(h16, u.conv_out, ch, kOutCh, H, W, 1, out, nullptr, 0, false);
     }
 
@@ -855,7 +929,8 @@ int unet_plan(const sdvk_unet_desc& d, sdvk_unet** out, const LaunchEnv& env) {
         t.s_off += s0;
         t.f_off += f0;
     }
-    u->arena_bytes = f0 + a256(u->f_bytes);
+    u->h_base = f0 + a256(u->f_bytes);
+    u->arena_bytes = u->h_base + a256(u->h_bytes);
     *out = u;
     return SDVK_OK;
 }
@@ -915,6 +990,12 @@ int unet_prepare(sdvk_unet* u, const LaunchEnv& env) {
                                           u->s(k.ff1_il_q), u->f(k.ff1_il_q + 1), env))
                 return rc;
         }
+    int rc = SDVK_OK;
+    u->for_each_repacked([&](const U::Lin& l) {
+        const U::Tensor& t = u->t[l.w];
+        if (rc == SDVK_OK) rc = conv_weights_f16(u->q(l.w), u->s(l.w), t.rows, t.cols / 9, u->h16(l), env);
+    });
+    if (rc) return rc;
     u->prepared = true;
     return SDVK_OK;
 }

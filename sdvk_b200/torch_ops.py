@@ -196,6 +196,48 @@ def conv3x3_q8(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, bias: Optional
     return y
 
 
+def conv3x3_weights_f16(q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """The fp16 tap-major repack of a Q8_0 conv weight q [cout, cin*9] for conv3x3_nhwc
+    (sdvk_conv3x3_weights_f16; cin % 64 == 0)."""
+    assert q.dtype == torch.int8 and q.is_contiguous() and q.dim() == 2 and q.shape[1] % 9 == 0
+    cout, K = q.shape
+    w16 = torch.empty((cout, K), dtype=torch.float16, device=q.device)
+    context(q.device).conv3x3_weights_f16(q.data_ptr(), s.data_ptr(), cout, K // 9, w16.data_ptr())
+    return w16
+
+
+def conv3x3_nhwc(x: torch.Tensor, w16: torch.Tensor, bias: Optional[torch.Tensor] = None, stride: int = 1,
+                 pad_off: int = -1, out_dtype: torch.dtype = torch.float32, bias_stride: int = 0,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The implicit-GEMM 3x3 convolution (sdvk_conv3x3_nhwc) of channels-last fp16 x [B, H, W, cin] with
+    w16 from conv3x3_weights_f16: y [B, cout, OH, OW], or y += conv when `out` is given (fp32)."""
+    assert x.dtype == torch.float16 and x.is_contiguous() and x.dim() == 4
+    B, H, W, cin = x.shape
+    cout = w16.shape[0]
+    OH, OW = (H, W) if stride == 1 else (H // 2, W // 2)
+    y = out if out is not None else torch.empty((B, cout, OH, OW), dtype=out_dtype, device=x.device)
+    context(x.device).conv3x3_nhwc(x.data_ptr(), w16.data_ptr(), bias.data_ptr() if bias is not None else None,
+                                   bias_stride, out is not None, y.data_ptr(), _dt(y), B, cin, cout, H, W, stride,
+                                   pad_off)
+    return y
+
+
+def groupnorm_cl(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, groups: int = 32, eps: float = 1e-5,
+                 silu: bool = False) -> torch.Tensor:
+    """GroupNorm (+SiLU) of fp32 x [B, C, *spatial] written channels-last as fp16 [B, P, C]
+    (sdvk_groupnorm_cl)."""
+    assert x.dtype == torch.float32 and x.is_contiguous() and x.dim() >= 2
+    B, C = x.shape[0], x.shape[1]
+    P = x.numel() // (B * C)
+    out = torch.empty((B, P, C), dtype=torch.float16, device=x.device)
+    ctx = context(x.device)
+    nbytes = ctx.groupnorm_workspace(B, C, P, groups)
+    ws = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=x.device)
+    ctx.groupnorm_cl(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), out.data_ptr(), B, C, P, groups, eps, silu,
+                     ws.data_ptr(), ws.numel())
+    return out
+
+
 def groupnorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, groups: int = 32, eps: float = 1e-5,
               silu: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """GroupNorm (+SiLU) of fp32 x [B, C, *spatial] (groupnorm.comp), via sdvk_groupnorm."""
