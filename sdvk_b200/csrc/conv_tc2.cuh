@@ -38,15 +38,23 @@ struct ConvParams {
     uint64_t timeout_ns;
 };
 
+#ifndef SDVK_CONV_EPI_BUFS
+#define SDVK_CONV_EPI_BUFS 2
+#endif
+#ifndef SDVK_CONV_MAX_STAGES
+#define SDVK_CONV_MAX_STAGES 8
+#endif
+
 template <int BN>
 struct ConvCfg {
     static constexpr int kABytes = 128 * 128;        // 128 positions x 64 fp16 channels
     static constexpr int kBBytes = (BN / 2) * 128;   // BN/2 output channels x 64 fp16
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kEpiBytes = 4 * 2 * 4096;   // 4 epilogue warps x 2 buffers x 32x32 fp32
+    static constexpr int kEpiBufs = SDVK_CONV_EPI_BUFS;  // 32x32 fp32 staging buffers per epilogue warp
+    static constexpr int kEpiBytes = 4 * kEpiBufs * 4096;
     static constexpr int kMaxSmem = 232448;
     static constexpr int kSFit = (kMaxSmem - 1024 - 256 - kEpiBytes) / kStageBytes;
-    static constexpr int kS = kSFit > 8 ? 8 : kSFit;
+    static constexpr int kS = kSFit > SDVK_CONV_MAX_STAGES ? SDVK_CONV_MAX_STAGES : kSFit;
     static constexpr int kAcc = 2;
     static constexpr uint32_t kTmemCols = (kAcc * BN <= 64) ? 64 : (kAcc * BN <= 128) ? 128 : (kAcc * BN <= 256) ? 256 : 512;
     static constexpr int kOffEpi = kS * kStageBytes;
@@ -193,7 +201,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         // Warp q reads TMEM lanes 32q..32q+31: output positions g0 + 32q + lane of this CTA's 128
         // (one image: P is a multiple of 128); each 32-column chunk is 32 output channels.
         const int q = warp & 3;
-        uint8_t* ebuf = sEpi + q * (2 * 4096);
+        uint8_t* ebuf = sEpi + q * (Cfg::kEpiBufs * 4096);
         uint32_t nstore = 0;
         for (uint32_t i = 0; ok && i < my_tiles; ++i) {
             const uint32_t tile = cid + i * ncl, nt = tile % p.tiles_n, mt = tile / p.tiles_n;
@@ -223,8 +231,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + __shfl_sync(0xffffffffu, bl, j);
-                uint8_t* buf = ebuf + (nstore & 1) * 4096;
-                if (lane == 0) bulk_wait_read<1>();  // the store that last used `buf` has read it
+                uint8_t* buf = ebuf + (nstore % Cfg::kEpiBufs) * 4096;
+                if (lane == 0) bulk_wait_read<Cfg::kEpiBufs - 1>();  // the store that last used `buf` has read it
                 __syncwarp();
                 store_epi_col<TC>(buf, lane, v);  // [32 channels][32 positions]
                 fence_proxy_async_smem();

@@ -220,48 +220,72 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(const float* __res
 }
 
 // The same values written channels-last, y[b][p][c] fp16 (the implicit convolution's input and the
-// spatial transformer's token layout).  grid (ceil(P / 128), C / 32, B), block (32, 8): 32 channels x
-// 128 positions per CTA, through 32 x 32 shared-memory tiles; the warps first merge the statistics of
-// the tile's groups (gn_group_norm, so the values equal gn_apply_kernel's bit for bit).  C % 32 == 0.
+// spatial transformer's token layout).  grid (ceil(P / 256), C / CT, B), 256 threads: CT channels x 256
+// positions per CTA in sub-tiles of 64 positions through shared memory.  The warps first merge the
+// statistics of the tile's groups (gn_group_norm, so the values equal gn_apply_kernel's bit for bit);
+// x is read as float4 rows along P (vec: P % 4 == 0 and x 16-byte aligned), y written as 16-byte rows
+// of 8 channels (CT * 2 contiguous bytes per position).  C % CT == 0, y 16-byte aligned.
+template <int CT>
 __global__ void __launch_bounds__(kGnThreads) gn_apply_cl_kernel(const float* __restrict__ x,
                                                                  const float* __restrict__ gamma,
                                                                  const float* __restrict__ beta, __half* __restrict__ y,
                                                                  uint32_t C, uint32_t P, uint32_t G, float eps,
                                                                  uint32_t act, const GnStat* __restrict__ stats,
-                                                                 uint32_t chunks) {
+                                                                 uint32_t chunks, bool vec) {
     grid_dependency_wait();
     grid_launch_dependents();
-    __shared__ float2 gnorm[32];
-    __shared__ float cm[32], csc[32], csh[32];
-    __shared__ float tile[32][33];
-    const uint32_t b = blockIdx.z, c0 = blockIdx.y * 32, p0 = blockIdx.x * 128;
-    const uint32_t tx = threadIdx.x, ty = threadIdx.y, cpg = C / G;
-    const uint32_t g_lo = c0 / cpg, g_hi = (c0 + 31) / cpg;
-    for (uint32_t g = g_lo + ty; g <= g_hi; g += 8) {
+    __shared__ float2 gnorm[CT];
+    __shared__ float cm[CT], csc[CT], csh[CT];
+    __shared__ float tile[CT][65];
+    const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const uint32_t b = blockIdx.z, c0 = blockIdx.y * CT, p0 = blockIdx.x * 256, cpg = C / G;
+    const uint32_t g_lo = c0 / cpg, g_hi = (c0 + CT - 1) / cpg;
+    for (uint32_t g = g_lo + warp; g <= g_hi; g += kGnThreads / 32) {
         const float2 r = gn_group_norm(stats + ((uint64_t)b * G + g) * chunks, chunks, eps);
-        if (tx == 0) gnorm[g - g_lo] = r;
+        if (lane == 0) gnorm[g - g_lo] = r;
     }
     __syncthreads();
-    if (ty == 0) {
-        const uint32_t c = c0 + tx;
+    if (t < CT) {
+        const uint32_t c = c0 + t;
         const float2 r = gnorm[c / cpg - g_lo];
-        cm[tx] = r.x, csc[tx] = r.y * gamma[c], csh[tx] = beta[c];
+        cm[t] = r.x, csc[t] = r.y * gamma[c], csh[t] = beta[c];
     }
     __syncthreads();
     const float* xb = x + ((uint64_t)b * C + c0) * P;
     __half* yb = y + (uint64_t)b * P * C + c0;
+    constexpr uint32_t kChunks = CT / 8;  // 16-byte rows of 8 channels per position
 #pragma unroll 1
-    for (uint32_t sub = 0; sub < 128; sub += 32) {
-        const uint32_t ps = p0 + sub;
-        if (ps >= P) break;
-        for (uint32_t r = ty; r < 32; r += 8) {
-            const uint32_t pp = ps + tx;
-            if (pp < P) tile[r][tx] = gn_out(__ldcs(xb + (uint64_t)r * P + pp), cm[r], csc[r], csh[r], act);
+    for (uint32_t ps = p0; ps < min(P, p0 + 256); ps += 64) {
+        // x[c][ps .. ps+63] -> tile[c][0..63], normalised
+#pragma unroll
+        for (uint32_t i = 0; i < CT / 16; ++i) {
+            const uint32_t r = t / 16 + 16 * i, q = (t % 16) * 4, pp = ps + q;
+            const float* src = xb + (uint64_t)r * P + pp;
+            float v[4];
+            if (vec && pp + 3 < P) {
+                const float4 f = __ldcs(reinterpret_cast<const float4*>(src));
+                v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[j] = pp + j < P ? __ldcs(src + j) : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tile[r][q + j] = gn_out(v[j], cm[r], csc[r], csh[r], act);
         }
         __syncthreads();
-        for (uint32_t r = ty; r < 32; r += 8) {
-            const uint32_t pp = ps + r;
-            if (pp < P) yb[(uint64_t)pp * C + tx] = __float2half_rn(tile[tx][r]);
+        // tile[c][p] -> y[ps + p][c0 + 8k .. 8k+7] as 16-byte stores
+#pragma unroll
+        for (uint32_t i = 0; i < CT / 32; ++i) {
+            const uint32_t k = t % kChunks, p = t / kChunks + (kGnThreads / kChunks) * i, pp = ps + p;
+            if (pp < P) {
+                uint32_t w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const __half2 h = __floats2half2_rn(tile[8 * k + 2 * j][p], tile[8 * k + 2 * j + 1][p]);
+                    w[j] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                *reinterpret_cast<uint4*>(yb + (uint64_t)pp * C + 8 * k) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
         }
         __syncthreads();
     }
@@ -303,8 +327,10 @@ int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y,
                  const LaunchEnv& env, bool channels_last) {
     if (!x || !gamma || !beta || !y) return fail(env, SDVK_E_ARG, "null pointer");
     if (y_dtype != SDVK_F32 && y_dtype != SDVK_F16) return fail(env, SDVK_E_ARG, "GroupNorm output must be F32 or F16");
-    if (channels_last && (y_dtype != SDVK_F16 || C % 32 || (C / 32) > 65535 || batch > 65535))
-        return fail(env, SDVK_E_SHAPE, "the channels-last GroupNorm writes F16 and needs C % 32 == 0");
+    if (channels_last && (y_dtype != SDVK_F16 || C % 32 || (C / 32) > 65535 || batch > 65535 ||
+                          (reinterpret_cast<uintptr_t>(y) & 15u)))
+        return fail(env, SDVK_E_SHAPE,
+                    "the channels-last GroupNorm writes F16 to a 16-byte aligned y and needs C % 32 == 0");
     if (batch == 0 || C == 0 || P == 0) return SDVK_OK;
     if (G == 0 || C % G || G > 65535 || batch > 65535)
         return fail(env, SDVK_E_SHAPE, "GroupNorm needs C % G == 0 and at most 65535 groups and images");
@@ -319,10 +345,16 @@ int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y,
     if (int rc = launch_pdl(gn_stats_kernel, dim3(chunks, G, batch), dim3(kGnThreads), 0, env, "gn_stats_kernel launch",
                             x, C, P, G, vec, st))
         return rc;
-    if (channels_last)
-        return launch_pdl(gn_apply_cl_kernel, dim3((P + 127) / 128, C / 32, batch), dim3(32, 8), 0, env,
+    if (channels_last) {
+        const bool xvec = P % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+        if (C % 64 == 0)
+            return launch_pdl(gn_apply_cl_kernel<64>, dim3((P + 255) / 256, C / 64, batch), dim3(kGnThreads), 0, env,
+                              "gn_apply_cl_kernel launch", x, gamma, beta, static_cast<__half*>(y), C, P, G, eps, act,
+                              (const GnStat*)st, chunks, xvec);
+        return launch_pdl(gn_apply_cl_kernel<32>, dim3((P + 255) / 256, C / 32, batch), dim3(kGnThreads), 0, env,
                           "gn_apply_cl_kernel launch", x, gamma, beta, static_cast<__half*>(y), C, P, G, eps, act,
-                          (const GnStat*)st, chunks);
+                          (const GnStat*)st, chunks, xvec);
+    }
     if (y_dtype == SDVK_F16)
         return launch_pdl(gn_apply_kernel<__half>, dim3(C, batch), dim3(kGnThreads), 0, env, "gn_apply_kernel launch",
                           x, gamma, beta, static_cast<__half*>(y), C, P, G, eps, act, (const GnStat*)st, chunks,
