@@ -14,11 +14,14 @@
 // The accumulator D[w][x] (TMEM lane = weight row, column = activation row) is stored transposed
 // for NT (C[x][w]) and directly for NN (C[w][x]).
 //
-// The tensor pipe idles whenever the issuing thread polls a barrier that is not yet complete, so
-// its per-stage control path is one CTA-scope poll of one barrier and one commit:
-//   full[s]   (even CTA)  activation TMA bytes of both CTAs (cta_group::2 TMA) + one dequantiser
-//                         group's warps of both CTAs; the even CTA's producer sets the tx count
-//   empty[s]  (each CTA)  one MMA commit multicast to both CTAs frees activation and operand slot s
+// Three rings, sized independently: the dequantised-weight ring (one slot per dequantiser group), the
+// raw int8 weight ring, and the activation ring, which takes the shared memory that is left (6 slots at
+// tile widths 224-256, 8 below).  The tensor pipe idles whenever the issuing thread polls a barrier that
+// is not yet complete, so its per-stage control path is two CTA-scope polls and two commits:
+//   x_full[sx]  (even CTA)  activation TMA bytes of both CTAs (cta_group::2 TMA); the even CTA's
+//                           producer sets the tx count
+//   a_full[sa]  (even CTA)  one dequantiser group's warps of both CTAs
+//   x_empty[sx], a_empty[sa] (each CTA)  an MMA commit multicast to both CTAs frees the slot
 //   acc_full  (each CTA)  MMA commit multicast;  acc_empty (even CTA): the 8 epilogue warps
 //   w_full, w_empty (each CTA)  the local raw int8 weight ring (TMA -> dequantisers)
 // Warp roles per CTA: 0 activation TMA, 1 TMEM + MMA (even CTA issues), 2 weight TMA,
@@ -44,26 +47,37 @@ struct Gemm2Config {
     static constexpr int kES = sizeof(TA);
     static constexpr int kBK = 128 / kES;
     static constexpr int kUmmaK = 32 / kES;
-#ifndef SDVK_GEMM2_STAGES
-#define SDVK_GEMM2_STAGES 5
+#ifndef SDVK_GEMM2_A_STAGES
+#define SDVK_GEMM2_A_STAGES 4
 #endif
 #ifndef SDVK_GEMM2_RAW_STAGES
 #define SDVK_GEMM2_RAW_STAGES 4
 #endif
-    static constexpr int kS = SDVK_GEMM2_STAGES;       // stages of (dequantised weight tile, activation tile)
-    static constexpr int kSW = SDVK_GEMM2_RAW_STAGES;  // raw int8 weight stages
+#ifndef SDVK_GEMM2_X_STAGES
+#define SDVK_GEMM2_X_STAGES 8
+#endif
+#ifndef SDVK_GEMM2_EPI_BUFS
+#define SDVK_GEMM2_EPI_BUFS 2
+#endif
+    static constexpr int kSA = SDVK_GEMM2_A_STAGES;    // dequantised weight tiles
+    static constexpr int kSW = SDVK_GEMM2_RAW_STAGES;  // raw int8 weight tiles
     static constexpr int kAcc = 2;
     static constexpr int kABytes = kBW * 128;
-    static constexpr int kXBytes = kBXC * 128;
-    static constexpr int kStageBytes = kABytes + ((kXBytes + 1023) / 1024) * 1024;
+    static constexpr int kXBytes = ((kBXC * 128 + 1023) / 1024) * 1024;
     static constexpr int kWBytes = kBW * kBK;
-    static constexpr int kEpiBytes = 4 * 2 * 4096;  // 4 epilogue warps x 2 buffers x 32x32 fp32
+    static constexpr int kEpiBufs = SDVK_GEMM2_EPI_BUFS;  // 32x32 fp32 staging buffers per epilogue warp
+    static constexpr int kEpiBytes = 4 * kEpiBufs * 4096;
+    static constexpr int kMaxSmem = 232448;
+    static constexpr int kFixed = kSA * kABytes + ((kSW * kWBytes + 1023) / 1024) * 1024 + kEpiBytes + 1024 + 512;
+    static constexpr int kSXFit = (kMaxSmem - kFixed) / kXBytes;
+    static constexpr int kSX = kSXFit > SDVK_GEMM2_X_STAGES ? SDVK_GEMM2_X_STAGES : kSXFit;  // activation tiles
     static constexpr uint32_t kTmemCols = (kAcc * BNX <= 256) ? 256 : 512;
-    static constexpr int kOffStage = 0;
-    static constexpr int kOffW = kOffStage + kS * kStageBytes;
+    static constexpr int kOffA = 0;
+    static constexpr int kOffX = kOffA + kSA * kABytes;
+    static constexpr int kOffW = kOffX + kSX * kXBytes;
     static constexpr int kOffEpi = kOffW + ((kSW * kWBytes + 1023) / 1024) * 1024;
     static constexpr int kOffBar = kOffEpi + kEpiBytes;
-    static constexpr int kNumBars = 2 * kS + 2 * kSW + 2 * kAcc + 1;
+    static constexpr int kNumBars = 2 * kSA + 2 * kSX + 2 * kSW + 2 * kAcc + 1;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
     static constexpr int kThreads = 512;
     // dequantiser groups (stages round-robin); bf16's dequantisation goes through fp32 and needs
@@ -77,9 +91,13 @@ struct Gemm2Config {
     static constexpr int kChunksPerRow = kBK / 16;
     static constexpr int kTasksPerThread = kBW * kChunksPerRow / kConvThreads;
     static constexpr int kRowStep = kConvThreads / kChunksPerRow;
-    static_assert(kSmemBytes <= 232448, "shared memory");
+    static_assert(kSX >= 3 && kSmemBytes <= kMaxSmem, "shared memory");
     static_assert(BNX % 32 == 0 && BNX >= 64 && BNX <= 256, "pair tile N");
     static_assert((kBW * kChunksPerRow) % kConvThreads == 0, "dequant task split");
+    // Groups take stages round-robin and stage it uses dequantised slot it % kSA.  With fewer slots than
+    // groups a group can reach a slot two phases ahead of the MMA, which a parity wait cannot tell
+    // from one phase ahead.
+    static_assert(kSA >= kDqGroups, "at least one dequantised-weight slot per dequantiser group");
 };
 
 template <class TA, int BNX, bool NN, class TC>
@@ -89,13 +107,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     using Cfg = Gemm2Config<TA, BNX>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sStage = smem + Cfg::kOffStage;  // stage s: dequantised weights, then activations
-    uint8_t* sW = smem + Cfg::kOffW;
+    uint8_t* sA = smem + Cfg::kOffA;  // dequantised weight tiles
+    uint8_t* sX = smem + Cfg::kOffX;  // activation tiles
+    uint8_t* sW = smem + Cfg::kOffW;  // raw int8 weight tiles
     uint8_t* sEpi = smem + Cfg::kOffEpi;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
-    uint64_t* full = bars;
-    uint64_t* empty = full + Cfg::kS;
-    uint64_t* w_full = empty + Cfg::kS;
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = a_full + Cfg::kSA;
+    uint64_t* x_full = a_empty + Cfg::kSA;
+    uint64_t* x_empty = x_full + Cfg::kSX;
+    uint64_t* w_full = x_empty + Cfg::kSX;
     uint64_t* w_empty = w_full + Cfg::kSW;
     uint64_t* acc_full = w_empty + Cfg::kSW;
     uint64_t* acc_empty = acc_full + Cfg::kAcc;
@@ -109,9 +130,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     const uint32_t cid = cluster_id_x(), ncl = nclusters_x();
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < Cfg::kS; ++i) {
-            mbar_init(&full[i], 1 + 2 * Cfg::kDqWarps);  // producer's expect_tx + one group's warps of both CTAs
-            mbar_init(&empty[i], 1);
+        for (int i = 0; i < Cfg::kSA; ++i) {
+            mbar_init(&a_full[i], 2 * Cfg::kDqWarps);  // one dequantiser group's warps of both CTAs
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < Cfg::kSX; ++i) {
+            mbar_init(&x_full[i], 1);  // the even CTA producer's expect_tx (both CTAs' bytes)
+            mbar_init(&x_empty[i], 1);
         }
         for (int i = 0; i < Cfg::kSW; ++i) {
             mbar_init(&w_full[i], 1);
@@ -161,21 +186,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ activation TMA producer (both CTAs)
         if (lane == 0) {
-            uint32_t it = 0;
+            uint32_t sx = 0, px = 0;
             for (uint32_t i = 0; ok && i < my_tiles; ++i) {
                 uint32_t z, xt, wt;
                 decode(cid + i * ncl, z, xt, wt);
                 const int x0 = (int)(xt * Cfg::kBNX + rank * Cfg::kBXC);
-                for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
-                    const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
+                for (uint32_t ks = 0; ks < p.k_stages; ++ks) {
                     const int k0 = (int)(ks * Cfg::kBK);
-                    if (!mbar_wait(&empty[s], ph ^ 1, p.timeout_ns)) {
+                    if (!mbar_wait(&x_empty[sx], px ^ 1, p.timeout_ns)) {
                         fail();
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kXBytes);  // both CTAs' bytes
-                    const uint32_t full_l = mapa_shared(&full[s], 0);
-                    uint8_t* x_dst = sStage + s * Cfg::kStageBytes + Cfg::kABytes;
+                    if (leader) mbar_arrive_expect_tx(&x_full[sx], 2 * Cfg::kBXC * 128);  // both CTAs' bytes
+                    const uint32_t full_l = mapa_shared(&x_full[sx], 0);
+                    uint8_t* x_dst = sX + sx * Cfg::kXBytes;
+                    if (++sx == Cfg::kSX) sx = 0, px ^= 1;
                     if constexpr (!NN) {
                         tma_load_3d_pair(x_dst, &tmX, full_l, k0, x0, (int)z);
                     } else {  // [K][x] activations: kBXC / kBK column blocks of kBK x kBK
@@ -217,18 +242,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         if (leader) {
             constexpr uint32_t idesc =
                 make_idesc(OperandTraits<TA>::kFmt, OperandTraits<TA>::kFmt, 0, NN ? 1 : 0, 2 * Cfg::kBW, Cfg::kBNX);
-            // Operand descriptors of stage 0; a stage adds kStageBytes, a K step of kUmmaK elements
+            // Operand descriptors of slot 0; a slot adds its ring's tile size, a K step of kUmmaK elements
             // adds 32 bytes (K-major) or kUmmaK rows of 128 bytes (MN-major activations).
-            const uint32_t a0 = smem_u32(sStage);
+            const uint32_t a0 = smem_u32(sA);
             const uint64_t adesc0 = smem_desc_sw128(a0, 16, 1024);
-            const uint32_t b0 = a0 + Cfg::kABytes;
+            const uint32_t b0 = smem_u32(sX);
             uint64_t bdesc0;
             if constexpr (!NN) bdesc0 = smem_desc_sw128(b0, 16, 1024);
             else if constexpr (!OperandTraits<TA>::kTf32) bdesc0 = smem_desc_sw128(b0, Cfg::kBK * 128, 1024);
             else bdesc0 = smem_desc(b0, Cfg::kBK * 128, 512, kLayoutSw128Base32);
-            constexpr uint64_t kStageDesc = Cfg::kStageBytes >> 4;
+            constexpr uint64_t kAStageDesc = Cfg::kABytes >> 4, kXStageDesc = Cfg::kXBytes >> 4;
             constexpr uint64_t kBStep = NN ? (Cfg::kUmmaK * 128) >> 4 : 2;
-            uint32_t s = 0, ph = 0;
+            uint32_t sa = 0, pa = 0, sx = 0, px = 0;
             for (uint32_t i = 0; ok && i < my_tiles; ++i) {
                 const uint32_t acc = i & (Cfg::kAcc - 1), aph = (i / Cfg::kAcc) & 1;
                 if (!__all_sync(0xffffffffu, mbar_wait(&acc_empty[acc], aph ^ 1, p.timeout_ns))) {
@@ -238,12 +263,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * Cfg::kBNX;
                 for (uint32_t ks = 0; ks < p.k_stages; ++ks) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.timeout_ns))) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&x_full[sx], px, p.timeout_ns) &&
+                                                     mbar_wait(&a_full[sa], pa, p.timeout_ns))) {
                         fail();
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = adesc0 + s * kStageDesc, bd = bdesc0 + s * kStageDesc;
+                    const uint64_t ad = adesc0 + sa * kAStageDesc, bd = bdesc0 + sx * kXStageDesc;
                     if (elect_one()) {
 #pragma unroll
                         for (int kk = 0; kk < Cfg::kBK / Cfg::kUmmaK; ++kk) {
@@ -252,10 +278,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                                 mma_tf32_pair(d_tmem, ad + 2 * kk, bd + kk * kBStep, idesc, accum);
                             else mma_f16_pair(d_tmem, ad + 2 * kk, bd + kk * kBStep, idesc, accum);
                         }
-                        mma_commit_pair_mc(&empty[s], 0x3);
+                        mma_commit_pair_mc(&x_empty[sx], 0x3);
+                        mma_commit_pair_mc(&a_empty[sa], 0x3);
                     }
                     __syncwarp();
-                    if (++s == Cfg::kS) s = 0, ph ^= 1;
+                    if (++sx == Cfg::kSX) sx = 0, px ^= 1;
+                    if (++sa == Cfg::kSA) sa = 0, pa ^= 1;
                 }
                 if (!ok) break;
                 if (elect_one()) mma_commit_pair_mc(&acc_full[acc], 0x3);
@@ -293,16 +321,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             next_own();
         }
         auto stage = [&](uint32_t it, float(&scale)[T]) -> bool {
-            const uint32_t s = it % Cfg::kS, ph = (it / Cfg::kS) & 1;
+            const uint32_t sa = it % Cfg::kSA, pa = (it / Cfg::kSA) & 1;
             const uint32_t sw = it % Cfg::kSW, pw = (it / Cfg::kSW) & 1;
             if (!__all_sync(0xffffffffu, mbar_wait(&w_full[sw], pw, p.timeout_ns))) return false;  // leave together
             const uint8_t* wsrc = sW + sw * Cfg::kWBytes;
-            uint8_t* adst = sStage + s * Cfg::kStageBytes;
+            uint8_t* adst = sA + sa * Cfg::kABytes;
             uint4 raw[T];
 #pragma unroll
             for (int t = 0; t < T; ++t)
                 raw[t] = *reinterpret_cast<const uint4*>(wsrc + (row0 + t * Cfg::kRowStep) * Cfg::kBK + chunk * 16);
-            if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1, p.timeout_ns))) return false;
+            if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[sa], pa ^ 1, p.timeout_ns))) return false;
 #pragma unroll
             for (int t = 0; t < T; ++t) {
                 const int r = row0 + t * Cfg::kRowStep;
@@ -316,7 +344,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive_cluster(mapa_shared(&full[s], 0));
+                mbar_arrive_cluster(mapa_shared(&a_full[sa], 0));
                 mbar_arrive(&w_empty[sw]);
             }
             cur.load<false>(scale, unused);  // the scales of this group's stage it + G * kRing
@@ -338,7 +366,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         // Warp q reads TMEM lanes 32q..32q+31: weight rows w = wt*256 + rank*128 + 32q + lane; each
         // 32-column chunk is 32 activation rows.
         const int q = warp & 3;
-        uint8_t* ebuf = sEpi + q * (2 * 4096);
+        uint8_t* ebuf = sEpi + q * (Cfg::kEpiBufs * 4096);
         uint32_t nstore = 0;
         for (uint32_t i = 0; ok && i < my_tiles; ++i) {
             uint32_t z, xt, wt;
@@ -366,8 +394,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + b;
-                uint8_t* buf = ebuf + (nstore & 1) * 4096;
-                if (lane == 0) bulk_wait_read<1>();  // the store that last used `buf` has read it
+                uint8_t* buf = ebuf + (nstore % Cfg::kEpiBufs) * 4096;
+                if (lane == 0) bulk_wait_read<Cfg::kEpiBufs - 1>();  // the store that last used `buf` has read it
                 __syncwarp();
                 if constexpr (!NN && sizeof(TC) == 2) {
                     if (p.geglu) {
