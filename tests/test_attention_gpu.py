@@ -138,6 +138,10 @@ KERNEL_CASES = [
     (2, 257, 129, 3, False, "bf16", "f32"),
     (1, 640, 640, 2, True, "bf16", "f16"),
     (3, 1, 2, 1, False, "f16", "f32"),
+    # the persistent tensor-core kernel walks several items per CTA: causal items of 1 to 8 key tiles,
+    # and items of an odd key-tile count (the two softmax groups get unequal shares)
+    (2, 1024, 1024, 40, True, "f16", "f16"),
+    (2, 1024, 384, 100, False, "f16", "f32"),
 ]
 
 
