@@ -44,25 +44,42 @@ __device__ __forceinline__ void store4<__half>(__half* dst, float a, float b, fl
 }
 
 // One warp per row; the row is held in registers between the passes (kChunks float4 per lane,
-// d <= 128 * kChunks), so x is read from HBM once.
+// d <= 128 * kChunks), so x is read from HBM once.  gamma and beta are loaded once per CTA into shared
+// memory, issued before x so that their latency hides under the row's loads and reductions.
 template <class TO, int kChunks>
 __global__ void __launch_bounds__(kLnWarps * 32) layernorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                                   const float* __restrict__ beta, TO* __restrict__ y,
                                                                   uint32_t rows, uint32_t d, uint64_t ldx, uint64_t ldy,
                                                                   float eps) {
+    constexpr int kThreads = kLnWarps * 32, kGB = (kChunks * 32 + kThreads - 1) / kThreads;
+    __shared__ float4 sg[kChunks * 32], sb[kChunks * 32];
     grid_dependency_wait();  // x is the previous kernel's output
     grid_launch_dependents();
-    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t lane = threadIdx.x & 31, nq = d / 4;
     const uint32_t row = blockIdx.x * kLnWarps + (threadIdx.x >> 5);
-    if (row >= rows) return;
-    const float* xr = x + (uint64_t)row * ldx;
+    const bool live = row < rows;  // warp-uniform
+    float4 gq[kGB], bq[kGB];
+#pragma unroll
+    for (int k = 0; k < kGB; ++k) {
+        const uint32_t i = threadIdx.x + k * kThreads;
+        if (i < nq) {
+            gq[k] = gamma ? reinterpret_cast<const float4*>(gamma)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+            bq[k] = beta ? reinterpret_cast<const float4*>(beta)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    const float* xr = x + (uint64_t)(live ? row : 0) * ldx;
     float4 v[kChunks];
     float s = 0.0f;
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) {
         const uint32_t j = (c * 32 + lane) * 4;
-        v[c] = j < d ? *reinterpret_cast<const float4*>(xr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[c] = (live && j < d) ? *reinterpret_cast<const float4*>(xr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
         s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
+    }
+#pragma unroll
+    for (int k = 0; k < kGB; ++k) {
+        const uint32_t i = threadIdx.x + k * kThreads;
+        if (i < nq) sg[i] = gq[k], sb[i] = bq[k];
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -79,13 +96,14 @@ __global__ void __launch_bounds__(kLnWarps * 32) layernorm_kernel(const float* _
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float inv = 1.0f / sqrtf(ss / (float)d + eps);
+    __syncthreads();  // sg, sb complete
+    if (!live) return;
     TO* yr = y + (uint64_t)row * ldy;
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) {
-        const uint32_t j = (c * 32 + lane) * 4;
+        const uint32_t q = c * 32 + lane, j = q * 4;
         if (j < d) {
-            const float4 g = gamma ? *reinterpret_cast<const float4*>(gamma + j) : make_float4(1.f, 1.f, 1.f, 1.f);
-            const float4 bb = beta ? *reinterpret_cast<const float4*>(beta + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 g = sg[q], bb = sb[q];
             store4<TO>(yr + j, (v[c].x - mean) * inv * g.x + bb.x, (v[c].y - mean) * inv * g.y + bb.y,
                        (v[c].z - mean) * inv * g.z + bb.z, (v[c].w - mean) * inv * g.w + bb.w);
         }

@@ -239,6 +239,27 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_cl_kernel(const float* __
     __shared__ float tile[CT][65];
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const uint32_t b = blockIdx.z, c0 = blockIdx.y * CT, p0 = blockIdx.x * 256, cpg = C / G;
+    const uint32_t p_end = min(P, p0 + 256);
+    const float* xb = x + ((uint64_t)b * C + c0) * P;
+    __half* yb = y + (uint64_t)b * P * C + c0;
+    // x[c][ps + q .. q+3] of this thread's CT/16 rows: the first sub-tile's loads are in flight while the
+    // warps merge the statistics, each next sub-tile's while the current one is stored
+    float v[CT / 16][4];
+    auto load = [&](uint32_t ps) {
+#pragma unroll
+        for (uint32_t i = 0; i < CT / 16; ++i) {
+            const uint32_t r = t / 16 + 16 * i, pp = ps + (t % 16) * 4;
+            const float* src = xb + (uint64_t)r * P + pp;
+            if (vec && pp + 3 < P) {
+                const float4 f = __ldcs(reinterpret_cast<const float4*>(src));
+                v[i][0] = f.x, v[i][1] = f.y, v[i][2] = f.z, v[i][3] = f.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[i][j] = pp + j < P ? __ldcs(src + j) : 0.0f;
+            }
+        }
+    };
+    load(p0);
     const uint32_t g_lo = c0 / cpg, g_hi = (c0 + CT - 1) / cpg;
     for (uint32_t g = g_lo + warp; g <= g_hi; g += kGnThreads / 32) {
         const float2 r = gn_group_norm(stats + ((uint64_t)b * G + g) * chunks, chunks, eps);
@@ -251,27 +272,17 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_cl_kernel(const float* __
         cm[t] = r.x, csc[t] = r.y * gamma[c], csh[t] = beta[c];
     }
     __syncthreads();
-    const float* xb = x + ((uint64_t)b * C + c0) * P;
-    __half* yb = y + (uint64_t)b * P * C + c0;
     constexpr uint32_t kChunks = CT / 8;  // 16-byte rows of 8 channels per position
 #pragma unroll 1
-    for (uint32_t ps = p0; ps < min(P, p0 + 256); ps += 64) {
-        // x[c][ps .. ps+63] -> tile[c][0..63], normalised
+    for (uint32_t ps = p0; ps < p_end; ps += 64) {
+        // normalised x[c][ps .. ps+63] -> tile[c][0..63]
 #pragma unroll
         for (uint32_t i = 0; i < CT / 16; ++i) {
-            const uint32_t r = t / 16 + 16 * i, q = (t % 16) * 4, pp = ps + q;
-            const float* src = xb + (uint64_t)r * P + pp;
-            float v[4];
-            if (vec && pp + 3 < P) {
-                const float4 f = __ldcs(reinterpret_cast<const float4*>(src));
-                v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
-            } else {
+            const uint32_t r = t / 16 + 16 * i, q = (t % 16) * 4;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) v[j] = pp + j < P ? __ldcs(src + j) : 0.0f;
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) tile[r][q + j] = gn_out(v[j], cm[r], csc[r], csh[r], act);
+            for (int j = 0; j < 4; ++j) tile[r][q + j] = gn_out(v[i][j], cm[r], csc[r], csh[r], act);
         }
+        if (ps + 64 < p_end) load(ps + 64);
         __syncthreads();
         // tile[c][p] -> y[ps + p][c0 + 8k .. 8k+7] as 16-byte stores
 #pragma unroll
