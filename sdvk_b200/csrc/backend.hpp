@@ -45,6 +45,9 @@ struct GemmQ8Desc {
     bool nn;
     bool accumulate;
     bool geglu;  // NT, f16 output: GEGLU-interleaved weight rows, output [rows][wrows / 2]
+    // The weights (payload and scales) are parameters that the kernel launched just before this GEMM
+    // does not write, so the CTA-pair kernel's weight roles may start before that kernel completes.
+    bool weights_static;
 };
 
 int gemm_q8(const GemmQ8Desc& d, const LaunchEnv& env);

@@ -234,6 +234,7 @@ BlockLayout block_layout(const sdvk_block_desc& d) {
 GemmQ8Desc linear_desc(const void* x, int x_dtype, uint64_t ldx, const sdvk_q8_linear& w, uint32_t N, uint32_t K,
                        void* c, int c_dtype, uint64_t ldc, uint32_t rows, bool accumulate) {
     GemmQ8Desc g{};
+    g.weights_static = true;  // the block's weights are parameters
     g.x = x;
     g.x_dtype = x_dtype;
     g.ldx = ldx;

@@ -188,6 +188,7 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     p.ldw = d.ldw;
     p.sW = d.sw;
     p.geglu = d.geglu ? 1u : 0u;
+    p.weights_static = d.weights_static ? 1u : 0u;
     p.tiles_x = (d.xrows + Cfg::kBNX - 1) / Cfg::kBNX;
     p.tiles_w = (d.wrows + 2 * Cfg::kBW - 1) / (2 * Cfg::kBW);
     p.num_tiles = p.tiles_x * p.tiles_w * d.batch;

@@ -42,6 +42,8 @@ struct GemmQ8Params {
     uint64_t timeout_ns;
     void* c;                // output (direct-store epilogue): NT C[z][x][w], NN C[z][w][x]
     uint64_t ldc, sc;       // output row and batch strides (elements)
+    uint32_t weights_static;  // the weights and scales are parameters no kernel writes while this GEMM
+                              // may run early: the weight roles read them before griddepcontrol.wait
     uint32_t geglu;         // NT only: the weight rows are GEGLU-interleaved (see gemm_q8_geglu), and
                             // each 32-column chunk [a(16) | gate(16)] is stored as 16 a * gelu(gate)
 };

@@ -163,9 +163,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // Everything above overlaps the previous kernel's tail; global memory is touched only after it.
-    grid_dependency_wait();
-    grid_launch_dependents();
+    // Everything above overlaps the previous kernel's tail.  With static weights the raw-weight
+    // producer, the dequantisers and the MMA issuer go on at once (they read only the weights and
+    // scales); the activation producer and the epilogue, which read and write the previous kernel's
+    // data, wait for it to complete, and they alone signal the next kernel's launch.
+    const bool early = p.weights_static && (warp == 1 || warp == 2 || (warp >= 4 && warp < 12));
+    if (!early) {
+        grid_dependency_wait();
+        grid_launch_dependents();
+    }
 
     bool ok = true;
     auto fail = [&]() {

@@ -614,6 +614,7 @@ struct Pass {
             return;
         }
         GemmQ8Desc g{};
+        g.weights_static = true;  // UNet parameters
         g.x = a;
         g.x_dtype = a_dtype;
         g.ldx = K;
@@ -639,6 +640,7 @@ struct Pass {
         ++launches;
         if (dry || !ok()) return;
         GemmQ8Desc g{};
+        g.weights_static = true;  // UNet parameters
         g.x = x;
         g.x_dtype = x_dtype;
         g.ldx = P;
@@ -702,6 +704,7 @@ struct Pass {
         ++launches;
         if (!dry && ok()) {
             GemmQ8Desc g{};
+        g.weights_static = true;  // UNet parameters
             g.x = ctx;
             g.x_dtype = ctx_dtype;
             g.ldx = u.d.ctx_dim;
