@@ -290,6 +290,26 @@ struct sdvk_unet {
     std::vector<Res> res;
     std::vector<St> st;
     bool prepared = false;
+    // sdvk_unet_forward replays the pass from a CUDA graph while its arguments and the context's
+    // settings stay the same (a sampler loop's fixed device buffers); any change captures a new one,
+    // on a stream of the UNet's own, and the graph is launched on the caller's stream
+    struct GraphKey {
+        const void *x, *t, *adm, *ctx, *out;
+        int ctx_dtype, precision;
+        cudaStream_t side;
+        cudaEvent_t fork, join;
+        uint32_t* err;
+        uint64_t timeout_ns;
+        bool operator==(const GraphKey& o) const {
+            return x == o.x && t == o.t && adm == o.adm && ctx == o.ctx && out == o.out && ctx_dtype == o.ctx_dtype &&
+                   precision == o.precision && side == o.side && fork == o.fork && join == o.join && err == o.err &&
+                   timeout_ns == o.timeout_ns;
+        }
+    };
+    GraphKey gkey{}, last_key{};  // the graph's arguments; the previous call's
+    bool have_last = false;
+    cudaGraphExec_t gexec = nullptr;
+    cudaStream_t cap_stream = nullptr;
     uint64_t arena_bytes = 0;  // parameters (null arena: a plan without device memory)
     uint64_t plan[9] = {};  // workspace offsets of the pass's scratch regions (fixed at creation)
 
@@ -968,6 +988,8 @@ int unet_destroy(sdvk_unet* u) {
     int cur = -1;
     cudaGetDevice(&cur);
     if (cur != u->device) cudaSetDevice(u->device);
+    if (u->gexec) cudaGraphExecDestroy(u->gexec);
+    if (u->cap_stream) cudaStreamDestroy(u->cap_stream);
     cudaFree(u->arena);
     cudaFree(u->ws);
     if (cur >= 0 && cur != u->device) cudaSetDevice(cur);
@@ -1043,10 +1065,63 @@ int unet_forward(sdvk_unet* u, const float* x, const float* timesteps, const flo
         return fail(env, SDVK_E_ARG, "context dtype must be F16, BF16 or F32");
     if (!u->arena) return fail(env, SDVK_E_STATE, "a UNet plan has no device memory (sdvk_unet_create makes one that has)");
     if (!u->prepared) return fail(env, SDVK_E_STATE, "sdvk_unet_prepare (or sdvk_unet_init_random) has not run");
-    Pass p{*u, env, false};
-    p.use_plan();
-    p.forward(x, timesteps, adm, ctx, ctx_dtype, out);
-    return p.rc;
+    auto eager = [&]() {
+        Pass p{*u, env, false};
+        p.use_plan();
+        p.forward(x, timesteps, adm, ctx, ctx_dtype, out);
+        return p.rc;
+    };
+    // A stream that is being captured (the caller's own graph) gets the launches themselves;
+    // SDVK_UNET_GRAPH=0 turns the graph off.
+    const char* e = getenv("SDVK_UNET_GRAPH");
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusActive;
+    if ((e && e[0] == '0') || cudaStreamIsCapturing(env.stream, &cs) != cudaSuccess ||
+        cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return eager();
+    }
+    const U::GraphKey key{x, timesteps, adm, ctx, out, ctx_dtype, env.precision, env.side, env.fork, env.join,
+                          env.err_dev, env.timeout_ns};
+    if (!u->gexec || !(key == u->gkey)) {
+        // The first call with new arguments runs the launches themselves (and sets every kernel's
+        // attributes outside any capture); a second call with the same arguments captures the graph.
+        if (!u->have_last || !(key == u->last_key)) {
+            u->last_key = key;
+            u->have_last = true;
+            return eager();
+        }
+        if (u->gexec) {
+            cudaGraphExecDestroy(u->gexec);
+            u->gexec = nullptr;
+        }
+        if (!u->cap_stream)
+            if (int rc = cuda_check(env, cudaStreamCreateWithFlags(&u->cap_stream, cudaStreamNonBlocking),
+                                    "UNet capture stream"))
+                return rc;
+        LaunchEnv cenv = env;
+        cenv.stream = u->cap_stream;
+        if (int rc = cuda_check(env, cudaStreamBeginCapture(cenv.stream, cudaStreamCaptureModeThreadLocal),
+                                "UNet graph capture"))
+            return rc;
+        Pass p{*u, cenv, false};
+        p.use_plan();
+        p.forward(x, timesteps, adm, ctx, ctx_dtype, out);
+        const int rc = p.rc;
+        cudaGraph_t g = nullptr;
+        const cudaError_t ec = cudaStreamEndCapture(cenv.stream, &g);
+        if (rc || ec != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            return rc ? rc : cuda_check(env, ec, "UNet graph capture");
+        }
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t ei = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (int r = cuda_check(env, ei, "UNet graph instantiate")) return r;
+        u->gexec = ex;
+        u->gkey = key;
+    }
+    return cuda_check(env, cudaGraphLaunch(u->gexec, env.stream), "UNet graph launch");
 }
 
 uint64_t unet_flops(const sdvk_unet* u) { return u ? u->flops : 0; }

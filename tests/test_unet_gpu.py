@@ -212,6 +212,38 @@ def test_unet_graph_replay_matches_eager():
     u.close()
 
 
+def test_unet_forward_replays_its_own_graph(monkeypatch):
+    """sdvk_unet_forward runs the launches themselves on a first call, captures a CUDA graph on a second
+    call with the same buffers and replays it after that; the graph reads the buffers' new contents at
+    every replay, new buffers start over, and every result equals the launches made one by one
+    (SDVK_UNET_GRAPH=0) bit for bit."""
+    from sdvk_b200.unet import Unet
+
+    u = Unet(2, 16, 16, device=0, **SMALL)
+    u.init_random(13)
+    dev = torch.device("cuda", 0)
+    x, t, adm, ctx = _inputs(u.arch, 2, 16, 16, 3, dev)
+    x2 = x * 0.5 + 0.1
+    monkeypatch.setenv("SDVK_UNET_GRAPH", "0")
+    eager1 = u.forward(x, t, adm, ctx).clone()
+    eager2 = u.forward(x2, t, adm, ctx).clone()
+    monkeypatch.delenv("SDVK_UNET_GRAPH")
+    out = torch.empty_like(x)
+    runs = [u.forward(x, t, adm, ctx, out=out).clone() for _ in range(3)]  # launches, capture, replay
+    x_keep = x.clone()
+    x.copy_(x2)  # the same buffer, new contents
+    replayed = u.forward(x, t, adm, ctx, out=out).clone()
+    other = torch.empty_like(x)
+    fresh = u.forward(x_keep, t, adm, ctx, out=other).clone()  # new buffers
+    torch.cuda.synchronize()
+    u.ctx.synchronize()
+    for r in runs:
+        assert torch.equal(r, eager1)
+    assert torch.equal(replayed, eager2)
+    assert torch.equal(fresh, eager1)
+    u.close()
+
+
 def test_unet_rejects_bad_shapes():
     import sdvk_b200
     from sdvk_b200.unet import Unet
