@@ -54,6 +54,26 @@ def test_status_strings_and_support_predicate():
     assert not sdvk_b200.fused_attn_supported(0, 1)
 
 
+def test_implicit_conv_shape_predicate(monkeypatch):
+    """sdvk_conv3x3_implicit_ok: cin % 64, OH*OW % 128, stride 1 or 2, at least 128 KB of input, and
+    the SDVK_CONV_IMPLICIT switch; every UNet conv but conv_in qualifies at the 1024^2 latent."""
+    from sdvk_b200 import Context
+
+    ok = Context.conv3x3_implicit_ok
+    for cin, HW in ((320, 128), (640, 64), (960, 128), (1280, 32), (2560, 32), (1920, 64)):
+        assert ok(2, cin, HW, HW, 1), (cin, HW)
+    assert ok(2, 320, 128, 128, 2) and ok(2, 640, 64, 64, 2)  # the downsamplers (64^2 and 32^2 out)
+    assert not ok(2, 32, 128, 128, 1)  # conv_in's padded 32 channels
+    assert not ok(2, 96, 32, 32, 1)  # cin % 64
+    assert not ok(1, 64, 12, 10, 1)  # 120 output positions
+    assert not ok(1, 64, 16, 16, 1)  # a 32 KB input
+    assert ok(2, 128, 16, 16, 1)  # exactly 128 KB
+    assert not ok(2, 320, 128, 128, 3)  # stride 3
+    assert not ok(0, 320, 128, 128, 1)
+    monkeypatch.setenv("SDVK_CONV_IMPLICIT", "0")
+    assert not ok(2, 320, 128, 128, 1)
+
+
 def test_argument_errors_need_no_device():
     import sdvk_b200
 
