@@ -232,8 +232,6 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_cl_kernel(const float* __
                                                                  uint32_t C, uint32_t P, uint32_t G, float eps,
                                                                  uint32_t act, const GnStat* __restrict__ stats,
                                                                  uint32_t chunks, bool vec) {
-    grid_dependency_wait();
-    grid_launch_dependents();
     __shared__ float2 gnorm[CT];
     __shared__ float cm[CT], csc[CT], csh[CT];
     __shared__ float tile[CT][65];
@@ -259,7 +257,11 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_cl_kernel(const float* __
             }
         }
     };
+    // x is complete before this kernel's statistics kernel started (both come from one groupnorm
+    // call, statistics first), so the first loads go out before waiting for the statistics
     load(p0);
+    grid_dependency_wait();
+    grid_launch_dependents();
     const uint32_t g_lo = c0 / cpg, g_hi = (c0 + CT - 1) / cpg;
     for (uint32_t g = g_lo + warp; g <= g_hi; g += kGnThreads / 32) {
         const float2 r = gn_group_norm(stats + ((uint64_t)b * G + g) * chunks, chunks, eps);
