@@ -401,7 +401,9 @@ SDVK_API int sdvk_groupnorm_cl(sdvk_ctx* ctx, const float* x, const float* gamma
  * (runPass twice, sdvkgen.cpp:3812-3813); with a GPU pair each rank runs one pass and the halves
  * meet by all-gather.  The unique id (SDVK_COMM_ID_BYTES) is made on one rank and passed to the
  * others out of band.  Creation and every wait poll the communicator against timeout_ms: a peer
- * that never joins or stops answering aborts the communicator and returns SDVK_E_TIMEOUT.
+ * that never joins or stops answering aborts the communicator and returns SDVK_E_TIMEOUT.  The
+ * first collective connects the peers and waits for all of them to reach it, under the same
+ * creation deadline; later enqueues use the context's timeout (sdvk_ctx_set_timeout_ms).
  * NCCL itself is loaded on first use (libnccl.so.2); without it these calls return SDVK_E_CUDA. */
 #define SDVK_COMM_ID_BYTES 128
 typedef struct sdvk_comm sdvk_comm;

@@ -13,6 +13,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <string>
@@ -24,6 +25,10 @@ struct sdvk_comm {
     ncclComm_t comm = nullptr;
     int nranks = 0, rank = 0;
     bool aborted = false;
+    // NCCL connects the peers lazily, inside the first collective's enqueue, which therefore waits
+    // for every rank to arrive: it gets the creation deadline, later enqueues the context's
+    uint32_t setup_ms = 0;
+    bool connected = false;
 };
 
 namespace sdvk {
@@ -184,6 +189,7 @@ int comm_create(int nranks, int rank, const void* id, uint32_t timeout_ms, sdvk_
     }
     c->nranks = nranks;
     c->rank = rank;
+    c->setup_ms = timeout_ms;
     if (int rc = comm_settle(c, timeout_ms, env, "communicator setup")) {
         delete c;
         return rc;
@@ -223,7 +229,10 @@ int allgather(sdvk_comm* c, const void* send, void* recv, uint64_t count, int dt
     ncclResult_t r = nccl().AllGather(send, recv, count, nccl_type(dtype), c->comm, env.stream);
     if (r != ncclSuccess && r != ncclInProgress)
         return fail(env, SDVK_E_CUDA, std::string("ncclAllGather: ") + nccl().GetErrorString(r));
-    return comm_settle(c, timeout_ms, env, "all-gather enqueue");
+    const uint32_t deadline = c->connected ? timeout_ms : std::max(timeout_ms, c->setup_ms);
+    if (int rc = comm_settle(c, deadline, env, "all-gather enqueue")) return rc;
+    c->connected = true;
+    return SDVK_OK;
 }
 
 int comm_wait(sdvk_comm* c, uint32_t timeout_ms, const LaunchEnv& env) {

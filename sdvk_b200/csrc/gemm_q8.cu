@@ -242,8 +242,27 @@ int pick_pair_bn(const GemmQ8Desc& d, int num_sms, bool nn) {
 }
 
 // Kernel choice: the CTA-pair kernel when the problem fills at least about half of the SM pairs
-// with 256 x 256 tiles; otherwise single-CTA tiles (128 x 128 or 128 x 256) give more parallelism.
+// with 256 x 256 tiles, or when a launch-time model says it is at least 10% faster: below about
+// half the pairs the single-CTA tiles (128 x 128 or 128 x 256) give more parallelism, but a
+// single-CTA stage dequantises twice the weight rows per SM, and over a long K (the batch-1
+// feed-forward output, K = 5120: 58.6 us single-CTA against 39.0 us as 20 pair tiles, measured
+// back to back on the B200) the per-stage cost decides.
 // SDVK_GEMM_VARIANT=1sm|2sm forces one of them; SDVK_GEMM_PAIR_BN forces the pair tile width.
+// Modelled launch time in units of 0.64 ns (a 256 x 256 pair k-stage = 512, about 0.33 us when
+// the clusters are not all busy; a 128 x 256 single-CTA stage about 0.62 us = 960), plus each
+// kernel's fill and drain (about 12.9 us pair, 8.7 us single-CTA), from back-to-back launches of
+// the 1024 x 1280 x {1280, 5120} projections.
+uint64_t modelled_pair(const GemmQ8Desc& d, int num_sms, int bn, int es) {
+    const uint64_t clusters = (uint64_t)num_sms / 2, ks = (d.K + 128 / es - 1) / (128 / es);
+    const uint64_t tiles = ((d.wrows + 255) / 256) * ((d.xrows + bn - 1) / bn) * d.batch;
+    return 20000 + (tiles + clusters - 1) / clusters * ks * (uint64_t)(bn + 256);
+}
+uint64_t modelled_single(const GemmQ8Desc& d, int num_sms, int es) {
+    const uint64_t bn = d.wrows <= 128 ? 128 : 256, ks = (d.K + 128 / es - 1) / (128 / es);
+    const uint64_t tiles = ((d.xrows + 127) / 128) * ((d.wrows + bn - 1) / bn) * d.batch;
+    return 13500 + (tiles + num_sms - 1) / num_sms * ks * (bn == 256 ? 960 : 600);
+}
+
 int variant_override() {
     const char* e = getenv("SDVK_GEMM_VARIANT");
     return (e && e[0] == '1') ? 1 : (e && e[0] == '2') ? 2 : 0;
@@ -254,10 +273,14 @@ int launch_bn(const GemmQ8Desc& d, const LaunchEnv& env) {
     const uint64_t pair_tiles = (uint64_t)((d.xrows + 255) / 256) * ((d.wrows + 255) / 256) * d.batch;
     const int forced = variant_override();
     // the GEGLU epilogue exists in the CTA-pair kernel only
-    const bool pair = d.geglu || forced == 2 || (forced == 0 && d.wrows > 128 && pair_tiles * 4 >= (uint64_t)env.num_sms);
+    const int pick = pick_pair_bn(d, env.num_sms, NN);
+    const bool fills = pair_tiles * 4 >= (uint64_t)env.num_sms;
+    const bool faster = !fills && d.wrows > 128 &&
+                        modelled_pair(d, env.num_sms, pick, sizeof(TA)) * 10 < modelled_single(d, env.num_sms, sizeof(TA)) * 9;
+    const bool pair = d.geglu || forced == 2 || (forced == 0 && d.wrows > 128 && (fills || faster));
     if (pair) {
         const char* e = getenv("SDVK_GEMM_PAIR_BN");
-        int bn = e ? atoi(e) : pick_pair_bn(d, env.num_sms, NN);
+        int bn = e ? atoi(e) : pick;
         if constexpr (NN) {
             return bn == 128 ? launch_pair<TA, 128, NN, TC>(d, env) : launch_pair<TA, 256, NN, TC>(d, env);
         } else {
