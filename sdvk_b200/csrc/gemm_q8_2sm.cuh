@@ -77,7 +77,7 @@ struct Gemm2Config {
     static constexpr int kOffW = kOffX + kSX * kXBytes;
     static constexpr int kOffEpi = kOffW + ((kSW * kWBytes + 1023) / 1024) * 1024;
     static constexpr int kOffBar = kOffEpi + kEpiBytes;
-    static constexpr int kNumBars = 2 * kSA + 2 * kSX + 2 * kSW + 2 * kAcc + 1;
+    static constexpr int kNumBars = 2 * kSA + 2 * kSX + 2 * kSW + 2 * kAcc + 2;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
     static constexpr int kThreads = 512;
     // dequantiser groups (stages round-robin); bf16's dequantisation goes through fp32 and needs
@@ -121,7 +121,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     uint64_t* acc_full = w_empty + Cfg::kSW;
     uint64_t* acc_empty = acc_full + Cfg::kAcc;
     uint64_t* mma_done = acc_empty + Cfg::kAcc;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* last_ready = mma_done + 1;  // the epilogue warps have seen the last tile's accumulator
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(last_ready + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -147,6 +148,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             mbar_init(&acc_empty[i], 8);
         }
         mbar_init(mma_done, 1);
+        mbar_init(last_ready, 4);
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -188,6 +190,73 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     };
     const uint32_t my_tiles = (p.num_tiles > cid) ? (p.num_tiles - cid + ncl - 1) / ncl : 0;
     const uint32_t my_iters = my_tiles * p.k_stages;
+
+    // One 32-column chunk cc of accumulator acc, TMEM lanes 32q..32q+31 (weight rows
+    // w0 .. w0 + 31, this thread's row w0 + lane with bias b): TMEM -> registers -> (GEGLU) ->
+    // the staging buffer `buf` -> TMA store (or reduce-add).  `release`: hand the accumulator back
+    // to the MMA as soon as this chunk's TMEM read has completed.
+    auto emit_chunk = [&](uint32_t acc, int q, int cc, uint32_t z, uint32_t xt, int w0, float b, uint8_t* buf,
+                          bool release) {
+        const int x0 = (int)(xt * Cfg::kBNX) + cc * 32;
+        uint32_t raw[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * Cfg::kBNX + cc * 32, raw);
+        tmem_wait_ld();
+        if (release) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+        }
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + b;
+        if (lane == 0) bulk_wait_read<Cfg::kEpiBufs - 1>();  // the store that last used `buf` has read it
+        __syncwarp();
+        if constexpr (!NN && sizeof(TC) == 2) {
+            if (p.geglu) {
+                // Lane l < 16 holds a of output column l, lane l + 16 the matching gate: 16
+                // outputs a * gelu(gate) per activation row, a [32 x][16] f16 tile.  Each
+                // lane computes half of the 32 rows (lanes < 16 rows 0-15, lanes >= 16 rows
+                // 16-31), trading the half its partner needs in one shuffle per row pair.
+                __half* t = reinterpret_cast<__half*>(buf);
+                const bool lo = lane < 16;
+                const int o = lane & 15;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float mine = lo ? v[j] : v[16 + j];  // a (lo) or gate (hi) of my row
+                    const float other = __shfl_xor_sync(0xffffffffu, lo ? v[16 + j] : v[j], 16);
+                    const float a = lo ? mine : other, g = lo ? other : mine;
+                    t[(lo ? j : 16 + j) * 16 + o] = __float2half_rn(a * gelu_erf_as_fast(g));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_3d(&tmC, buf, w0 / 2, x0, (int)z);
+                    bulk_commit();
+                }
+                return;
+            }
+        }
+        if constexpr (!NN) store_epi_col<TC>(buf, lane, v);  // [32 x][32 w]
+        else store_epi_row<TC>(buf, lane, v);                // [32 w][32 x]
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            if constexpr (!NN) {
+                if (p.accumulate) tma_reduce_add_3d(&tmC, buf, w0, x0, (int)z);
+                else tma_store_3d(&tmC, buf, w0, x0, (int)z);
+            } else {
+                if (p.accumulate) tma_reduce_add_3d(&tmC, buf, x0, w0, (int)z);
+                else tma_store_3d(&tmC, buf, x0, w0, (int)z);
+            }
+            bulk_commit();
+        }
+    };
+    // The last tile's epilogue has nothing left to overlap, so the dequantisers, idle by then, share
+    // it: quadrant q's chunks go round-robin to epilogue warp 12 + q (share 0) and dequantiser warps
+    // 4 + q, 8 + q (shares 1, 2), which stage through the dequantised-weight ring (free once the
+    // last accumulator is complete).
+    constexpr int kShares = 3;
+    static_assert(Cfg::kSA * Cfg::kABytes >= 8 * Cfg::kEpiBufs * 4096, "helper staging in the weight ring");
 
     if (warp == 0) {
         // ------------------------------------------------------------ activation TMA producer (both CTAs)
@@ -367,6 +436,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 }
             }
         }
+        if (ok && my_tiles > 0) {  // a share of the last tile's epilogue
+            const int q = warp & 3, share = 1 + (warp - 4) / 4;
+            const uint32_t i = my_tiles - 1, acc = i % Cfg::kAcc;
+            uint32_t z, xt, wt;
+            decode(cid + i * ncl, z, xt, wt);
+            if (!__all_sync(0xffffffffu, mbar_wait(last_ready, 0, p.timeout_ns))) {
+                fail();
+            } else {
+                tc_fence_after();
+                grid_dependency_wait();  // stores into C: the previous kernel has completed (a no-op if already waited)
+                uint8_t* hbuf = sA + (warp - 4) * (Cfg::kEpiBufs * 4096);
+                const int w0 = (int)(wt * 2 * Cfg::kBW + rank * Cfg::kBW) + q * 32;
+                const uint32_t n = (uint32_t)w0 + lane;
+                const float b = (p.bias && n < p.wrows) ? __ldg(p.bias + z * p.sbias + n) : 0.0f;
+                uint32_t nstore = 0;
+#pragma unroll 1
+                for (int cc = share; cc < Cfg::kBNX / 32; cc += kShares, ++nstore)
+                    emit_chunk(acc, q, cc, z, xt, w0, b, hbuf + (nstore % Cfg::kEpiBufs) * 4096, false);
+                tc_fence_before();
+                if (lane == 0) bulk_wait_all();
+            }
+        }
     } else if (warp >= 12) {
         // ------------------------------------------------------------ epilogue (both CTAs)
         // Warp q reads TMEM lanes 32q..32q+31: weight rows w = wt*256 + rank*128 + 32q + lane; each
@@ -383,67 +474,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                 break;
             }
             tc_fence_after();
+            const bool last = i + 1 == my_tiles;
+            if (last && lane == 0) mbar_arrive(last_ready);  // the helpers may read this accumulator
             const int w0 = (int)(wt * 2 * Cfg::kBW + rank * Cfg::kBW) + q * 32;  // this warp's first weight row
             const uint32_t n = (uint32_t)w0 + lane;                           // this thread's weight row
             const float b = (p.bias && n < p.wrows) ? __ldg(p.bias + z * p.sbias + n) : 0.0f;
 #pragma unroll 1
-            for (int cc = 0; cc < Cfg::kBNX / 32; ++cc, ++nstore) {
-                const int x0 = (int)(xt * Cfg::kBNX) + cc * 32;
-                uint32_t raw[32];
-                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * Cfg::kBNX + cc * 32, raw);
-                tmem_wait_ld();
-                if (cc + 1 == Cfg::kBNX / 32) {  // accumulator fully read: hand it back to the MMA
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
-                }
-                float v[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) + b;
-                uint8_t* buf = ebuf + (nstore % Cfg::kEpiBufs) * 4096;
-                if (lane == 0) bulk_wait_read<Cfg::kEpiBufs - 1>();  // the store that last used `buf` has read it
-                __syncwarp();
-                if constexpr (!NN && sizeof(TC) == 2) {
-                    if (p.geglu) {
-                        // Lane l < 16 holds a of output column l, lane l + 16 the matching gate: 16
-                        // outputs a * gelu(gate) per activation row, a [32 x][16] f16 tile.  Each
-                        // lane computes half of the 32 rows (lanes < 16 rows 0-15, lanes >= 16 rows
-                        // 16-31), trading the half its partner needs in one shuffle per row pair.
-                        __half* t = reinterpret_cast<__half*>(buf);
-                        const bool lo = lane < 16;
-                        const int o = lane & 15;
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const float mine = lo ? v[j] : v[16 + j];  // a (lo) or gate (hi) of my row
-                            const float other = __shfl_xor_sync(0xffffffffu, lo ? v[16 + j] : v[j], 16);
-                            const float a = lo ? mine : other, g = lo ? other : mine;
-                            t[(lo ? j : 16 + j) * 16 + o] = __float2half_rn(a * gelu_erf_as_fast(g));
-                        }
-                        fence_proxy_async_smem();
-                        __syncwarp();
-                        if (lane == 0) {
-                            tma_store_3d(&tmC, buf, w0 / 2, x0, (int)z);
-                            bulk_commit();
-                        }
-                        continue;
-                    }
-                }
-                if constexpr (!NN) store_epi_col<TC>(buf, lane, v);  // [32 x][32 w]
-                else store_epi_row<TC>(buf, lane, v);                // [32 w][32 x]
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    if constexpr (!NN) {
-                        if (p.accumulate) tma_reduce_add_3d(&tmC, buf, w0, x0, (int)z);
-                        else tma_store_3d(&tmC, buf, w0, x0, (int)z);
-                    } else {
-                        if (p.accumulate) tma_reduce_add_3d(&tmC, buf, x0, w0, (int)z);
-                        else tma_store_3d(&tmC, buf, x0, w0, (int)z);
-                    }
-                    bulk_commit();
-                }
-            }
+            for (int cc = 0; cc < Cfg::kBNX / 32; cc += last ? kShares : 1, ++nstore)
+                emit_chunk(acc, q, cc, z, xt, w0, b, ebuf + (nstore % Cfg::kEpiBufs) * 4096,
+                           !last && cc + 1 == Cfg::kBNX / 32);
         }
+        tc_fence_before();  // the TMEM reads before the teardown's deallocation
         if (lane == 0) bulk_wait_all();
     }
 
