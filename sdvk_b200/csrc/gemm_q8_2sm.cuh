@@ -14,18 +14,23 @@
 // The accumulator D[w][x] (TMEM lane = weight row, column = activation row) is stored transposed
 // for NT (C[x][w]) and directly for NN (C[w][x]).
 //
-// Three rings, sized independently: the dequantised-weight ring (one slot per dequantiser group), the
-// raw int8 weight ring, and the activation ring, which takes the shared memory that is left (6 slots at
-// tile widths 224-256, 8 below).  The tensor pipe idles whenever the issuing thread polls a barrier that
-// is not yet complete, so its per-stage control path is two CTA-scope polls and two commits:
+// Two rings, sized independently: the dequantised-weight ring (one slot per dequantiser group) and the
+// activation ring (6 slots: 8 measured slower in the UNet pass, and the shared memory freed by the raw
+// ring is left unused).  The raw int8 weights do not
+// pass through shared memory: the kernel is bound by shared-memory bandwidth (a k-stage moves about
+// 745 128-byte wavefronts per SM at tile width 224: tensor-core operand reads, TMA writes, the
+// dequantised tile's stores, the epilogue), and a TMA write plus a load of the raw tile were 128 of
+// them.  Each dequantiser thread loads its 16-byte chunks of raw weights and their scales from
+// global memory SDVK_GEMM2_RAW_AHEAD of its group's stages ahead, into registers.
+// The tensor pipe idles whenever the issuing thread polls a barrier that is not yet complete, so its
+// per-stage control path is two CTA-scope polls and two commits:
 //   x_full[sx]  (even CTA)  activation TMA bytes of both CTAs (cta_group::2 TMA); the even CTA's
 //                           producer sets the tx count
 //   a_full[sa]  (even CTA)  one dequantiser group's warps of both CTAs
 //   x_empty[sx], a_empty[sa] (each CTA)  an MMA commit multicast to both CTAs frees the slot
 //   acc_full  (each CTA)  MMA commit multicast;  acc_empty (even CTA): the 8 epilogue warps
-//   w_full, w_empty (each CTA)  the local raw int8 weight ring (TMA -> dequantisers)
-// Warp roles per CTA: 0 activation TMA, 1 TMEM + MMA (even CTA issues), 2 weight TMA,
-// 4-11 dequantisers in groups that take stages round-robin, 12-15 epilogue (3 idle).  One warp's pass
+// Warp roles per CTA: 0 activation TMA, 1 TMEM + MMA (even CTA issues), 4-11 dequantisers in groups
+// that take stages round-robin, 12-15 epilogue (2 and 3 idle).  One warp's pass
 // over a stage is a chain of waits, shared-memory round trips, a proxy fence and a remote arrive
 // that lasts several times the stage's MMA time, so several groups keep several stages in flight.
 //
@@ -50,34 +55,32 @@ struct Gemm2Config {
 #ifndef SDVK_GEMM2_A_STAGES
 #define SDVK_GEMM2_A_STAGES 4
 #endif
-#ifndef SDVK_GEMM2_RAW_STAGES
-#define SDVK_GEMM2_RAW_STAGES 4
+#ifndef SDVK_GEMM2_RAW_AHEAD
+#define SDVK_GEMM2_RAW_AHEAD 2
 #endif
 #ifndef SDVK_GEMM2_X_STAGES
-#define SDVK_GEMM2_X_STAGES 8
+#define SDVK_GEMM2_X_STAGES 6
 #endif
 #ifndef SDVK_GEMM2_EPI_BUFS
 #define SDVK_GEMM2_EPI_BUFS 2
 #endif
     static constexpr int kSA = SDVK_GEMM2_A_STAGES;    // dequantised weight tiles
-    static constexpr int kSW = SDVK_GEMM2_RAW_STAGES;  // raw int8 weight tiles
+    static constexpr int kRawAhead = SDVK_GEMM2_RAW_AHEAD;  // own stages of raw weights in registers
     static constexpr int kAcc = 2;
     static constexpr int kABytes = kBW * 128;
     static constexpr int kXBytes = ((kBXC * 128 + 1023) / 1024) * 1024;
-    static constexpr int kWBytes = kBW * kBK;
     static constexpr int kEpiBufs = SDVK_GEMM2_EPI_BUFS;  // 32x32 fp32 staging buffers per epilogue warp
     static constexpr int kEpiBytes = 4 * kEpiBufs * 4096;
     static constexpr int kMaxSmem = 232448;
-    static constexpr int kFixed = kSA * kABytes + ((kSW * kWBytes + 1023) / 1024) * 1024 + kEpiBytes + 1024 + 512;
+    static constexpr int kFixed = kSA * kABytes + kEpiBytes + 1024 + 512;
     static constexpr int kSXFit = (kMaxSmem - kFixed) / kXBytes;
     static constexpr int kSX = kSXFit > SDVK_GEMM2_X_STAGES ? SDVK_GEMM2_X_STAGES : kSXFit;  // activation tiles
     static constexpr uint32_t kTmemCols = (kAcc * BNX <= 256) ? 256 : 512;
     static constexpr int kOffA = 0;
     static constexpr int kOffX = kOffA + kSA * kABytes;
-    static constexpr int kOffW = kOffX + kSX * kXBytes;
-    static constexpr int kOffEpi = kOffW + ((kSW * kWBytes + 1023) / 1024) * 1024;
+    static constexpr int kOffEpi = kOffX + kSX * kXBytes;
     static constexpr int kOffBar = kOffEpi + kEpiBytes;
-    static constexpr int kNumBars = 2 * kSA + 2 * kSX + 2 * kSW + 2 * kAcc + 2;
+    static constexpr int kNumBars = 2 * kSA + 2 * kSX + 2 * kAcc + 2;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
     static constexpr int kThreads = 512;
     // dequantiser groups (stages round-robin); bf16's dequantisation goes through fp32 and needs
@@ -109,16 +112,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem + Cfg::kOffA;  // dequantised weight tiles
     uint8_t* sX = smem + Cfg::kOffX;  // activation tiles
-    uint8_t* sW = smem + Cfg::kOffW;  // raw int8 weight tiles
     uint8_t* sEpi = smem + Cfg::kOffEpi;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
     uint64_t* a_full = bars;
     uint64_t* a_empty = a_full + Cfg::kSA;
     uint64_t* x_full = a_empty + Cfg::kSA;
     uint64_t* x_empty = x_full + Cfg::kSX;
-    uint64_t* w_full = x_empty + Cfg::kSX;
-    uint64_t* w_empty = w_full + Cfg::kSW;
-    uint64_t* acc_full = w_empty + Cfg::kSW;
+    uint64_t* acc_full = x_empty + Cfg::kSX;
     uint64_t* acc_empty = acc_full + Cfg::kAcc;
     uint64_t* mma_done = acc_empty + Cfg::kAcc;
     uint64_t* last_ready = mma_done + 1;  // the epilogue warps have seen the last tile's accumulator
@@ -139,10 +139,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             mbar_init(&x_full[i], 1);  // the even CTA producer's expect_tx (both CTAs' bytes)
             mbar_init(&x_empty[i], 1);
         }
-        for (int i = 0; i < Cfg::kSW; ++i) {
-            mbar_init(&w_full[i], 1);
-            mbar_init(&w_empty[i], Cfg::kDqWarps);
-        }
         for (int i = 0; i < Cfg::kAcc; ++i) {
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 8);
@@ -153,7 +149,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmX);
-        tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmC);
     }
     if (warp == 1) {
@@ -165,11 +160,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // Everything above overlaps the previous kernel's tail.  With static weights the raw-weight
-    // producer, the dequantisers and the MMA issuer go on at once (they read only the weights and
-    // scales); the activation producer and the epilogue, which read and write the previous kernel's
-    // data, wait for it to complete, and they alone signal the next kernel's launch.
-    const bool early = p.weights_static && (warp == 1 || warp == 2 || (warp >= 4 && warp < 12));
+    // Everything above overlaps the previous kernel's tail.  With static weights the dequantisers
+    // and the MMA issuer go on at once (they read only the weights and scales); the activation
+    // producer and the epilogue, which read and write the previous kernel's data, wait for it to
+    // complete, and they alone signal the next kernel's launch.
+    const bool early = p.weights_static && (warp == 1 || (warp >= 4 && warp < 12));
     if (!early) {
         grid_dependency_wait();
         grid_launch_dependents();
@@ -287,28 +282,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             }
             // The activation loads are drained by the MMA (it waits for every one it consumes).
         }
-    } else if (warp == 2) {
-        // ------------------------------------------------------------ raw weight TMA producer (both CTAs)
-        if (lane == 0) {
-            uint32_t it = 0;
-            for (uint32_t i = 0; ok && i < my_tiles; ++i) {
-                uint32_t z, xt, wt;
-                decode(cid + i * ncl, z, xt, wt);
-                const int zw = p.sW ? (int)z : 0;
-                for (uint32_t ks = 0; ks < p.k_stages; ++ks, ++it) {
-                    const uint32_t sw = it % Cfg::kSW, pw = (it / Cfg::kSW) & 1;
-                    if (!mbar_wait(&w_empty[sw], pw ^ 1, p.timeout_ns)) {
-                        fail();
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&w_full[sw], Cfg::kWBytes);
-                    tma_load_3d(sW + sw * Cfg::kWBytes, &tmW, &w_full[sw], (int)(ks * Cfg::kBK),
-                                (int)(wt * 2 * Cfg::kBW + rank * Cfg::kBW), zw);
-                }
-            }
-            for (uint32_t i = (it > Cfg::kSW ? it - Cfg::kSW : 0); i < it; ++i)  // drain
-                if (!mbar_wait(&w_full[i % Cfg::kSW], (i / Cfg::kSW) & 1, p.timeout_ns)) fail();
-        }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (even CTA)
         // The whole warp runs the loop (warp-uniform control flow and operands, no divisions on
@@ -376,11 +349,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         const int chunk = ct % Cfg::kChunksPerRow;
         const int row0 = ct / Cfg::kChunksPerRow;
         constexpr int T = Cfg::kTasksPerThread;
-        // Scales come from L2 (far-die hits take about a thousand cycles under load) kRing own
-        // stages ahead of use, into a ring of registers indexed by compile-time constants: the loop
-        // body is unrolled over the ring, so no instruction (not even a register move) touches a
-        // scale before its load has had kRing stages to land.
-        constexpr int kRing = 4;
+        // The raw int8 chunks and their scales come from global memory (L2 hits of far-die data take
+        // about a thousand cycles under load) kRing of this group's own stages ahead of use -- G *
+        // kRing k-stages, several microseconds at full occupancy -- into a ring of registers
+        // indexed by compile-time constants: the loop body is unrolled over the ring, so no
+        // instruction (not even a register move) touches a value before its load has had kRing
+        // stages to land.  Rows past wrows and chunks past K load as zeros (the TMA's fill).
+        constexpr int kRing = Cfg::kRawAhead;
         WeightCursor<T> cur;
         cur.init(&p, cid, ncl, row0, Cfg::kRowStep, Cfg::kBK, chunk * 16, 2 * Cfg::kBW, rank * Cfg::kBW, Cfg::kBW);
         for (uint32_t g = 0; g < grp; ++g) cur.advance();
@@ -389,40 +364,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             for (int g = 0; g < G; ++g) cur.advance();
         };
         float sc[kRing][T];
-        uint4 unused[T];
+        uint4 rw[kRing][T];
 #pragma unroll
         for (int j = 0; j < kRing; ++j) {
-            cur.load<false>(sc[j], unused);
+            cur.load<true>(sc[j], rw[j]);
             next_own();
         }
-        auto stage = [&](uint32_t it, float(&scale)[T]) -> bool {
+        auto stage = [&](uint32_t it, float(&scale)[T], uint4(&raw)[T]) -> bool {
             const uint32_t sa = it % Cfg::kSA, pa = (it / Cfg::kSA) & 1;
-            const uint32_t sw = it % Cfg::kSW, pw = (it / Cfg::kSW) & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&w_full[sw], pw, p.timeout_ns))) return false;  // leave together
-            const uint8_t* wsrc = sW + sw * Cfg::kWBytes;
             uint8_t* adst = sA + sa * Cfg::kABytes;
-            uint4 raw[T];
-#pragma unroll
-            for (int t = 0; t < T; ++t)
-                raw[t] = *reinterpret_cast<const uint4*>(wsrc + (row0 + t * Cfg::kRowStep) * Cfg::kBK + chunk * 16);
             if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[sa], pa ^ 1, p.timeout_ns))) return false;
 #pragma unroll
             for (int t = 0; t < T; ++t) {
                 const int r = row0 + t * Cfg::kRowStep;
                 dequant16<TA>(raw[t], scale[t], adst + r * 128, r, chunk * Cfg::kES);
             }
-            // Only this SM's tensor core reads these rows (operand A of the pair MMA).  The fence
-            // also orders this thread's generic reads of the raw slot before the weight TMA's next
-            // (async-proxy) write into it: the raw slot is handed back only here.  Handing it back
-            // right after the reads, behind a warp barrier alone, let the next TMA overwrite it
-            // before every read had been performed (stale weight rows in up to a third of launches).
+            // Only this SM's tensor core reads these rows (operand A of the pair MMA): a CTA-scope
+            // proxy fence orders the generic stores before its async-proxy reads.
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive_cluster(mapa_shared(&a_full[sa], 0));
-                mbar_arrive(&w_empty[sw]);
-            }
-            cur.load<false>(scale, unused);  // the scales of this group's stage it + G * kRing
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(&a_full[sa], 0));
+            cur.load<true>(scale, raw);  // this group's stage it + G * kRing
             next_own();
             return true;
         };
@@ -430,7 +392,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
 #pragma unroll
             for (int j = 0; j < kRing; ++j) {
                 if (it + G * j >= my_iters) break;
-                if (!stage(it + G * j, sc[j])) {
+                if (!stage(it + G * j, sc[j], rw[j])) {
                     fail();
                     break;
                 }
