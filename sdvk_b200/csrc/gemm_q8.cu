@@ -152,7 +152,7 @@ template <class TA, int BNX, bool NN, class TC>
 int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     using Cfg = Gemm2Config<TA, BNX>;
     const int es = sizeof(TA), ces = sizeof(TC);
-    CUtensorMap tmX, tmW, tmC;
+    CUtensorMap tmX, tmC;
     int rc;
     if (!NN) {
         rc = make_map(&tmX, tma_type(d.x_dtype), d.x, d.K, d.xrows, d.batch, d.ldx * es, d.sx * es, Cfg::kBK,
@@ -163,9 +163,8 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
                       "activation");
     }
     if (rc) return rc;
-    rc = make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, d.wq, d.K, d.wrows, d.sw ? d.batch : 1, d.ldw, d.sw,
-                  Cfg::kBK, Cfg::kBW, CU_TENSOR_MAP_SWIZZLE_NONE, env, "weight");
-    if (rc) return rc;
+    // no weight map: the dequantisers load the raw weights with 16-byte loads (gemm_q8 checked
+    // the 16-byte base and the 32-element strides they rely on)
     if (!NN && d.geglu) {  // 16 output columns per 32 weight rows: [32 x][16] f16 tiles
         rc = make_map(&tmC, tma_type(d.c_dtype), d.c, d.wrows / 2, d.xrows, d.batch, d.ldc * ces, d.sc * ces, 16, 32,
                       CU_TENSOR_MAP_SWIZZLE_NONE, env, "output");
@@ -216,7 +215,7 @@ int launch_pair(const GemmQ8Desc& d, const LaunchEnv& env) {
     attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_check(env, cudaLaunchKernelEx(&cfg, kern, tmX, tmW, tmC, p), "gemm_q8_tc2_kernel launch");
+    return cuda_check(env, cudaLaunchKernelEx(&cfg, kern, tmX, tmC, p), "gemm_q8_tc2_kernel launch");
 }
 
 // Pair-tile width (tensor-core N = activation rows): the candidate minimising waves x per-tile

@@ -105,8 +105,8 @@ struct Gemm2Config {
 
 template <class TA, int BNX, bool NN, class TC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
-    gemm_q8_tc2_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                       const __grid_constant__ CUtensorMap tmC, const GemmQ8Params p) {
+    gemm_q8_tc2_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmC,
+                       const GemmQ8Params p) {
     using Cfg = Gemm2Config<TA, BNX>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
