@@ -15,13 +15,13 @@
 // for NT (C[x][w]) and directly for NN (C[w][x]).
 //
 // Two rings, sized independently: the dequantised-weight ring (one slot per dequantiser group) and the
-// activation ring (6 slots: 8 measured slower in the UNet pass, and the shared memory freed by the raw
-// ring is left unused).  The raw int8 weights do not
-// pass through shared memory: the kernel is bound by shared-memory bandwidth (a k-stage moves about
-// 745 128-byte wavefronts per SM at tile width 224: tensor-core operand reads, TMA writes, the
-// dequantised tile's stores, the epilogue), and a TMA write plus a load of the raw tile were 128 of
-// them.  Each dequantiser thread loads its 16-byte chunks of raw weights and their scales from
-// global memory SDVK_GEMM2_RAW_AHEAD of its group's stages ahead, into registers.
+// activation ring (6 slots: 8 measured slower in the UNet pass; the shared memory a raw-weight ring
+// used to take is left unused).  The raw int8 weights do not pass through shared memory: the kernel
+// is bound by shared-memory bandwidth (a k-stage moved about 745 128-byte wavefronts per SM at tile
+// width 224: tensor-core operand reads, TMA writes, the dequantised tile's stores, the epilogue), and
+// a TMA write plus a load of the raw tile were 128 of them.  Each dequantiser thread loads its
+// 16-byte chunks of raw weights and their scales from global memory SDVK_GEMM2_RAW_AHEAD of its
+// group's stages ahead, into registers.
 // The tensor pipe idles whenever the issuing thread polls a barrier that is not yet complete, so its
 // per-stage control path is two CTA-scope polls and two commits:
 //   x_full[sx]  (even CTA)  activation TMA bytes of both CTAs (cta_group::2 TMA); the even CTA's
@@ -30,9 +30,9 @@
 //   x_empty[sx], a_empty[sa] (each CTA)  an MMA commit multicast to both CTAs frees the slot
 //   acc_full  (each CTA)  MMA commit multicast;  acc_empty (even CTA): the 8 epilogue warps
 // Warp roles per CTA: 0 activation TMA, 1 TMEM + MMA (even CTA issues), 4-11 dequantisers in groups
-// that take stages round-robin, 12-15 epilogue (2 and 3 idle).  One warp's pass
-// over a stage is a chain of waits, shared-memory round trips, a proxy fence and a remote arrive
-// that lasts several times the stage's MMA time, so several groups keep several stages in flight.
+// that take stages round-robin, 12-15 epilogue (2 and 3 idle).  One warp's pass over a stage is a
+// chain of waits, shared-memory stores, a proxy fence and a remote arrive that lasts several times
+// the stage's MMA time, so several groups keep several stages in flight.
 //
 // Every wait is bounded (GemmQ8Params::timeout_ns): a wait that runs out records kErrTimeout, the
 // CTA drains what it issued, both CTAs meet at the final cluster barrier and free TMEM.
