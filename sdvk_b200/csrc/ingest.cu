@@ -79,6 +79,13 @@ __global__ void __launch_bounds__(kIngestBlocks) q8_0_split_kernel(const uint16_
 
 // ---------------------------------------------------------------------------------- GroupNorm
 constexpr int kGnThreads = 256;
+// Positions per CTA of the channels-last apply: 128 (two 64-position sub-tiles).  Each CTA keeps one
+// sub-tile of loads in flight, so the bytes in flight per SM grow with the CTAs per SM (UNet pass at
+// batch 1: 14.46 ms with 256 positions per CTA, 14.37 ms with 128; batch 2 unchanged).
+#ifndef SDVK_GN_CL_POS
+#define SDVK_GN_CL_POS 128
+#endif
+constexpr uint32_t kGnClPos = SDVK_GN_CL_POS;
 constexpr uint32_t kGnChunk = 16384;  // values per statistics CTA
 
 struct GnStat {
@@ -220,8 +227,8 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_kernel(const float* __res
 }
 
 // The same values written channels-last, y[b][p][c] fp16 (the implicit convolution's input and the
-// spatial transformer's token layout).  grid (ceil(P / 256), C / CT, B), 256 threads: CT channels x 256
-// positions per CTA in sub-tiles of 64 positions through shared memory.  The warps first merge the
+// spatial transformer's token layout).  grid (ceil(P / kGnClPos), C / CT, B), 256 threads: CT channels
+// x kGnClPos positions per CTA in sub-tiles of 64 positions through shared memory.  The warps first merge the
 // statistics of the tile's groups (gn_group_norm, so the values equal gn_apply_kernel's bit for bit);
 // x is read as float4 rows along P (vec: P % 4 == 0 and x 16-byte aligned), y written as 16-byte rows
 // of 8 channels (CT * 2 contiguous bytes per position).  C % CT == 0, y 16-byte aligned.
@@ -236,8 +243,8 @@ __global__ void __launch_bounds__(kGnThreads) gn_apply_cl_kernel(const float* __
     __shared__ float cm[CT], csc[CT], csh[CT];
     __shared__ float tile[CT][65];
     const uint32_t t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const uint32_t b = blockIdx.z, c0 = blockIdx.y * CT, p0 = blockIdx.x * 256, cpg = C / G;
-    const uint32_t p_end = min(P, p0 + 256);
+    const uint32_t b = blockIdx.z, c0 = blockIdx.y * CT, p0 = blockIdx.x * kGnClPos, cpg = C / G;
+    const uint32_t p_end = min(P, p0 + kGnClPos);
     const float* xb = x + ((uint64_t)b * C + c0) * P;
     __half* yb = y + (uint64_t)b * P * C + c0;
     // x[c][ps + q .. q+3] of this thread's CT/16 rows: the first sub-tile's loads are in flight while the
@@ -361,10 +368,10 @@ int groupnorm_ex(const float* x, const float* gamma, const float* beta, void* y,
     if (channels_last) {
         const bool xvec = P % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
         if (C % 64 == 0)
-            return launch_pdl(gn_apply_cl_kernel<64>, dim3((P + 255) / 256, C / 64, batch), dim3(kGnThreads), 0, env,
+            return launch_pdl(gn_apply_cl_kernel<64>, dim3((P + kGnClPos - 1) / kGnClPos, C / 64, batch), dim3(kGnThreads), 0, env,
                               "gn_apply_cl_kernel launch", x, gamma, beta, static_cast<__half*>(y), C, P, G, eps, act,
                               (const GnStat*)st, chunks, xvec);
-        return launch_pdl(gn_apply_cl_kernel<32>, dim3((P + 255) / 256, C / 32, batch), dim3(kGnThreads), 0, env,
+        return launch_pdl(gn_apply_cl_kernel<32>, dim3((P + kGnClPos - 1) / kGnClPos, C / 32, batch), dim3(kGnThreads), 0, env,
                           "gn_apply_cl_kernel launch", x, gamma, beta, static_cast<__half*>(y), C, P, G, eps, act,
                           (const GnStat*)st, chunks, xvec);
     }
